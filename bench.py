@@ -1,0 +1,399 @@
+#!/usr/bin/env python
+"""Benchmark of the block-scaled GEMM path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload fp8_prefill|fp4_decode|fp4_cfg1|moe]
+
+Default workload (one "step"): the dense prefill fp8_gemm, M=N=K=4096, A
+quantised per 1x128 (fp32 scales), W e4m3 with fp32 128x128 block scales,
+bf16 output.  At N>1 GPUs the weight is column-sharded (tensor parallel):
+each rank computes C[:, N/g slice] and an NCCL all-gather (plus the column
+interleave) rebuilds C on every rank; total work is fixed (strong scaling).
+
+Rank 0 prints one JSON line.  ``value`` is device-timed (CUDA events on the
+launching stream, max over ranks) with inputs resident in HBM; input sets
+rotate so that no step finds its operands in L2.  ``e2e`` times the public
+API (act_quant + fp8_gemm) from pinned host activations to a host copy of the
+result.  ``--impl reference`` times the reference algorithm's CPU port
+(oracle/) on the host cores instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+PKG = "deepseek-v4-experimental-platform-on-dgx-spark_b200"
+
+PEAKS_FILE = os.path.join(ROOT, "MEASURED_PEAKS.json")
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    try:
+        with open(PEAKS_FILE) as f:
+            return json.load(f), "measured"
+    except Exception:
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+class Clocks:
+    """Samples nvidia-smi during the timed region (SM clock, throttle reasons)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            return None
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# workloads
+# ---------------------------------------------------------------------------
+
+def make_fp8_prefill(torch, dev, M, N, K, seed, n_sets):
+    """Config-2 operands generated on the device (seeded)."""
+    pkg = __import__("importlib").import_module(PKG)
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    sets = []
+    for _ in range(n_sets):
+        x = torch.randn(M, K, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+        a, a_s = pkg.act_quant(x, 128)
+        w = torch.randn(N, K, generator=g, device=dev, dtype=torch.float32) * 0.02
+        wb = w.view(N // 128, 128, K // 128, 128)
+        s = (wb.abs().amax(dim=(1, 3)).clamp(min=1e-4) / 448.0)
+        b = (wb / s[:, None, :, None]).clamp(-448, 448).to(torch.float8_e4m3fn).view(N, K)
+        sets.append((a, a_s, b, s.contiguous(), x))
+    return sets
+
+
+def bench_fp8_prefill(args, torch, dist, ws, rank, dev):
+    pkg = __import__("importlib").import_module(PKG)
+    M = N = K = 4096
+    if N % (ws * 128):
+        raise SystemExit("N must split into 128-row blocks per rank")
+    n_local = N // ws
+    n_sets = 5  # 5 x (16 MiB A + 16/ws MiB B) rotating: inputs >> L2 across consecutive steps
+    sets = make_fp8_prefill(torch, dev, M, N, K, 1234, n_sets)
+    # this rank's column shard of every weight copy
+    shards = [(a, a_s, b[rank * n_local:(rank + 1) * n_local].contiguous(),
+               s[rank * n_local // 128:(rank + 1) * n_local // 128].contiguous()) for a, a_s, b, s, _ in sets]
+    outs = [torch.empty(M, n_local, device=dev, dtype=torch.bfloat16) for _ in range(2)]
+    gathered = torch.empty(ws, M, n_local, device=dev, dtype=torch.bfloat16)
+    full = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    lib = pkg._lib.load()
+    stream = torch.cuda.current_stream()
+
+    def gemm(i, out):
+        a, a_s, b, s = shards[i % n_sets]
+        pkg._lib.check(lib.bs_fp8_gemm(a.data_ptr(), a_s.data_ptr(), pkg._lib.DT_F32, b.data_ptr(), s.data_ptr(),
+                                       pkg._lib.DT_F32, M, n_local, K, out.data_ptr(), stream.cuda_stream))
+
+    def step(i):
+        out = outs[i & 1]
+        gemm(i, out)
+        if ws > 1:
+            dist.all_gather_into_tensor(gathered, out)
+            full.view(M, ws, n_local).copy_(gathered.permute(1, 0, 2))
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+
+    # kernel-only timing of the GEMM (roofline numerator), separate short loop
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for i in range(args.steps):
+        ev[i][0].record()
+        gemm(i, outs[i & 1])
+        ev[i][1].record()
+    torch.cuda.synchronize()
+    kern_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in ev)
+
+    clocks = Clocks(torch.cuda.current_device())
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(args.steps):
+        step(i)
+    t1.record()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    ms = max_over_ranks(torch, dist, ms)
+    kern_ms = max_over_ranks(torch, dist, kern_ms)
+    flops = 2.0 * M * N * K
+    value = flops / (ms * 1e-3) / 1e12
+
+    # end to end through the public API: pinned host bf16 activations ->
+    # act_quant -> fp8_gemm (local shard) [-> all-gather] -> pinned host output
+    x_host = sets[0][4].cpu().pin_memory()
+    o_host = torch.empty(M, N if ws > 1 else n_local, dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty_like(sets[0][4])
+    b_loc, s_loc = shards[0][2], shards[0][3]
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        a, a_s = pkg.act_quant(x_dev, 128)
+        c = pkg.fp8_gemm(a, a_s, b_loc, s_loc)
+        if ws > 1:
+            dist.all_gather_into_tensor(gathered, c)
+            full.view(M, ws, n_local).copy_(gathered.permute(1, 0, 2))
+            c = full
+        o_host.copy_(c, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(torch, dist, e0.elapsed_time(e1) / args.steps)
+
+    peaks, src = load_peaks()
+    peak = 2.0 * peaks["bf16_tflops"]  # dense e4m3 rate = 2x the measured dense bf16 rate
+    local_flops = 2.0 * M * n_local * K
+    achieved = local_flops / (kern_ms * 1e-3) / 1e12
+    traffic = None
+    tfile = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tfile):
+        with open(tfile) as f:
+            traffic = json.load(f).get(f"fp8_gemm_{M}x{n_local}x{K}")
+    line = {
+        "metric": "block-scaled FP8 GEMM TFLOP/s (dense fp8_gemm, 1x128 act + 128x128 weight fp32 scales)",
+        "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong" if ws > 1 else "weak",
+        "vs_baseline": None, "dtype": "e4m3", "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights)",
+        "config": {"workload": f"fp8_gemm M=N=K={M}" + (f", column-sharded TP{ws} + all-gather" if ws > 1 else ""),
+                   "M": M, "N": N, "K": K, "parallelism": f"tp{ws}" if ws > 1 else "none",
+                   "l2": f"{n_sets} rotating input sets ({n_sets * (M * K + n_local * K) // 2**20} MiB) > L2"},
+        "e2e": {"value": round(flops / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * (N if ws > 1 else n_local) * 2,
+                "ms_per_step": round(e2e_ms, 4), "path": "act_quant + fp8_gemm public API, pinned host I/O"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 3), "traffic": traffic,
+                     "kernel": "bsg_kernel<normal,fp8,BN=256>", "kernel_ms": round(kern_ms, 4),
+                     "peak_source": f"2 x bf16_tflops of {src} MEASURED_PEAKS.json (dense e4m3 rate)"},
+        "gpu_launches": args.steps * (1 if ws == 1 else 1),
+        "clocks": clk,
+    }
+    return line
+
+
+def bench_fp4_decode(args, torch, dist, ws, rank, dev):
+    """Config-3 decode sweep point (M tokens, K=4096, N), HBM-bound."""
+    pkg = __import__("importlib").import_module(PKG)
+    M, N, K = args.m, args.n, 4096
+    g = torch.Generator(device=dev)
+    g.manual_seed(77)
+    n_sets = max(8, int(np.ceil(400e6 / (N * K // 2))))  # >= 400 MB of distinct weights: no L2 reuse
+    x = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
+    a, a_s = pkg.act_quant(x, 128)
+    ws_ = [(torch.randint(0, 256, (N, K // 2), generator=g, device=dev, dtype=torch.uint8),
+            (127 - torch.randint(0, 7, (N, K // 32), generator=g, device=dev, dtype=torch.uint8)))
+           for _ in range(n_sets)]
+    out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    lib = pkg._lib.load()
+    st = torch.cuda.current_stream().cuda_stream
+
+    def step(i):
+        b, bs = ws_[i % n_sets]
+        pkg._lib.check(lib.bs_fp4_gemm(a.data_ptr(), a_s.data_ptr(), pkg._lib.DT_F32, b.data_ptr(), bs.data_ptr(),
+                                       pkg._lib.DT_E8M0, M, N, K, out.data_ptr(), st))
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    steps = max(args.steps, 2 * n_sets)
+    clocks = Clocks(torch.cuda.current_device())
+    clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(steps):
+        step(i)
+    t1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / steps
+    nbytes = N * K // 2 + N * K // 32 + M * K + 4 * M * K // 128 + 2 * M * N
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    peaks, src = load_peaks()
+    return {"metric": "fp4_gemm decode HBM GB/s", "value": round(gbs, 1), "unit": "GB/s", "n_gpus": 1,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 x e2m1",
+            "data": "synthetic", "config": {"workload": f"fp4_gemm decode M={M} N={N} K={K}",
+                                            "l2": f"{n_sets} rotating weight copies"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(gbs / peaks["hbm_gbs"], 3), "traffic": None, "peak_source": src},
+            "gpu_launches": steps, "clocks": clk}
+
+
+def max_over_ranks(torch, dist, v):
+    if dist is None:
+        return v
+    t = torch.tensor([v], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# CPU legs: the oracle port of the reference algorithm on the host cores
+# ---------------------------------------------------------------------------
+
+def cpu_threads():
+    return len(os.sched_getaffinity(0))
+
+
+def cpu_fp8_prefill(steps: int, warmup: int, m_rows: int = 4096):
+    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+    import cases
+    from oracle import blockscaled as ob
+    c = cases.cfg2_fp8(M=m_rows)
+    for _ in range(warmup):
+        ob.fp8_gemm(c["a"], c["a_s"], c["b"], c["b_s"])
+    times = []
+    for _ in range(steps):
+        t = time.perf_counter()
+        ob.fp8_gemm(c["a"], c["a_s"], c["b"], c["b_s"])
+        times.append(time.perf_counter() - t)
+    s = min(times)
+    return 2.0 * m_rows * 4096 * 4096 / s / 1e12, s
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["fp8_prefill", "fp4_decode"], default="fp8_prefill")
+    ap.add_argument("--m", type=int, default=16)
+    ap.add_argument("--n", type=int, default=4096)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    ws, rank, local = dist_env()
+
+    if args.impl == "reference":
+        # CPU port of the reference algorithm, rank 0 only; other ranks exit.
+        if rank != 0:
+            return
+        steps = max(1, min(args.steps, 3))
+        v, s = cpu_fp8_prefill(steps, 1)
+        print(json.dumps({
+            "impl": "reference", "metric": "block-scaled FP8 GEMM TFLOP/s (dense fp8_gemm, 1x128 act + 128x128 weight fp32 scales)",
+            "value": round(v, 4), "unit": "TFLOP/s", "n_gpus": ws, "steps": steps, "warmup": 1,
+            "ms_per_step": round(s * 1e3, 2), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "e4m3", "data": "synthetic",
+            "config": {"workload": "fp8_gemm M=N=K=4096 on the host CPU", "M": 4096, "N": 4096, "K": 4096},
+            "cpu_baseline": {"value": round(v, 4), "unit": "TFLOP/s", "cores": cpu_threads(), "kind": "port",
+                             "sample": "one full 4096^3 fp8_gemm per step: LUT dequant -> bf16 -> fp32 matmul (numpy)"},
+            "e2e": {"value": round(v, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }), flush=True)
+        return
+
+    import torch
+    dist = None
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist_mod
+        torch.cuda.set_device(local)
+        dist_mod.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local))
+        dist = dist_mod
+    else:
+        torch.cuda.set_device(0)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    importlib = __import__("importlib")
+    importlib.import_module(PKG)._lib.load()
+
+    if args.workload == "fp8_prefill":
+        line = bench_fp8_prefill(args, torch, dist, ws, rank, dev)
+    else:
+        line = bench_fp4_decode(args, torch, dist, ws, rank, dev)
+
+    if rank == 0 and ws == 1 and args.workload == "fp8_prefill" and not args.no_cpu_baseline:
+        torch.set_num_threads(cpu_threads())
+        v, s = cpu_fp8_prefill(1, 0, m_rows=4096)
+        line["cpu_baseline"] = {"value": round(v, 4), "unit": "TFLOP/s", "cores": cpu_threads(), "kind": "port",
+                                "sample": f"one full 4096^3 fp8_gemm ({s:.2f} s): LUT dequant -> bf16 -> fp32 matmul (numpy)"}
+    pkg = importlib.import_module(PKG)
+    pkg._lib.device_error_check()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,493 @@
+// Block-scaled GEMMs on the sm_100a tensor cores (tcgen05 + TMEM + TMA).
+//
+//   fp8_gemm : C[M,N] = sum_kb (A[:,kb] . B[:,kb]^T) * a_s[m,kb] * b_s[n/128,kb]
+//   fp4_gemm : C[m,n] = sum_k A[m,k] a_s[m,k/128] * e2m1(B[n,k]) 2^(b_s[n,k/32]-127)
+//
+// One CTA computes a 128 x BN tile of D = X . Y^T where X feeds the MMA's
+// A operand (128 rows) and Y its B operand (BN rows).  Normal mode: X = the
+// activations, Y = the weights.  Swap mode (decode, M <= 64): X = the
+// weights, Y = the activations, so a few tokens still fill an M=128 MMA.
+//
+// Warp roles (no thread does two jobs):
+//   warp 0       TMA producer: 128-wide K blocks of X and Y into a ring of
+//                STAGES shared-memory stages (128B swizzle); the per-32-K
+//                ue8m0 scales of the e2m1 operand arrive by cp.async.
+//   warp 1       TMEM allocator and MMA issuer (one elected lane): per K
+//                block, 4 x tcgen05.mma (K=32 each) into a TMEM partial
+//                buffer; fp4 B uses kind::mxf8f6f4.block_scale with its
+//                scales copied into TMEM by tcgen05.cp.
+//   warps 2..    epilogue: per K block, tcgen05.ld the fp32 partial and
+//                fold it into registers with the fp32 scales of that block
+//                (the reference's per-128-K "promotion"; it keeps arbitrary,
+//                non power-of-two fp32 scales exact).  Two partial buffers
+//                let the MMA run one K block ahead of the epilogue.
+// Split-K (swap mode): a thread-block cluster of S CTAs along K reduces its
+// fp32 tiles through distributed shared memory; no workspace, one launch.
+//
+// Every wait is bounded (common.cuh); a stuck pipeline records
+// BS_ERR_DEVICE_TIMEOUT and the CTA exits.
+#include "common.cuh"
+
+namespace {
+
+struct GemmArgs {
+  int M, N, K;
+  const void* a_s;
+  int as_dtype;
+  const void* b_s;
+  int bs_dtype;
+  __nv_bfloat16* c;
+  int kb_per_split;
+};
+
+BS_DEVINL float load_scale(const void* p, int dtype, int64_t idx) {
+  if (dtype == BS_DT_F32) return __ldg(reinterpret_cast<const float*>(p) + idx);
+  return bs_e8m0_to_f32(__ldg(reinterpret_cast<const uint8_t*>(p) + idx));
+}
+
+template <bool SWAP, bool FP4, int BN>
+struct Cfg {
+  static constexpr int kBM = 128;                       // MMA M (rows of X)
+  static constexpr int kBK = 128;                       // K per stage
+  static constexpr int kStages = SWAP ? 4 : (BN == 256 ? 4 : 6);
+  static constexpr int kXBytes = kBM * kBK;             // smem bytes (e2m1 unpacked to 1 B/elem)
+  static constexpr int kYBytes = BN * kBK;
+  static constexpr int kStageBytes = kXBytes + kYBytes;
+  static constexpr bool kXFp4 = SWAP && FP4;
+  static constexpr bool kYFp4 = !SWAP && FP4;
+  static constexpr int kXTx = kXFp4 ? kXBytes / 2 : kXBytes;   // TMA transaction bytes (packed)
+  static constexpr int kYTx = kYFp4 ? kYBytes / 2 : kYBytes;
+  static constexpr int kSfYBlocks = (BN + 127) / 128;
+  static constexpr int kSfBytes = FP4 ? 512 * (1 + kSfYBlocks) : 0;   // per stage: X chunk + Y chunks
+  static constexpr int kEpiWarps = BN > 128 ? 8 : 4;
+  static constexpr int kCols = BN > 128 ? 128 : BN;     // columns per epilogue warp
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;
+  static constexpr int kSfCols = FP4 ? 4 * (1 + kSfYBlocks) : 0;  // TMEM columns per SF slot
+  static constexpr int kTmemNeed = 2 * BN + 2 * kSfCols;
+  static constexpr int kTmemCols = kTmemNeed <= 32 ? 32 : kTmemNeed <= 64 ? 64 : kTmemNeed <= 128 ? 128
+                                   : kTmemNeed <= 256 ? 256 : 512;
+  static_assert(kTmemNeed <= 512, "TMEM budget");
+  static constexpr int kMaxKbSmem = 32;                 // swap mode: column scales cached in smem
+  static constexpr int kColScaleBytes = SWAP ? BN * kMaxKbSmem * 4 : 0;
+  static constexpr int kSmemBytes = 1024 /*align slack*/ + kStages * (kStageBytes + kSfBytes) + kColScaleBytes + 256;
+  static_assert(!SWAP || kStages * kStageBytes >= kBM * BN * 4, "reduction buffer reuses the stage ring");
+};
+
+template <bool SWAP, bool FP4, int BN>
+__global__ void __launch_bounds__(Cfg<SWAP, FP4, BN>::kThreads, 1)
+    bsg_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_y, GemmArgs p) {
+  using C = Cfg<SWAP, FP4, BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stage_base = smem;
+  uint8_t* sf_base = smem + C::kStages * C::kStageBytes;
+  float* col_scale = reinterpret_cast<float*>(sf_base + C::kStages * C::kSfBytes);
+  uint8_t* tail = reinterpret_cast<uint8_t*>(col_scale) + C::kColScaleBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(tail);
+  uint64_t* empty = full + C::kStages;
+  uint64_t* pfull = empty + C::kStages;
+  uint64_t* pempty = pfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int x0 = blockIdx.x * C::kBM;    // first row of X
+  const int y0 = blockIdx.y * BN;        // first row of Y
+  const int num_kb_total = p.K / 128;
+  const int split = blockIdx.z;
+  const int kb_begin = split * p.kb_per_split;
+  int kb_end = kb_begin + p.kb_per_split;
+  if (kb_end > num_kb_total) kb_end = num_kb_total;
+  const int n_kb = kb_end > kb_begin ? kb_end - kb_begin : 0;
+  // rows of M (activations) and N (weights) covered by X / Y
+  const int m0 = SWAP ? y0 : x0;
+  const int n0 = SWAP ? x0 : y0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1 + (FP4 ? 32 : 0));
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&pfull[b], 1);
+      mbar_init(&pempty[b], C::kEpiWarps);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (FP4) {
+    // The activation operand's block scales are 1.0 (its fp32 scales are
+    // applied in the epilogue): fill its SF chunk once in every stage.
+    const int act_chunk = SWAP ? 1 : 0;  // X chunk at 0, Y chunks from 512
+    for (int i = threadIdx.x; i < C::kStages * 128; i += blockDim.x) {
+      const int s = i / 128, w = i % 128;
+      uint32_t* chunk = reinterpret_cast<uint32_t*>(sf_base + s * C::kSfBytes + act_chunk * 512);
+      chunk[w] = 0x7F7F7F7Fu;
+      if (SWAP && C::kSfYBlocks > 1) {
+        for (int b = 1; b < C::kSfYBlocks; ++b)
+          reinterpret_cast<uint32_t*>(sf_base + s * C::kSfBytes + (1 + b) * 512)[w] = 0x7F7F7F7Fu;
+      }
+    }
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_x);
+    tma_prefetch_desc(&tm_y);
+  }
+  // swap mode: fp32 column scales (one per token) for every K block of this split
+  if (SWAP) {
+    for (int i = threadIdx.x; i < n_kb * BN; i += blockDim.x) {
+      const int kbl = i / BN, j = i % BN;
+      const int m = m0 + j;
+      col_scale[kbl * BN + j] = m < p.M ? load_scale(p.a_s, p.as_dtype, (int64_t)m * num_kb_total + kb_begin + kbl) : 0.0f;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    for (int it = 0; it < n_kb; ++it) {
+      const int s = it % C::kStages;
+      const uint32_t ph = (it / C::kStages) & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1, abort_flag))) break;
+      const int kb = kb_begin + it;
+      if (FP4) {
+        // weights' per-32 scales: row r of the 128(+)-row operand lands at
+        // (r%32)*16 + ((r/32)%4)*4 + (r/128)*512, the tcgen05 scale layout.
+        uint8_t* chunk = sf_base + s * C::kSfBytes + (SWAP ? 0 : 512);
+        const int rows = SWAP ? 128 : BN;
+        const uint8_t* bs = reinterpret_cast<const uint8_t*>(p.b_s);
+        const int64_t ld = p.K / 32;
+        for (int r = lane; r < rows; r += 32) {
+          int n = n0 + r;
+          n = n < p.N ? n : p.N - 1;
+          cp_async_4(chunk + (r % 32) * 16 + ((r / 32) % 4) * 4 + (r / 128) * 512, bs + n * ld + kb * 4);
+        }
+        cp_async_mbar_arrive_noinc(&full[s]);
+      }
+      if (lane == 0) {
+        uint8_t* sx = stage_base + s * C::kStageBytes;
+        uint8_t* sy = sx + C::kXBytes;
+        mbar_arrive_expect_tx(&full[s], C::kXTx + C::kYTx);
+        tma_load_2d(sx, &tm_x, &full[s], kb * 128, x0);
+        tma_load_2d(sy, &tm_y, &full[s], kb * 128, y0);
+      }
+      __syncwarp();
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    const uint32_t sf_col0 = 2 * BN;
+    for (int it = 0; it < n_kb; ++it) {
+      const int s = it % C::kStages;
+      const uint32_t ph = (it / C::kStages) & 1;
+      const int buf = it & 1;
+      const uint32_t pph = (it >> 1) & 1;
+      bool ok = mbar_wait(&full[s], ph, abort_flag);
+      ok = ok && mbar_wait(&pempty[buf], pph ^ 1, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      if (FP4) fence_proxy_async_smem();
+      if (lane == 0) {
+        const uint32_t sx = smem_u32(stage_base + s * C::kStageBytes);
+        const uint32_t sy = sx + C::kXBytes;
+        const uint32_t d = tmem_base + buf * BN;
+        if constexpr (FP4) {
+          const uint32_t slot = sf_col0 + (it & 1) * C::kSfCols;
+          const uint32_t sfa = tmem_base + slot;
+          const uint32_t sfb = tmem_base + slot + 4;
+          const uint32_t sfs = smem_u32(sf_base + s * C::kSfBytes);
+          tc_cp_32x128b_warpx4(sfa, sdesc_sf_chunk(sfs));
+          for (int b = 0; b < C::kSfYBlocks; ++b) tc_cp_32x128b_warpx4(sfb + 4 * b, sdesc_sf_chunk(sfs + 512 * (1 + b)));
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t idesc =
+                idesc_mxf8f6f4(C::kXFp4 ? 5 : 0, C::kYFp4 ? 5 : 0, 128, BN, k, k);
+            tc_mma_mxf8f6f4(d, sdesc_k128_sw128(sx + k * 32), sdesc_k128_sw128(sy + k * 32), idesc,
+                            sfa | ((uint32_t)k << 30), sfb | ((uint32_t)k << 30), k > 0 ? 1u : 0u);
+          }
+        } else {
+          constexpr uint32_t idesc = idesc_f8f6f4(0, 0, 128, BN);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            tc_mma_f8f6f4(d, sdesc_k128_sw128(sx + k * 32), sdesc_k128_sw128(sy + k * 32), idesc, k > 0 ? 1u : 0u);
+        }
+        tc_commit(&empty[s]);
+        tc_commit(&pfull[buf]);
+      }
+      __syncwarp();
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int ew = warp - 2;                 // epilogue warp index
+    const int quad = warp & 3;               // TMEM lane quadrant this warp may access
+    const int col0 = (ew >> 2) * C::kCols;   // column half for BN = 256
+    const int row = quad * 32 + lane;        // row of the 128-row X tile
+    const int64_t nkb_all = num_kb_total;
+    float acc[C::kCols];
+#pragma unroll
+    for (int j = 0; j < C::kCols; ++j) acc[j] = 0.0f;
+
+    // scale of this thread's X row for K block kb
+    auto row_scale = [&](int kb) -> float {
+      if (!SWAP) {
+        const int m = x0 + row;
+        return m < p.M ? load_scale(p.a_s, p.as_dtype, (int64_t)m * nkb_all + kb) : 0.0f;
+      } else if (!FP4) {
+        const int n = x0 + row;
+        return load_scale(p.b_s, p.bs_dtype, (int64_t)((n < p.N ? n : p.N - 1) / 128) * nkb_all + kb);
+      }
+      return 1.0f;
+    };
+    // normal-mode fp8: one B scale per 128 columns
+    auto blk_scale = [&](int kb) -> float {
+      if (!SWAP && !FP4) {
+        int n = y0 + col0;
+        n = n < p.N ? n : p.N - 1;
+        return load_scale(p.b_s, p.bs_dtype, (int64_t)(n / 128) * nkb_all + kb);
+      }
+      return 1.0f;
+    };
+
+    float rs_next = n_kb > 0 ? row_scale(kb_begin) * blk_scale(kb_begin) : 0.0f;
+    for (int it = 0; it < n_kb; ++it) {
+      const int buf = it & 1;
+      const uint32_t pph = (it >> 1) & 1;
+      const float rs = rs_next;
+      if (it + 1 < n_kb) rs_next = row_scale(kb_begin + it + 1) * blk_scale(kb_begin + it + 1);
+      if (!__all_sync(0xffffffffu, mbar_wait(&pfull[buf], pph, abort_flag))) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + buf * BN + col0;
+#pragma unroll
+      for (int c = 0; c < C::kCols / 16; ++c) {
+        uint32_t r[16];
+        BS_TMEM_LD16(taddr + c * 16, r);
+        tmem_ld_wait();
+        if constexpr (SWAP) {
+          const float* cs = col_scale + it * BN + c * 16;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc[c * 16 + j] = fmaf(__uint_as_float(r[j]), rs * cs[j], acc[c * 16 + j]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc[c * 16 + j] = fmaf(__uint_as_float(r[j]), rs, acc[c * 16 + j]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&pempty[buf]);
+    }
+
+    if (gridDim.z == 1) {
+      if (!SWAP) {
+        const int m = x0 + row;
+        if (m < p.M) {
+          __nv_bfloat16* out = p.c + (int64_t)m * p.N;
+          const bool vec_ok = (p.N % 8) == 0;
+#pragma unroll
+          for (int j = 0; j < C::kCols; j += 8) {
+            const int n = y0 + col0 + j;
+            if (vec_ok && n + 8 <= p.N) {
+              uint4 v;
+              __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&v);
+#pragma unroll
+              for (int t = 0; t < 4; ++t) h[t] = __floats2bfloat162_rn(acc[j + 2 * t], acc[j + 2 * t + 1]);
+              *reinterpret_cast<uint4*>(out + n) = v;
+            } else {
+#pragma unroll
+              for (int t = 0; t < 8; ++t)
+                if (n + t < p.N) out[n + t] = __float2bfloat16_rn(acc[j + t]);
+            }
+          }
+        }
+      } else {
+        const int n = x0 + row;
+        if (n < p.N) {
+#pragma unroll
+          for (int j = 0; j < BN; ++j) {
+            const int m = y0 + j;
+            if (m < p.M) p.c[(int64_t)m * p.N + n] = __float2bfloat16_rn(acc[j]);
+          }
+        }
+      }
+    } else {
+      // split-K: park the fp32 tile in this CTA's (now idle) stage ring
+      float* red = reinterpret_cast<float*>(stage_base);
+#pragma unroll
+      for (int j = 0; j < C::kCols; j += 4)
+        *reinterpret_cast<float4*>(red + row * BN + col0 + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+    }
+  }
+
+  if (gridDim.z > 1) {
+    // every thread of every CTA in the cluster takes part in both barriers
+    __syncthreads();
+    cluster_sync();
+    if (SWAP && warp >= 2) {
+      const int S = gridDim.z;
+      const int rank = (int)cluster_ctarank();
+      const int rows_per = C::kBM / S;
+      const int t = threadIdx.x - 64;
+      const int nthr = blockDim.x - 64;
+      const uint32_t red_local = smem_u32(stage_base);
+      // this CTA reduces rows [rank*rows_per, (rank+1)*rows_per) over all S tiles
+      for (int e = t; e < rows_per * (BN / 4); e += nthr) {
+        const int rr = rank * rows_per + e % rows_per;
+        const int j4 = (e / rows_per) * 4;
+        float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int q = 0; q < S; ++q) {
+          float4 v = ld_shared_cluster_f4(mapa_shared(red_local + (uint32_t)(rr * BN + j4) * 4, q));
+          sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
+        }
+        const int n = x0 + rr;
+        if (n < p.N) {
+          const float vals[4] = {sum.x, sum.y, sum.z, sum.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int m = y0 + j4 + u;
+            if (m < p.M) p.c[(int64_t)m * p.N + n] = __float2bfloat16_rn(vals[u]);
+          }
+        }
+      }
+    }
+    cluster_sync();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side: tensor maps and launch
+// ---------------------------------------------------------------------------
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// 2-D K-major map: inner dim K (elements), outer dim rows; box 128 x box_rows.
+bool make_map(CUtensorMap* m, const void* base, bool fp4, int64_t K, int64_t rows, int box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(fp4 ? K / 2 : K)};
+  cuuint32_t box[2] = {128u, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = enc(m, fp4 ? CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int g_num_sms = 0;
+int num_sms() {
+  if (!g_num_sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return g_num_sms;
+}
+
+template <bool SWAP, bool FP4, int BN>
+cudaError_t launch(const CUtensorMap& mx, const CUtensorMap& my, const GemmArgs& a, dim3 grid, int split,
+                   cudaStream_t st) {
+  using C = Cfg<SWAP, FP4, BN>;
+  auto kern = bsg_kernel<SWAP, FP4, BN>;
+  static bool attr_done = false;
+  if (!attr_done) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    if (SWAP) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    attr_done = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(C::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  cfg.numAttrs = 0;
+  if (split > 1) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = split;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, kern, mx, my, a);
+}
+
+}  // namespace
+
+// Returns 0 on success, BS_ERR_UNSUPPORTED if a tensor map could not be
+// built, or BS_ERR_CUDA with the CUDA error in *cerr.
+int bs_launch_gemm(bool fp4, const void* a, const void* a_s, int as_dtype, const void* b, const void* b_s,
+                   int bs_dtype, int64_t M, int64_t N, int64_t K, void* c, cudaStream_t st, cudaError_t* cerr) {
+  *cerr = cudaSuccess;
+  GemmArgs args;
+  args.M = (int)M;
+  args.N = (int)N;
+  args.K = (int)K;
+  args.a_s = a_s;
+  args.as_dtype = as_dtype;
+  args.b_s = b_s;
+  args.bs_dtype = bs_dtype;
+  args.c = reinterpret_cast<__nv_bfloat16*>(c);
+  const int nkb = (int)(K / 128);
+  CUtensorMap mx, my;
+  if (M <= 64) {
+    // decode: weights as the 128-row MMA operand, tokens as N = 16..64
+    const int bn = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
+    if (!make_map(&mx, b, fp4, K, N, 128) || !make_map(&my, a, false, K, M, bn)) return BS_ERR_UNSUPPORTED;
+    const int x_tiles = (int)((N + 127) / 128);
+    const int y_tiles = (int)((M + bn - 1) / bn);
+    int split = 1;
+    const int slots = 2 * num_sms();
+    while (split < 8 && x_tiles * y_tiles * split * 2 <= slots && nkb % (split * 2) == 0 && nkb / (split * 2) >= 2)
+      split *= 2;
+    // the column scales of one split are cached in shared memory (32 K blocks)
+    while (split < 8 && (nkb + split - 1) / split > 32) split *= 2;
+    args.kb_per_split = (nkb + split - 1) / split;
+    if (args.kb_per_split > 32) return BS_ERR_UNSUPPORTED;
+    dim3 grid(x_tiles, y_tiles, split);
+#define BS_DEC(F, B) *cerr = launch<true, F, B>(mx, my, args, grid, split, st)
+    if (fp4) {
+      if (bn == 16) BS_DEC(true, 16); else if (bn == 32) BS_DEC(true, 32); else BS_DEC(true, 64);
+    } else {
+      if (bn == 16) BS_DEC(false, 16); else if (bn == 32) BS_DEC(false, 32); else BS_DEC(false, 64);
+    }
+#undef BS_DEC
+  } else {
+    const int bn = fp4 ? 128 : 256;
+    if (!make_map(&mx, a, false, K, M, 128) || !make_map(&my, b, fp4, K, N, bn)) return BS_ERR_UNSUPPORTED;
+    args.kb_per_split = nkb;
+    dim3 grid((unsigned)((M + 127) / 128), (unsigned)((N + bn - 1) / bn), 1);
+    if (fp4) *cerr = launch<false, true, 128>(mx, my, args, grid, 1, st);
+    else *cerr = launch<false, false, 256>(mx, my, args, grid, 1, st);
+  }
+  return *cerr == cudaSuccess ? 0 : BS_ERR_CUDA;
+}

@@ -1,0 +1,6 @@
+// The whole library is one translation unit: the kernels, their launchers
+// and the extern "C" entry points share the device error word directly.
+#include "common.cuh"
+#include "quant.cu"
+#include "gemm.cu"
+#include "capi.cu"

@@ -1,0 +1,260 @@
+// Block-wise quantisers: act_quant (e4m3, 1 x block scales), its in-place
+// quantise-dequantise form, and the in-place e2m1 fake quantiser.
+//
+// HBM-bound byte work: every thread moves one 16-byte vector per pass, the
+// threads of one quantisation block reduce amax with warp shuffles, and the
+// grid is a multiple of the SM count with a grid-stride loop.
+//
+// Rounding follows the reference's PyTorch ops exactly (kernel_sm121.py):
+//   act_quant      :55-87   amax clamp 1e-4, s = amax/448 (IEEE divide),
+//                           optional 2^ceil(log2 s), y = e4m3_rn(clamp(x/s))
+//   fp4_act_quant  :94-121  s = 2^ceil(log2(max(amax, 6*2^-126)/6)),
+//                           nearest e2m1 magnitude with ties to the smaller,
+//                           sign from torch.sign (+0 for -0 and NaN)
+#include "common.cuh"
+
+namespace {
+
+constexpr int kThreads = 256;
+
+template <typename T> struct Vec;
+template <> struct Vec<__nv_bfloat16> { using type = uint4; static constexpr int n = 8; };
+template <> struct Vec<__half> { using type = uint4; static constexpr int n = 8; };
+template <> struct Vec<float> { using type = uint4; static constexpr int n = 4; };
+
+template <typename T>
+BS_DEVINL void unpack(const uint4& v, float* f) {
+  const T* p = reinterpret_cast<const T*>(&v);
+#pragma unroll
+  for (int i = 0; i < Vec<T>::n; ++i) f[i] = bs_to_f32<T>(p[i]);
+}
+
+template <typename T>
+BS_DEVINL uint4 pack(const float* f) {
+  uint4 v;
+  T* p = reinterpret_cast<T*>(&v);
+#pragma unroll
+  for (int i = 0; i < Vec<T>::n; ++i) p[i] = bs_from_f32<T>(f[i]);
+  return v;
+}
+
+// max of |x| that propagates NaN like torch.amax
+BS_DEVINL float nan_max(float m, float a) { return (a > m || a != a) ? a : m; }
+
+constexpr int kMaxVecPerThread = 4;
+
+// One group of `tpb` consecutive lanes owns one quantisation block of
+// `bs` elements; each lane holds `nv` 16-byte vectors of it.
+template <typename T, bool kInplace>
+__global__ void __launch_bounds__(kThreads) act_quant_kernel(const T* __restrict__ x, T* __restrict__ xout,
+                                                             uint8_t* __restrict__ y, void* __restrict__ s,
+                                                             int s_dtype, int64_t n_groups, int bs, int tpb_log2,
+                                                             int nv, int pow2) {
+  constexpr int V = Vec<T>::n;
+  const int tpb = 1 << tpb_log2;
+  const int lane_g = threadIdx.x & (tpb - 1);
+  const int groups_per_warp = 32 >> tpb_log2;
+  const int64_t warp_global = ((int64_t)blockIdx.x * kThreads + threadIdx.x) >> 5;
+  const int64_t n_warps = ((int64_t)gridDim.x * kThreads) >> 5;
+  const int sub = (threadIdx.x & 31) >> tpb_log2;
+
+  for (int64_t g0 = warp_global * groups_per_warp; g0 < n_groups; g0 += n_warps * groups_per_warp) {
+    const int64_t g = g0 + sub;
+    const bool valid = g < n_groups;
+    float f[kMaxVecPerThread][V];
+    float amax = 0.0f;
+#pragma unroll
+    for (int v = 0; v < kMaxVecPerThread; ++v) {
+      if (v < nv) {
+        if (valid) {
+          const int64_t off = g * bs + ((int64_t)v * tpb + lane_g) * V;
+          uint4 raw = __ldg(reinterpret_cast<const uint4*>(x + off));
+          unpack<T>(raw, f[v]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < V; ++i) f[v][i] = 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < V; ++i) amax = nan_max(amax, fabsf(f[v][i]));
+      }
+    }
+    for (int o = tpb >> 1; o > 0; o >>= 1) amax = nan_max(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    amax = amax < 1e-4f ? 1e-4f : amax;  // torch.clamp(min=1e-4); NaN passes through
+    float scale = __fdiv_rn(amax, 448.0f);
+    if (pow2) scale = bs_round_pow2(scale);
+    if (!valid) continue;
+#pragma unroll
+    for (int v = 0; v < kMaxVecPerThread; ++v) {
+      if (v < nv) {
+        const int64_t off = g * bs + ((int64_t)v * tpb + lane_g) * V;
+        uint8_t codes[V];
+#pragma unroll
+        for (int i = 0; i < V; i += 2) {
+          float q0 = bs_clamp(__fdiv_rn(f[v][i], scale), -448.0f, 448.0f);
+          float q1 = bs_clamp(__fdiv_rn(f[v][i + 1], scale), -448.0f, 448.0f);
+          uint16_t c2 = bs_cvt_e4m3x2(q0, q1);
+          codes[i] = (uint8_t)(c2 & 0xFF);
+          codes[i + 1] = (uint8_t)(c2 >> 8);
+        }
+        if constexpr (kInplace) {
+          float r[V];
+#pragma unroll
+          for (int i = 0; i < V; ++i) r[i] = bs_e4m3_to_f32(codes[i]) * scale;
+          *reinterpret_cast<uint4*>(xout + off) = pack<T>(r);
+        } else {
+          if constexpr (V == 8) {
+            uint2 w;
+            w.x = codes[0] | (codes[1] << 8) | (codes[2] << 16) | ((uint32_t)codes[3] << 24);
+            w.y = codes[4] | (codes[5] << 8) | (codes[6] << 16) | ((uint32_t)codes[7] << 24);
+            *reinterpret_cast<uint2*>(y + off) = w;
+          } else {
+            uint32_t w = codes[0] | (codes[1] << 8) | (codes[2] << 16) | ((uint32_t)codes[3] << 24);
+            *reinterpret_cast<uint32_t*>(y + off) = w;
+          }
+        }
+      }
+    }
+    if (!kInplace && lane_g == 0) {
+      if (s_dtype == BS_DT_F32) reinterpret_cast<float*>(s)[g] = scale;
+      else if (s_dtype == BS_DT_BF16) reinterpret_cast<__nv_bfloat16*>(s)[g] = __float2bfloat16_rn(scale);
+      else if (s_dtype == BS_DT_F16) reinterpret_cast<__half*>(s)[g] = __float2half_rn(scale);
+      else reinterpret_cast<uint8_t*>(s)[g] = bs_f32_to_e8m0(scale);
+    }
+  }
+}
+
+// e2m1 magnitudes {0,.5,1,1.5,2,3,4,6}: index = number of midpoints
+// {.25,.75,1.25,1.75,2.5,3.5,5} strictly below |v| (a tie keeps the smaller
+// magnitude, as argmin's first index does).  Differences to the two
+// neighbouring table values are exact in fp32, so this is the reference's
+// argmin over |v - table|.
+BS_DEVINL float e2m1_nearest(float a) {
+  float r = 0.0f;
+  r = a > 0.25f ? 0.5f : r;
+  r = a > 0.75f ? 1.0f : r;
+  r = a > 1.25f ? 1.5f : r;
+  r = a > 1.75f ? 2.0f : r;
+  r = a > 2.5f ? 3.0f : r;
+  r = a > 3.5f ? 4.0f : r;
+  r = a > 5.0f ? 6.0f : r;
+  return r;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) fp4_act_quant_kernel(T* __restrict__ x, int64_t n_groups, int bs,
+                                                                  int tpb_log2, int nv) {
+  constexpr int V = Vec<T>::n;
+  const int tpb = 1 << tpb_log2;
+  const int lane_g = threadIdx.x & (tpb - 1);
+  const int groups_per_warp = 32 >> tpb_log2;
+  const int64_t warp_global = ((int64_t)blockIdx.x * kThreads + threadIdx.x) >> 5;
+  const int64_t n_warps = ((int64_t)gridDim.x * kThreads) >> 5;
+  const int sub = (threadIdx.x & 31) >> tpb_log2;
+
+  for (int64_t g0 = warp_global * groups_per_warp; g0 < n_groups; g0 += n_warps * groups_per_warp) {
+    const int64_t g = g0 + sub;
+    const bool valid = g < n_groups;
+    float f[kMaxVecPerThread][V];
+    float amax = 0.0f;
+#pragma unroll
+    for (int v = 0; v < kMaxVecPerThread; ++v) {
+      if (v < nv) {
+        if (valid) {
+          const int64_t off = g * bs + ((int64_t)v * tpb + lane_g) * V;
+          unpack<T>(*reinterpret_cast<const uint4*>(x + off), f[v]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < V; ++i) f[v][i] = 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < V; ++i) amax = nan_max(amax, fabsf(f[v][i]));
+      }
+    }
+    for (int o = tpb >> 1; o > 0; o >>= 1) amax = nan_max(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float floor_v = 6.0f * 1.1754943508222875e-38f;  // 6 * 2^-126
+    amax = amax < floor_v ? floor_v : amax;
+    const float scale = bs_round_pow2(__fdiv_rn(amax, 6.0f));
+    if (!valid) continue;
+#pragma unroll
+    for (int v = 0; v < kMaxVecPerThread; ++v) {
+      if (v < nv) {
+        const int64_t off = g * bs + ((int64_t)v * tpb + lane_g) * V;
+        float r[V];
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+          float c = bs_clamp(__fdiv_rn(f[v][i], scale), -6.0f, 6.0f);
+          float sgn = c > 0.0f ? 1.0f : (c < 0.0f ? -1.0f : 0.0f);
+          float q = sgn * e2m1_nearest(fabsf(c));
+          r[i] = q * scale;
+        }
+        *reinterpret_cast<uint4*>(x + off) = pack<T>(r);
+      }
+    }
+  }
+}
+
+int grid_for(int64_t n_groups, int tpb) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t threads = n_groups * tpb;
+  int64_t blocks = (threads + kThreads - 1) / kThreads;
+  const int64_t cap = (int64_t)sms * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return (int)blocks;
+}
+
+int ilog2(int v) {
+  int r = 0;
+  while ((1 << r) < v) ++r;
+  return r;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// host launchers (called from capi.cu after argument validation)
+// ---------------------------------------------------------------------------
+
+cudaError_t bs_launch_act_quant(const void* x, int x_dtype, int64_t rows, int64_t K, int bs, int pow2, void* y,
+                                void* s, int s_dtype, bool inplace, cudaStream_t st) {
+  const int V = x_dtype == BS_DT_F32 ? 4 : 8;
+  const int lanes = bs / V;
+  const int tpb = lanes < 32 ? lanes : 32;
+  const int nv = lanes / tpb;
+  const int64_t n_groups = rows * (K / bs);
+  if (n_groups == 0) return cudaSuccess;
+  const int grid = grid_for(n_groups, tpb);
+  const int tl = ilog2(tpb);
+#define BS_AQ(T)                                                                                                  \
+  if (inplace)                                                                                                    \
+    act_quant_kernel<T, true><<<grid, kThreads, 0, st>>>((const T*)x, (T*)x, nullptr, nullptr, 0, n_groups, bs,   \
+                                                          tl, nv, pow2);                                          \
+  else                                                                                                            \
+    act_quant_kernel<T, false><<<grid, kThreads, 0, st>>>((const T*)x, nullptr, (uint8_t*)y, s, s_dtype,          \
+                                                           n_groups, bs, tl, nv, pow2);
+  if (x_dtype == BS_DT_BF16) { BS_AQ(__nv_bfloat16) }
+  else if (x_dtype == BS_DT_F16) { BS_AQ(__half) }
+  else { BS_AQ(float) }
+#undef BS_AQ
+  return cudaGetLastError();
+}
+
+cudaError_t bs_launch_fp4_act_quant(void* x, int x_dtype, int64_t rows, int64_t K, int bs, cudaStream_t st) {
+  const int V = x_dtype == BS_DT_F32 ? 4 : 8;
+  const int lanes = bs / V;
+  const int tpb = lanes < 32 ? lanes : 32;
+  const int nv = lanes / tpb;
+  const int64_t n_groups = rows * (K / bs);
+  if (n_groups == 0) return cudaSuccess;
+  const int grid = grid_for(n_groups, tpb);
+  const int tl = ilog2(tpb);
+  if (x_dtype == BS_DT_BF16)
+    fp4_act_quant_kernel<__nv_bfloat16><<<grid, kThreads, 0, st>>>((__nv_bfloat16*)x, n_groups, bs, tl, nv);
+  else if (x_dtype == BS_DT_F16)
+    fp4_act_quant_kernel<__half><<<grid, kThreads, 0, st>>>((__half*)x, n_groups, bs, tl, nv);
+  else
+    fp4_act_quant_kernel<float><<<grid, kThreads, 0, st>>>((float*)x, n_groups, bs, tl, nv);
+  return cudaGetLastError();
+}

@@ -1,0 +1,192 @@
+"""Drop-in replacement for the block-scaled ops of the reference's ``kernel`` module.
+
+The reference (``kernel_sm121.py``) is injected as ``sys.modules['kernel']``
+and DeepSeek's model code does ``from kernel import act_quant, fp4_act_quant,
+fp8_gemm, fp4_gemm, ...``.  This module keeps those four signatures, defaults,
+return conventions and error behaviour, and runs every call through the
+sm_100a CUDA library (``libbsgemm.so``, C ABI in ``include/bsgemm.h``):
+
+  act_quant(x, block_size=128, scale_fmt=None, scale_dtype=torch.float32, inplace=False)
+  fp4_act_quant(x, block_size=32, inplace=False)
+  fp8_gemm(a, a_s, b, b_s, scale_dtype=torch.float32)
+  fp4_gemm(a, a_s, b, b_s, scale_dtype=torch.float32)
+
+CPU tensors are an error: there is no CPU fallback here.
+"""
+
+from __future__ import annotations
+
+import time as _time
+from collections import defaultdict
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+__all__ = ["act_quant", "fp4_act_quant", "fp8_gemm", "fp4_gemm", "profile_report"]
+
+# Same shape as the reference's profiler (kernel_sm121.py:31-44): call count
+# and host seconds per op.  Host time without a device sync measures launch
+# cost for asynchronous kernels, exactly as in the reference.
+_PROFILE = defaultdict(lambda: [0, 0.0])
+
+
+def profile_report():
+    """Print accumulated per-op call counts / host seconds and reset."""
+    if not _PROFILE:
+        return
+    print("[bsgemm] === Profile Report ===", flush=True)
+    total = sum(v[1] for v in _PROFILE.values())
+    for name, (cnt, sec) in sorted(_PROFILE.items(), key=lambda kv: -kv[1][1]):
+        pct = sec / total * 100 if total > 0 else 0
+        print(f"  {name:25s}: {cnt:6d} calls, {sec:7.3f}s ({pct:5.1f}%)", flush=True)
+    print(f"  {'TOTAL':25s}: {sum(v[0] for v in _PROFILE.values()):6d} calls, {total:7.3f}s", flush=True)
+    _PROFILE.clear()
+
+
+_X_DT = {torch.bfloat16: _lib.DT_BF16, torch.float16: _lib.DT_F16, torch.float32: _lib.DT_F32}
+_S_DT = {torch.float32: _lib.DT_F32, torch.bfloat16: _lib.DT_BF16, torch.float16: _lib.DT_F16,
+         torch.float8_e8m0fnu: _lib.DT_E8M0}
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _require_cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if not t.is_cuda:
+            raise RuntimeError("bsgemm ops run on CUDA tensors only (no CPU fallback)")
+
+
+def act_quant(x: torch.Tensor, block_size: int = 128, scale_fmt: Optional[str] = None,
+              scale_dtype: torch.dtype = torch.float32, inplace: bool = False):
+    """Block-wise e4m3 quantisation (kernel_sm121.py:55-87).
+
+    Returns ``(y, s)`` with ``y`` float8_e4m3fn shaped like ``x`` and ``s``
+    shaped ``[..., K/block_size]`` in ``scale_dtype``; with ``inplace=True``
+    quantises-dequantises ``x`` in place and returns it.
+    """
+    t0 = _time.perf_counter()
+    N = x.size(-1)
+    assert N % block_size == 0
+    _require_cuda(x)
+    xc = x.contiguous()
+    if xc.dtype not in _X_DT:
+        xc = xc.float()
+    rows = xc.numel() // N if N else 0
+    lib = _lib.load()
+    pow2 = 1 if scale_fmt is not None else 0
+    if inplace:
+        _lib.check(lib.bs_act_quant_inplace(xc.data_ptr(), _X_DT[xc.dtype], rows, N, block_size, pow2, _stream(x)))
+        if xc.data_ptr() != x.data_ptr() or xc.dtype != x.dtype:
+            x.copy_(xc)
+        _PROFILE["act_quant_inplace"][0] += 1
+        _PROFILE["act_quant_inplace"][1] += _time.perf_counter() - t0
+        return x
+    if scale_dtype not in _S_DT:
+        raise NotImplementedError(f"act_quant: scale_dtype {scale_dtype} not supported")
+    y = torch.empty(x.shape, dtype=torch.float8_e4m3fn, device=x.device)
+    s = torch.empty(*x.shape[:-1], N // block_size, dtype=scale_dtype, device=x.device)
+    _lib.check(lib.bs_act_quant(xc.data_ptr(), _X_DT[xc.dtype], rows, N, block_size, pow2, y.data_ptr(),
+                                s.data_ptr(), _S_DT[scale_dtype], _stream(x)))
+    _PROFILE["act_quant"][0] += 1
+    _PROFILE["act_quant"][1] += _time.perf_counter() - t0
+    return y, s
+
+
+def fp4_act_quant(x: torch.Tensor, block_size: int = 32, inplace: bool = False) -> torch.Tensor:
+    """In-place e2m1 fake quantisation (kernel_sm121.py:94-124)."""
+    N = x.size(-1)
+    assert N % block_size == 0
+    if not inplace:
+        raise NotImplementedError("fp4_act_quant non-inplace not needed for sm_121 fallback")
+    _require_cuda(x)
+    xc = x.contiguous()
+    if xc.dtype not in _X_DT:
+        xc = xc.float()
+    rows = xc.numel() // N if N else 0
+    _lib.check(_lib.load().bs_fp4_act_quant_inplace(xc.data_ptr(), _X_DT[xc.dtype], rows, N, block_size, _stream(x)))
+    if xc.data_ptr() != x.data_ptr() or xc.dtype != x.dtype:
+        x.copy_(xc)
+    return x
+
+
+def _scale_arg(s: torch.Tensor):
+    """Scales as the library takes them: fp32 or raw e8m0 bytes."""
+    if s.dtype == torch.float8_e8m0fnu:
+        return s.contiguous(), _lib.DT_E8M0
+    if s.dtype == torch.float32:
+        return s.contiguous(), _lib.DT_F32
+    return s.float().contiguous(), _lib.DT_F32
+
+
+def fp8_gemm(a: torch.Tensor, a_s: torch.Tensor, b: torch.Tensor, b_s: torch.Tensor,
+             scale_dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """C[M,N] = A_e4m3[M,K] @ B_e4m3[N,K]^T with 1x128 / 128x128 block scales
+    (kernel_sm121.py:190-255).  Returns bf16 shaped ``[..., N]``."""
+    t0 = _time.perf_counter()
+    K = a.size(-1)
+    M = a.numel() // K
+    N = b.size(0)
+    out_shape = (*a.shape[:-1], N)
+    _require_cuda(a, a_s, b, b_s)
+    a_flat = a.view(M, K).contiguous()
+    b_flat = b.contiguous()
+    a_sf, as_dt = _scale_arg(a_s.view(M, -1))
+    b_sf, bs_dt = _scale_arg(b_s)
+    if a_flat.dtype != torch.float8_e4m3fn or b_flat.dtype != torch.float8_e4m3fn:
+        raise TypeError("fp8_gemm expects float8_e4m3fn operands")
+    if a_sf.shape != (M, K // 128) or b_sf.shape != ((N + 127) // 128, K // 128):
+        raise ValueError(f"fp8_gemm: scale shapes {tuple(a_sf.shape)} / {tuple(b_sf.shape)} do not match "
+                         f"M={M}, N={N}, K={K}")
+    out = torch.empty(M, N, device=a.device, dtype=torch.bfloat16)
+    _lib.check(_lib.load().bs_fp8_gemm(a_flat.data_ptr(), a_sf.data_ptr(), as_dt, b_flat.data_ptr(),
+                                       b_sf.data_ptr(), bs_dt, M, N, K, out.data_ptr(), _stream(a)))
+    _PROFILE["fp8_gemm"][0] += 1
+    _PROFILE["fp8_gemm"][1] += _time.perf_counter() - t0
+    return out.view(out_shape)
+
+
+def _fp4_weight_scales(b_s: torch.Tensor) -> torch.Tensor:
+    if b_s.dtype == torch.float8_e8m0fnu:
+        return b_s.contiguous()
+    # fp32 weight scales are usable only if they are exact powers of two in
+    # the e8m0 range (the reference's CPU path multiplies by them exactly).
+    f = b_s.float().contiguous()
+    bits = f.view(torch.int32)
+    exact = bool(((bits & 0x807FFFFF) == 0).all()) and bool(((bits >> 23) > 0).all())
+    if not exact:
+        raise NotImplementedError("fp4_gemm: fp32 weight scales must be powers of two (ue8m0)")
+    return (bits >> 23).to(torch.uint8).view(torch.float8_e8m0fnu)
+
+
+def fp4_gemm(a: torch.Tensor, a_s: torch.Tensor, b: torch.Tensor, b_s: torch.Tensor,
+             scale_dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """C[M,N] = A_e4m3[M,K] @ B_e2m1[N,K]^T; A scales per 1x128, B scales
+    ue8m0 per 1x32 (kernel_sm121.py:343-421).  ``b`` is packed two codes per
+    byte ``[N, K/2]`` (float4_e2m1fn_x2 or uint8).  Returns bf16 ``[..., N]``."""
+    t0 = _time.perf_counter()
+    K = a.size(-1)
+    M = a.numel() // K
+    N = b.size(0)
+    out_shape = (*a.shape[:-1], N)
+    _require_cuda(a, a_s, b, b_s)
+    a_flat = a.view(M, K).contiguous()
+    if a_flat.dtype != torch.float8_e4m3fn:
+        raise TypeError("fp4_gemm expects a float8_e4m3fn activation")
+    b_u8 = b.contiguous().view(torch.uint8)
+    if b_u8.shape != (N, K // 2):
+        raise ValueError(f"fp4_gemm: weight shape {tuple(b.shape)} does not match K={K}")
+    a_sf, as_dt = _scale_arg(a_s.view(M, -1))
+    b_sf = _fp4_weight_scales(b_s)
+    if a_sf.shape != (M, K // 128) or b_sf.shape != (N, K // 32):
+        raise ValueError(f"fp4_gemm: scale shapes {tuple(a_sf.shape)} / {tuple(b_sf.shape)} do not match "
+                         f"M={M}, N={N}, K={K}")
+    out = torch.empty(M, N, device=a.device, dtype=torch.bfloat16)
+    _lib.check(_lib.load().bs_fp4_gemm(a_flat.data_ptr(), a_sf.data_ptr(), as_dt, b_u8.data_ptr(),
+                                       b_sf.data_ptr(), _lib.DT_E8M0, M, N, K, out.data_ptr(), _stream(a)))
+    _PROFILE["fp4_gemm"][0] += 1
+    _PROFILE["fp4_gemm"][1] += _time.perf_counter() - t0
+    return out.view(out_shape)

@@ -1,0 +1,112 @@
+/*
+ * bsgemm.h - C ABI of the B200 (sm_100a) block-scaled quantise / GEMM library.
+ *
+ * The library replaces the hot path of the reference module kernel_sm121.py
+ * (lmxxf/deepseek-v4-experimental-platform-on-dgx-spark): act_quant,
+ * fp4_act_quant, fp8_gemm, fp4_gemm, and the per-expert MoE loop that calls
+ * them.  Every entry point:
+ *   - takes plain device pointers, element counts and a CUDA stream
+ *     (cudaStream_t passed as void*; NULL = legacy default stream);
+ *   - never allocates: the caller owns every buffer, including workspace;
+ *   - enqueues work on the stream and returns without synchronising;
+ *   - returns 0 on success or a BS_ERR_* code, with a message available from
+ *     bs_last_error() (thread-local).  No C++ exception crosses the ABI.
+ * Device-side failures (a bounded wait that ran out) are recorded in a
+ * device word and reported by bs_device_error_check().
+ *
+ * Layouts (all row-major, contiguous):
+ *   bf16/f16/f32 activations [rows, K]; e4m3 codes one byte each;
+ *   e2m1 weights packed two per byte [N, K/2], low nibble = even k;
+ *   ue8m0 scales one byte each; fp32 scales 4 bytes each.
+ */
+#ifndef BSGEMM_H_
+#define BSGEMM_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* dtype tags */
+typedef enum {
+  BS_DT_F32 = 0,
+  BS_DT_BF16 = 1,
+  BS_DT_F16 = 2,
+  BS_DT_E4M3 = 3,
+  BS_DT_E8M0 = 4,
+  BS_DT_E2M1X2 = 5
+} bs_dtype;
+
+/* status codes */
+enum {
+  BS_OK = 0,
+  BS_ERR_INVALID_ARG = 1,
+  BS_ERR_UNSUPPORTED = 2,
+  BS_ERR_CUDA = 3,
+  BS_ERR_DEVICE_TIMEOUT = 4,
+  BS_ERR_DEVICE_FAULT = 5
+};
+
+/* Library version (major*10000 + minor*100 + patch). */
+int bs_version(void);
+
+/* Message for the last non-zero status returned on this thread. */
+const char* bs_last_error(void);
+
+/* Reads and clears the device-side error word of the current device
+ * (synchronises the device).  Returns 0 or a BS_ERR_* code. */
+int bs_device_error_check(void);
+
+/*
+ * act_quant: block-wise e4m3 quantisation.
+ * Replaces kernel_sm121.py:55-87 act_quant(x, block_size, scale_fmt,
+ * scale_dtype, inplace=False).
+ *   x        [rows, K] in x_dtype (BS_DT_BF16 / BS_DT_F16 / BS_DT_F32)
+ *   y        [rows, K] e4m3 codes (output)
+ *   s        [rows, K/block_size] scales in s_dtype (BS_DT_F32 / BS_DT_BF16 /
+ *            BS_DT_E8M0) (output)
+ *   pow2     non-zero = scale_fmt set (scale rounded up to a power of two)
+ * block_size must be a power of two in [16, 1024] dividing K.
+ */
+int bs_act_quant(const void* x, int x_dtype, int64_t rows, int64_t K, int block_size, int pow2, void* y, void* s,
+                 int s_dtype, void* stream);
+
+/*
+ * act_quant(..., inplace=True): quantise-dequantise x in place.
+ * Replaces kernel_sm121.py:75-81.
+ */
+int bs_act_quant_inplace(void* x, int x_dtype, int64_t rows, int64_t K, int block_size, int pow2, void* stream);
+
+/*
+ * fp4_act_quant(x, block_size, inplace=True): e2m1 fake quantisation in place.
+ * Replaces kernel_sm121.py:94-121.  block_size must be a power of two in
+ * [8, 1024] dividing K.
+ */
+int bs_fp4_act_quant_inplace(void* x, int x_dtype, int64_t rows, int64_t K, int block_size, void* stream);
+
+/*
+ * fp8_gemm: C[M,N] (bf16) = A[M,K] (e4m3) x B[N,K]^T (e4m3) with per-(1x128)
+ * A scales a_s [M, K/128] and per-(128x128) B scales b_s [ceil(N/128), K/128],
+ * each BS_DT_F32 or BS_DT_E8M0 (e8m0 decoded as the reference does).
+ * Replaces kernel_sm121.py:190-255 fp8_gemm(a, a_s, b, b_s, scale_dtype).
+ * K must be a multiple of 128.
+ */
+int bs_fp8_gemm(const void* a, const void* a_s, int as_dtype, const void* b, const void* b_s, int bs_dtype,
+                int64_t M, int64_t N, int64_t K, void* c, void* stream);
+
+/*
+ * fp4_gemm: C[M,N] (bf16) = A[M,K] (e4m3) x B[N,K]^T (packed e2m1 [N,K/2])
+ * with per-(1x128) A scales a_s [M, K/128] (BS_DT_F32 or BS_DT_E8M0) and
+ * per-(1x32) B scales b_s [N, K/32] (BS_DT_E8M0).
+ * Replaces kernel_sm121.py:343-421 fp4_gemm(a, a_s, b, b_s, scale_dtype).
+ * K must be a multiple of 128.
+ */
+int bs_fp4_gemm(const void* a, const void* a_s, int as_dtype, const void* b, const void* b_s, int bs_dtype,
+                int64_t M, int64_t N, int64_t K, void* c, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BSGEMM_H_ */

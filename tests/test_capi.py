@@ -1,0 +1,86 @@
+"""The C-ABI library loads, exports every symbol include/bsgemm.h declares, and
+rejects bad arguments with a status code and message (no GPU needed: argument
+validation runs before any CUDA call)."""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT, import_pkg
+
+HEADER = os.path.join(ROOT, "include", "bsgemm.h")
+
+
+def declared_symbols():
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(bs_\w+)\s*\(", src, re.M)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    pkg = import_pkg()
+    from importlib import import_module
+    build = import_module(pkg.__name__ + ".build")
+    build.build()
+    return pkg._lib.load()
+
+
+def test_header_declares_entry_points():
+    syms = declared_symbols()
+    for s in ["bs_version", "bs_last_error", "bs_device_error_check", "bs_act_quant", "bs_act_quant_inplace",
+              "bs_fp4_act_quant_inplace", "bs_fp8_gemm", "bs_fp4_gemm"]:
+        assert s in syms
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for s in declared_symbols():
+        assert hasattr(lib, s), s
+    pkg = import_pkg()
+    assert set(pkg._lib.SIGNATURES) == set(declared_symbols())
+    assert lib.bs_version() >= 100
+
+
+def test_invalid_args_return_status(lib):
+    pkg = import_pkg()
+    L = pkg._lib
+    # bad x dtype
+    assert lib.bs_act_quant(None, 99, 4, 128, 128, 0, None, None, L.DT_F32, None) == L.BS_ERR_INVALID_ARG
+    assert b"dtype" in lib.bs_last_error()
+    # K not a multiple of block_size
+    assert lib.bs_act_quant(None, L.DT_BF16, 4, 100, 128, 0, None, None, L.DT_F32, None) == L.BS_ERR_INVALID_ARG
+    # non-power-of-two block size
+    assert lib.bs_fp4_act_quant_inplace(None, L.DT_BF16, 4, 96, 48, None) == L.BS_ERR_UNSUPPORTED
+    # GEMM: K not a multiple of 128
+    assert lib.bs_fp4_gemm(None, None, L.DT_F32, None, None, L.DT_E8M0, 16, 256, 100, None, None) == L.BS_ERR_UNSUPPORTED
+    # GEMM: fp4 weight scales must be e8m0
+    assert lib.bs_fp4_gemm(None, None, L.DT_F32, None, None, L.DT_F32, 16, 256, 128, None, None) == L.BS_ERR_UNSUPPORTED
+    # GEMM: null pointers
+    assert lib.bs_fp8_gemm(None, None, L.DT_F32, None, None, L.DT_F32, 16, 256, 128, None, None) == L.BS_ERR_INVALID_ARG
+    # empty problems are a no-op
+    assert lib.bs_fp8_gemm(None, None, L.DT_F32, None, None, L.DT_F32, 0, 256, 128, None, None) == L.BS_OK
+    assert lib.bs_act_quant(None, L.DT_BF16, 0, 128, 128, 0, None, None, L.DT_F32, None) == L.BS_OK
+
+
+def test_python_check_maps_status(lib):
+    pkg = import_pkg()
+    L = pkg._lib
+    with pytest.raises(ValueError):
+        L.check(lib.bs_act_quant(None, 99, 4, 128, 128, 0, None, None, L.DT_F32, None))
+    with pytest.raises(NotImplementedError):
+        L.check(lib.bs_fp4_gemm(None, None, L.DT_F32, None, None, L.DT_F32, 16, 256, 128, None, None))
+
+
+def test_cpu_tensors_rejected():
+    import torch
+    pkg = import_pkg()
+    x = torch.zeros(4, 128, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        pkg.act_quant(x)
+    with pytest.raises(AssertionError):
+        pkg.act_quant(torch.zeros(4, 100, dtype=torch.bfloat16))
+    with pytest.raises(NotImplementedError):
+        pkg.fp4_act_quant(torch.zeros(4, 32, dtype=torch.bfloat16), 32, False)

@@ -1,0 +1,115 @@
+"""CUDA fp8_gemm / fp4_gemm vs the reference's dequantise-then-matmul result.
+
+Tolerance (from the block-scaled path's spec): relative Frobenius error
+<= 1e-2 against the reference / oracle bf16 output; the max-abs error is
+printed.  The kernels multiply exact e4m3 x e2m1 products in fp32 and apply
+the fp32 block scales per 128-K block, while the reference rounds the
+dequantised operands to bf16 first, so ~1e-3 is the expected error.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import cases
+from conftest import max_abs, rel_fro
+from gpu_util import bits, cuda_f32, cuda_u8
+from oracle import blockscaled as ob
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+DT = {"f32": ob.DT_F32, "e8m0": ob.DT_E8M0}
+
+
+def _scale(a, dt):
+    return cuda_f32(a) if dt == "f32" else cuda_u8(a, torch.float8_e8m0fnu)
+
+
+def run_fp8(pkg, c):
+    return pkg.fp8_gemm(cuda_u8(c["a"], torch.float8_e4m3fn), _scale(c["a_s"], c["as_dt"]),
+                        cuda_u8(c["b"], torch.float8_e4m3fn), _scale(c["b_s"], c["bs_dt"]))
+
+
+def run_fp4(pkg, c):
+    return pkg.fp4_gemm(cuda_u8(c["a"], torch.float8_e4m3fn), _scale(c["a_s"], c["as_dt"]),
+                        cuda_u8(c["b"], torch.float4_e2m1fn_x2), cuda_u8(c["b_s"], torch.float8_e8m0fnu))
+
+
+def check(out, ref, label):
+    e, m = rel_fro(out, ref), max_abs(out, ref)
+    print(f"{label}: rel_fro={e:.3e} max_abs={m:.3e}")
+    assert e <= TOL, (label, e)
+    assert np.isfinite(ob.bf16_to_f32(out)).all(), label
+
+
+@pytest.mark.parametrize("name", ["small_f32", "small_e8m0", "cfg2"])
+def test_fp8_gemm_golden(pkg, golden, name):
+    c = cases.fp8_gemm_cases()[name]
+    out = bits(run_fp8(pkg, c))
+    if out.shape[0] > 1024:
+        out = out[::256]
+    check(out, golden[f"g8/{name}/out"], f"fp8 {name}")
+
+
+@pytest.mark.parametrize("name", ["cfg1", "cfg1_ue8m0", "ragged_e8m0", "decode_m1"])
+def test_fp4_gemm_golden(pkg, golden, name):
+    c = cases.fp4_gemm_cases()[name]
+    check(bits(run_fp4(pkg, c)), golden[f"g4/{name}/out"], f"fp4 {name}")
+
+
+@pytest.mark.parametrize("M", [1, 4, 16, 64])
+@pytest.mark.parametrize("N", [2048, 4096])
+def test_fp4_decode_sweep(pkg, M, N):
+    c = cases.cfg1_fp4(M=M, N=N, K=4096, seed=10 + M + N)
+    ref = ob.fp4_gemm(c["a"], c["a_s"], c["b"], c["b_s"], ob.DT_F32, ob.DT_E8M0)
+    out = run_fp4(pkg, c)
+    check(bits(out), ref, f"fp4 decode M={M} N={N}")
+    np.testing.assert_array_equal(bits(run_fp4(pkg, c)), bits(out))  # deterministic
+
+
+@pytest.mark.parametrize("shape", [(1, 256, 512), (16, 384, 1024), (64, 1024, 4096), (33, 200, 384)])
+def test_fp8_decode_vs_oracle(pkg, shape):
+    M, N, K = shape
+    rng = np.random.default_rng(M * 7 + N)
+    x = ob.f32_to_bf16(rng.standard_normal((M, K)).astype(np.float32))
+    a, a_s = ob.act_quant(x, ob.DT_BF16, 128, None, ob.DT_F32)
+    b, b_s = cases.quant_weight_128x128((rng.standard_normal((N, K)) * 0.02).astype(np.float32))
+    c = dict(a=a, a_s=a_s, b=b, b_s=b_s, as_dt="f32", bs_dt="f32")
+    check(bits(run_fp8(pkg, c)), ob.fp8_gemm(a, a_s, b, b_s), f"fp8 M={M} N={N} K={K}")
+
+
+@pytest.mark.parametrize("shape", [(256, 512, 1024), (130, 200, 384), (512, 768, 2048)])
+def test_fp8_prefill_vs_oracle(pkg, shape):
+    M, N, K = shape
+    rng = np.random.default_rng(M + N + K)
+    x = ob.f32_to_bf16(rng.standard_normal((M, K)).astype(np.float32))
+    a, a_s = ob.act_quant(x, ob.DT_BF16, 128, None, ob.DT_F32)
+    b, b_s = cases.quant_weight_128x128((rng.standard_normal((N, K)) * 0.02).astype(np.float32))
+    c = dict(a=a, a_s=a_s, b=b, b_s=b_s, as_dt="f32", bs_dt="f32")
+    check(bits(run_fp8(pkg, c)), ob.fp8_gemm(a, a_s, b, b_s), f"fp8 M={M} N={N} K={K}")
+
+
+@pytest.mark.parametrize("shape", [(256, 512, 1024), (130, 200, 384), (300, 1024, 4096)])
+@pytest.mark.parametrize("fmt", [None, "ue8m0"])
+def test_fp4_prefill_vs_oracle(pkg, shape, fmt):
+    M, N, K = shape
+    c = cases.cfg1_fp4(M=M, N=N, K=K, scale_fmt=fmt, seed=M + N)
+    ref = ob.fp4_gemm(c["a"], c["a_s"], c["b"], c["b_s"], ob.DT_F32, ob.DT_E8M0)
+    check(bits(run_fp4(pkg, c)), ref, f"fp4 M={M} N={N} K={K} fmt={fmt}")
+
+
+def test_gemm_leading_dims(pkg):
+    c = cases.cfg1_fp4(M=12, N=256, K=512, seed=3)
+    a = cuda_u8(c["a"], torch.float8_e4m3fn).view(3, 4, 512)
+    a_s = cuda_f32(c["a_s"]).view(3, 4, 4)
+    out = pkg.fp4_gemm(a, a_s, cuda_u8(c["b"], torch.float4_e2m1fn_x2), cuda_u8(c["b_s"], torch.float8_e8m0fnu))
+    assert out.shape == (3, 4, 256)
+    ref = ob.fp4_gemm(c["a"], c["a_s"], c["b"], c["b_s"], ob.DT_F32, ob.DT_E8M0)
+    check(bits(out).reshape(12, 256), ref, "fp4 leading dims")
+
+
+def test_no_device_error(pkg):
+    pkg._lib.device_error_check()

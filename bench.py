@@ -297,6 +297,47 @@ def bench_fp4_decode(args, torch, dist, ws, rank, dev):
             "gpu_launches": steps, "clocks": clk}
 
 
+def bench_moe_1gpu(args, torch, dist, ws, rank, dev):
+    """Config-4 MoE layer on one GPU: T=1024, H=4096, I=2048, E=256, top-8."""
+    pkg = __import__("importlib").import_module(PKG)
+    moe = __import__("importlib").import_module(PKG + ".moe")
+    T, H, I, E, k = args.tokens, 4096, 2048, 256, 8
+    g = torch.Generator(device=dev)
+    g.manual_seed(4)
+    x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    logits = torch.randn(T, E, generator=g, device=dev)
+    w13 = torch.randint(0, 256, (E, 2 * I, H // 2), generator=g, device=dev, dtype=torch.uint8)
+    w13_s = 127 - torch.randint(0, 7, (E, 2 * I, H // 32), generator=g, device=dev, dtype=torch.uint8)
+    w2 = torch.randint(0, 256, (E, H, I // 2), generator=g, device=dev, dtype=torch.uint8)
+    w2_s = 127 - torch.randint(0, 7, (E, H, I // 32), generator=g, device=dev, dtype=torch.uint8)
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    for _ in range(args.warmup):
+        moe.moe_forward(x, logits, w13, w13_s, w2, w2_s, k, out=out)
+    torch.cuda.synchronize()
+    clocks = Clocks(torch.cuda.current_device())
+    clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        moe.moe_forward(x, logits, w13, w13_s, w2, w2_s, k, out=out)
+    t1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    wbytes = w13.numel() + w13_s.numel() + w2.numel() + w2_s.numel()
+    peaks, src = load_peaks()
+    gbs = wbytes / (ms * 1e-3) / 1e9
+    return {"metric": "MoE-layer tokens/s", "value": round(T / (ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "e4m3 x e2m1", "data": "synthetic",
+            "config": {"workload": f"MoE layer T={T} H={H} I={I} E={E} top-{k}", "parallelism": "none",
+                       "l2": f"weights {wbytes / 2**30:.2f} GiB >> L2"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(gbs / peaks["hbm_gbs"], 3), "traffic": None,
+                         "note": "expert weight bytes per layer / layer time", "peak_source": src},
+            "gpu_launches": args.steps * 8, "clocks": clk}
+
+
 def max_over_ranks(torch, dist, v):
     if dist is None:
         return v
@@ -335,7 +376,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["fp8_prefill", "fp4_decode"], default="fp8_prefill")
+    ap.add_argument("--workload", choices=["fp8_prefill", "fp4_decode", "moe"], default="fp8_prefill")
+    ap.add_argument("--tokens", type=int, default=1024)
     ap.add_argument("--m", type=int, default=16)
     ap.add_argument("--n", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -378,6 +420,8 @@ def main():
 
     if args.workload == "fp8_prefill":
         line = bench_fp8_prefill(args, torch, dist, ws, rank, dev)
+    elif args.workload == "moe":
+        line = bench_moe_1gpu(args, torch, dist, ws, rank, dev)
     else:
         line = bench_fp4_decode(args, torch, dist, ws, rank, dev)
 

@@ -30,8 +30,20 @@ SIGNATURES = {
     "bs_fp4_act_quant_inplace": [_c_void_p, _i32, _i64, _i64, _i32, _c_void_p],
     "bs_fp8_gemm": [_c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p, _i32, _i64, _i64, _i64, _c_void_p, _c_void_p],
     "bs_fp4_gemm": [_c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p, _i32, _i64, _i64, _i64, _c_void_p, _c_void_p],
+    "bs_moe_workspace_size": [_i64, _i32, _i32, _i32, _i32],
+    "bs_moe_forward": [_c_void_p, _c_void_p, _i64, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p,
+                       _c_void_p, _c_void_p, _c_void_p, ctypes.c_size_t, _c_void_p],
+    "bs_moe_route": [_c_void_p, _i64, _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p],
+    "bs_moe_scan": [_c_void_p, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p],
+    "bs_moe_dispatch": [_c_void_p, _i64, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _c_void_p,
+                        _c_void_p, _c_void_p, _c_void_p],
+    "bs_moe_regroup": [_c_void_p, _i32, _i32, _i64, _c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p, _c_void_p,
+                       _c_void_p, _c_void_p, _c_void_p, _c_void_p],
+    "bs_moe_experts": [_i32, _i64, _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+                       _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p],
+    "bs_moe_combine": [_c_void_p, _c_void_p, _c_void_p, _i64, _i32, _i32, _c_void_p, _c_void_p],
 }
-RESTYPES = {"bs_last_error": ctypes.c_char_p}
+RESTYPES = {"bs_last_error": ctypes.c_char_p, "bs_moe_workspace_size": ctypes.c_size_t}
 
 
 class BsError(RuntimeError):

@@ -10,6 +10,22 @@ cudaError_t bs_launch_act_quant(const void* x, int x_dtype, int64_t rows, int64_
 cudaError_t bs_launch_fp4_act_quant(void* x, int x_dtype, int64_t rows, int64_t K, int bs, cudaStream_t st);
 int bs_launch_gemm(bool fp4, const void* a, const void* a_s, int as_dtype, const void* b, const void* b_s,
                    int bs_dtype, int64_t M, int64_t N, int64_t K, void* c, cudaStream_t st, cudaError_t* cerr);
+cudaError_t bs_launch_moe_route(const float* logits, int T, int E, int topk, int* idx, float* w, int* counts,
+                                cudaStream_t st);
+cudaError_t bs_launch_moe_scan(const int* counts, int E, int* offsets, int* chunk_prefix, int* cursor,
+                               cudaStream_t st);
+cudaError_t bs_launch_moe_dispatch(const int* idx, int T, int topk, const int* offsets, int* cursor,
+                                   const uint8_t* xq, const uint8_t* xs, int H, uint8_t* ap, uint32_t* aps32,
+                                   int* pos_of, int* row_token, cudaStream_t st);
+cudaError_t bs_launch_moe_combine(const __nv_bfloat16* y, const int* pos_of, const float* w, int T, int topk, int H,
+                                  __nv_bfloat16* out, cudaStream_t st);
+int bs_launch_moe_experts(int E, int64_t rows, int H, int I, const uint8_t* ap, const uint32_t* aps32,
+                          const int* offsets, const int* chunk_prefix, const void* w13, const uint8_t* w13_s,
+                          const void* w2, const uint8_t* w2_s, const int* y_rowmap, uint8_t* hq, uint32_t* hs32,
+                          __nv_bfloat16* y, cudaStream_t st, cudaError_t* cerr);
+cudaError_t bs_launch_moe_regroup(const int* cnt, int S, int E, int64_t capacity, const uint8_t* rows_in,
+                                  const uint32_t* sc_in, int H, uint8_t* rows_out, uint32_t* sc_out, int* rowmap,
+                                  int* offsets, int* chunk_prefix, int* scratch, cudaStream_t st);
 
 namespace {
 
@@ -133,6 +149,161 @@ int bs_fp8_gemm(const void* a, const void* a_s, int as_dtype, const void* b, con
 int bs_fp4_gemm(const void* a, const void* a_s, int as_dtype, const void* b, const void* b_s, int bs_dtype,
                 int64_t M, int64_t N, int64_t K, void* c, void* stream) {
   return gemm_common(true, a, a_s, as_dtype, b, b_s, bs_dtype, M, N, K, c, stream);
+}
+
+// ---------------------------------------------------------------------------
+// MoE layer
+// ---------------------------------------------------------------------------
+
+static int check_moe_dims(int64_t T, int H, int I, int E, int topk) {
+  if (T < 0 || T > (1 << 24)) return fail(BS_ERR_INVALID_ARG, "moe: token count %lld out of range", (long long)T);
+  if (H <= 0 || H % 128 || I <= 0 || I % 128)
+    return fail(BS_ERR_UNSUPPORTED, "moe: hidden (%d) and inter (%d) must be positive multiples of 128", H, I);
+  if (E <= 0 || E > 1024) return fail(BS_ERR_UNSUPPORTED, "moe: %d experts (1..1024 supported)", E);
+  if (topk <= 0 || topk > 8 || topk > E) return fail(BS_ERR_UNSUPPORTED, "moe: top-k %d (1..8, <= experts)", topk);
+  return BS_OK;
+}
+
+namespace {
+struct MoeLayout {
+  size_t counts, cursor, offsets, chunks, idx, w, pos, xq, xs, ap, aps, hq, hs, y, total;
+};
+size_t up256(size_t v) { return (v + 255) & ~size_t(255); }
+MoeLayout moe_layout(int64_t T, int H, int I, int E, int topk) {
+  MoeLayout L;
+  const size_t R = (size_t)T * topk;
+  size_t o = 0;
+  auto take = [&](size_t bytes) { size_t at = o; o += up256(bytes); return at; };
+  L.counts = take(4 * (size_t)E);
+  L.cursor = take(4 * (size_t)E);
+  L.offsets = take(4 * (size_t)(E + 1));
+  L.chunks = take(4 * (size_t)(E + 1));
+  L.idx = take(4 * R);
+  L.w = take(4 * R);
+  L.pos = take(4 * R);
+  L.xq = take((size_t)T * H);
+  L.xs = take((size_t)T * (H / 128));
+  L.ap = take(R * H);
+  L.aps = take(R * (H / 128) * 4);
+  L.hq = take(R * I);
+  L.hs = take(R * (I / 128) * 4);
+  L.y = take(R * H * 2);
+  L.total = o;
+  return L;
+}
+}  // namespace
+
+size_t bs_moe_workspace_size(int64_t T, int H, int I, int E, int topk) {
+  if (check_moe_dims(T, H, I, E, topk)) return 0;
+  return moe_layout(T, H, I, E, topk).total;
+}
+
+int bs_moe_forward(const void* x, const float* logits, int64_t T, int H, int I, int E, int topk, const void* w13,
+                   const void* w13_s, const void* w2, const void* w2_s, void* out, void* workspace,
+                   size_t workspace_bytes, void* stream) {
+  int st = check_moe_dims(T, H, I, E, topk);
+  if (st) return st;
+  if (T == 0) return BS_OK;
+  if (!x || !logits || !w13 || !w13_s || !w2 || !w2_s || !out || !workspace)
+    return fail(BS_ERR_INVALID_ARG, "moe: null pointer");
+  if (!aligned(x, 16) || !aligned(out, 16) || !aligned(w13, 32) || !aligned(w2, 32) || !aligned(workspace, 256) ||
+      !aligned(w13_s, 4) || !aligned(w2_s, 4))
+    return fail(BS_ERR_INVALID_ARG, "moe: alignment (x,out 16 B; weights 32 B; scales 4 B; workspace 256 B)");
+  const MoeLayout L = moe_layout(T, H, I, E, topk);
+  if (workspace_bytes < L.total)
+    return fail(BS_ERR_INVALID_ARG, "moe: workspace of %zu bytes, %zu needed", workspace_bytes, L.total);
+  cudaStream_t s = (cudaStream_t)stream;
+  uint8_t* ws = (uint8_t*)workspace;
+  int* counts = (int*)(ws + L.counts);
+  int* cursor = (int*)(ws + L.cursor);
+  int* offsets = (int*)(ws + L.offsets);
+  int* chunks = (int*)(ws + L.chunks);
+  int* idx = (int*)(ws + L.idx);
+  float* w = (float*)(ws + L.w);
+  int* pos = (int*)(ws + L.pos);
+  cudaError_t e = bs_launch_act_quant(x, BS_DT_BF16, T, H, 128, 1, ws + L.xq, ws + L.xs, BS_DT_E8M0, false, s);
+  if (e == cudaSuccess) e = bs_launch_moe_route(logits, (int)T, E, topk, idx, w, counts, s);
+  if (e == cudaSuccess) e = bs_launch_moe_scan(counts, E, offsets, chunks, cursor, s);
+  if (e == cudaSuccess)
+    e = bs_launch_moe_dispatch(idx, (int)T, topk, offsets, cursor, ws + L.xq, ws + L.xs, H, ws + L.ap,
+                               (uint32_t*)(ws + L.aps), pos, nullptr, s);
+  if (e != cudaSuccess) return cuda_status(e, "moe front end");
+  int r = bs_launch_moe_experts(E, T * topk, H, I, ws + L.ap, (const uint32_t*)(ws + L.aps), offsets, chunks, w13,
+                                (const uint8_t*)w13_s, w2, (const uint8_t*)w2_s, nullptr, ws + L.hq,
+                                (uint32_t*)(ws + L.hs), (__nv_bfloat16*)(ws + L.y), s, &e);
+  if (r == BS_ERR_UNSUPPORTED) return fail(r, "moe: could not build TMA descriptors");
+  if (r) return cuda_status(e, "moe grouped GEMM");
+  e = bs_launch_moe_combine((const __nv_bfloat16*)(ws + L.y), pos, w, (int)T, topk, H, (__nv_bfloat16*)out, s);
+  return cuda_status(e, "moe combine");
+}
+
+int bs_moe_route(const float* logits, int64_t T, int E, int topk, int* idx, float* w, int* counts, void* stream) {
+  if (T < 0 || E <= 0 || E > 1024 || topk <= 0 || topk > 8 || topk > E)
+    return fail(BS_ERR_UNSUPPORTED, "moe_route: T=%lld E=%d topk=%d", (long long)T, E, topk);
+  if (!counts || (T > 0 && (!logits || !idx || !w))) return fail(BS_ERR_INVALID_ARG, "moe_route: null pointer");
+  return cuda_status(bs_launch_moe_route(logits, (int)T, E, topk, idx, w, counts, (cudaStream_t)stream), "moe_route");
+}
+
+int bs_moe_scan(const int* counts, int E, int* offsets, int* chunk_prefix, int* cursor, void* stream) {
+  if (E <= 0 || E > 1024) return fail(BS_ERR_UNSUPPORTED, "moe_scan: %d experts", E);
+  if (!counts || !offsets || !chunk_prefix || !cursor) return fail(BS_ERR_INVALID_ARG, "moe_scan: null pointer");
+  return cuda_status(bs_launch_moe_scan(counts, E, offsets, chunk_prefix, cursor, (cudaStream_t)stream), "moe_scan");
+}
+
+int bs_moe_dispatch(const int* idx, int64_t T, int topk, const int* offsets, int* cursor, const void* xq,
+                    const void* xs, int H, void* rows, void* row_scales, int* pos_of, void* stream) {
+  if (T < 0 || topk <= 0 || topk > 8 || H <= 0 || H % 128) return fail(BS_ERR_UNSUPPORTED, "moe_dispatch: bad sizes");
+  if (T > 0 && (!idx || !offsets || !cursor || !xq || !xs || !rows || !row_scales || !pos_of))
+    return fail(BS_ERR_INVALID_ARG, "moe_dispatch: null pointer");
+  if (T > 0 && (!aligned(xq, 16) || !aligned(rows, 16) || !aligned(row_scales, 4)))
+    return fail(BS_ERR_INVALID_ARG, "moe_dispatch: alignment");
+  return cuda_status(bs_launch_moe_dispatch(idx, (int)T, topk, offsets, cursor, (const uint8_t*)xq,
+                                            (const uint8_t*)xs, H, (uint8_t*)rows, (uint32_t*)row_scales, pos_of,
+                                            nullptr, (cudaStream_t)stream),
+                     "moe_dispatch");
+}
+
+int bs_moe_regroup(const int* recv_counts, int n_src, int E, int64_t capacity, const void* rows_in,
+                   const void* scales_in, int H, void* rows_out, void* scales_out, int* rowmap, int* offsets,
+                   int* chunk_prefix, int* scratch, void* stream) {
+  if (n_src <= 0 || E <= 0 || n_src * E > 1024 || H <= 0 || H % 128 || capacity < 0)
+    return fail(BS_ERR_UNSUPPORTED, "moe_regroup: bad sizes");
+  if (!recv_counts || !offsets || !chunk_prefix || !scratch ||
+      (capacity > 0 && (!rows_in || !scales_in || !rows_out || !scales_out || !rowmap)))
+    return fail(BS_ERR_INVALID_ARG, "moe_regroup: null pointer");
+  return cuda_status(bs_launch_moe_regroup(recv_counts, n_src, E, capacity, (const uint8_t*)rows_in,
+                                           (const uint32_t*)scales_in, H, (uint8_t*)rows_out, (uint32_t*)scales_out,
+                                           rowmap, offsets, chunk_prefix, scratch, (cudaStream_t)stream),
+                     "moe_regroup");
+}
+
+int bs_moe_experts(int E, int64_t capacity, int H, int I, const void* rows, const void* row_scales,
+                   const int* offsets, const int* chunk_prefix, const void* w13, const void* w13_s, const void* w2,
+                   const void* w2_s, const int* y_rowmap, void* hq, void* hs, void* y, void* stream) {
+  int st = check_moe_dims(capacity, H, I, E, 1);
+  if (st) return st;
+  if (capacity == 0) return BS_OK;
+  if (!rows || !row_scales || !offsets || !chunk_prefix || !w13 || !w13_s || !w2 || !w2_s || !hq || !hs || !y)
+    return fail(BS_ERR_INVALID_ARG, "moe_experts: null pointer");
+  if (!aligned(rows, 16) || !aligned(hq, 16) || !aligned(y, 16) || !aligned(w13, 32) || !aligned(w2, 32))
+    return fail(BS_ERR_INVALID_ARG, "moe_experts: alignment");
+  cudaError_t e;
+  int r = bs_launch_moe_experts(E, capacity, H, I, (const uint8_t*)rows, (const uint32_t*)row_scales, offsets,
+                                chunk_prefix, w13, (const uint8_t*)w13_s, w2, (const uint8_t*)w2_s, y_rowmap,
+                                (uint8_t*)hq, (uint32_t*)hs, (__nv_bfloat16*)y, (cudaStream_t)stream, &e);
+  if (r == BS_ERR_UNSUPPORTED) return fail(r, "moe_experts: could not build TMA descriptors");
+  if (r) return cuda_status(e, "moe_experts");
+  return BS_OK;
+}
+
+int bs_moe_combine(const void* y, const int* pos_of, const float* w, int64_t T, int topk, int H, void* out,
+                   void* stream) {
+  if (T < 0 || topk <= 0 || topk > 8 || H <= 0 || H % 8) return fail(BS_ERR_UNSUPPORTED, "moe_combine: bad sizes");
+  if (T > 0 && (!y || !pos_of || !w || !out)) return fail(BS_ERR_INVALID_ARG, "moe_combine: null pointer");
+  if (T > 0 && (!aligned(y, 16) || !aligned(out, 16))) return fail(BS_ERR_INVALID_ARG, "moe_combine: alignment");
+  return cuda_status(bs_launch_moe_combine((const __nv_bfloat16*)y, pos_of, w, (int)T, topk, H, (__nv_bfloat16*)out,
+                                           (cudaStream_t)stream),
+                     "moe_combine");
 }
 
 }  // extern "C"

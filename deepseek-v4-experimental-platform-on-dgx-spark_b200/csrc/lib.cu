@@ -3,4 +3,5 @@
 #include "common.cuh"
 #include "quant.cu"
 #include "gemm.cu"
+#include "moe.cu"
 #include "capi.cu"

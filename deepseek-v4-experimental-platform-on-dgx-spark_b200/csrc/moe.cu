@@ -1,0 +1,675 @@
+// Grouped per-expert MoE form of the block-scaled path.
+//
+// Replaces the reference's per-expert Python loop (one act_quant and three
+// fp4_gemm launches per active expert; its caller lives in the external
+// DeepSeek model file) with a fixed sequence of kernels and no host sync:
+//
+//   route     top-k over gate logits + softmax weights, expert histogram
+//   scan      histogram -> row offsets and 128-token chunk prefix per expert
+//   dispatch  expert-sorted copy of the e4m3 token rows and their ue8m0
+//             scales (the layout the grouped GEMM and the EP exchange read)
+//   gemm13    persistent grouped GEMM: W1|W3 (e2m1, ue8m0 1x32) x tokens
+//             (e4m3, ue8m0 1x128), fused SwiGLU + e4m3 act_quant epilogue
+//   gemm2     persistent grouped GEMM: W2 x quantised hidden -> bf16 rows
+//   combine   out[t] = sum_k w[t,k] * y[row(t,k)]   (fp32, deterministic)
+//
+// GEMM orientation: the expert's weight rows are the 128-row MMA operand and
+// the expert's tokens the MMA N dimension (16..128, set per work item in the
+// runtime instruction descriptor), so a handful of tokens per expert still
+// streams each weight tile exactly once per 128-token chunk.  Both operands
+// carry ue8m0 block scales in TMEM (kind::mxf8f6f4.block_scale), so the
+// accumulator stays in TMEM for the whole K loop.
+#include "common.cuh"
+
+namespace moe {
+
+constexpr int kTok = 128;  // tokens per work item (MMA N <= 128)
+
+// ---------------------------------------------------------------------------
+// routing
+// ---------------------------------------------------------------------------
+
+// One warp per token.  Ties keep the lower expert index (a stable sort of
+// -logits).  Weights: softmax over the k selected logits.
+__global__ void route_kernel(const float* __restrict__ logits, int T, int E, int topk, int* __restrict__ idx,
+                             float* __restrict__ w, int* __restrict__ counts) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  const float* row = logits + (int64_t)warp * E;
+  constexpr int kMaxPer = 32;  // E <= 1024
+  float v[kMaxPer];
+  const int per = (E + 31) / 32;
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    const int e = i * 32 + lane;
+    v[i] = (i < per && e < E) ? row[e] : -INFINITY;
+    if (v[i] != v[i]) v[i] = -INFINITY;
+  }
+  float sel_v[8];
+  int sel_e[8];
+  for (int k = 0; k < topk; ++k) {
+    float bv = -INFINITY;
+    int be = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) {
+      const int e = i * 32 + lane;
+      if (i < per && e < E && (v[i] > bv || (v[i] == bv && e < be))) { bv = v[i]; be = e; }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+      if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; }
+    }
+    sel_v[k] = bv;
+    sel_e[k] = be;
+    if ((be & 31) == lane) {
+#pragma unroll
+      for (int i = 0; i < kMaxPer; ++i)
+        if (i == (be >> 5)) v[i] = -INFINITY;
+    }
+  }
+  if (lane == 0) {
+    const float m = sel_v[0];
+    float den = 0.f;
+    for (int k = 0; k < topk; ++k) den += expf(sel_v[k] - m);
+    for (int k = 0; k < topk; ++k) {
+      idx[(int64_t)warp * topk + k] = sel_e[k];
+      w[(int64_t)warp * topk + k] = expf(sel_v[k] - m) / den;
+      atomicAdd(&counts[sel_e[k]], 1);
+    }
+  }
+}
+
+// Histogram of externally supplied expert ids (idx [n]) into counts[E].
+__global__ void histogram_kernel(const int* __restrict__ idx, int64_t n, int E, int* __restrict__ counts,
+                                 int* __restrict__ bad) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int e = idx[i];
+    if (e >= 0 && e < E) atomicAdd(&counts[e], 1);
+    else atomicExch(bad, 1);
+  }
+}
+
+// Single block of 1024 threads: exclusive scans of counts (row offsets) and
+// of 128-token chunks per expert (E <= 1024); zeroes the dispatch cursors.
+__global__ void __launch_bounds__(1024) scan_kernel(const int* __restrict__ counts, int E, int* __restrict__ offsets,
+                                                    int* __restrict__ chunk_prefix, int* __restrict__ cursor) {
+  __shared__ int w_rows[32], w_chunks[32];
+  const int e = threadIdx.x, lane = e & 31, wid = e >> 5;
+  const int c = e < E ? counts[e] : 0;
+  const int ch = (c + kTok - 1) / kTok;
+  int r_inc = c, c_inc = ch;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int rv = __shfl_up_sync(0xffffffffu, r_inc, o);
+    const int cv = __shfl_up_sync(0xffffffffu, c_inc, o);
+    if (lane >= o) { r_inc += rv; c_inc += cv; }
+  }
+  if (lane == 31) { w_rows[wid] = r_inc; w_chunks[wid] = c_inc; }
+  __syncthreads();
+  if (wid == 0) {
+    int rv = w_rows[lane], cv = w_chunks[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int a = __shfl_up_sync(0xffffffffu, rv, o);
+      const int b = __shfl_up_sync(0xffffffffu, cv, o);
+      if (lane >= o) { rv += a; cv += b; }
+    }
+    w_rows[lane] = rv;
+    w_chunks[lane] = cv;
+  }
+  __syncthreads();
+  const int r_base = wid > 0 ? w_rows[wid - 1] : 0;
+  const int c_base = wid > 0 ? w_chunks[wid - 1] : 0;
+  if (e < E) {
+    offsets[e] = r_base + r_inc - c;
+    chunk_prefix[e] = c_base + c_inc - ch;
+    cursor[e] = 0;
+  }
+  if (e == E - 1) {
+    offsets[E] = r_base + r_inc;
+    chunk_prefix[E] = c_base + c_inc;
+  }
+}
+
+// One warp per (token, slot): claim a row in the expert's segment and copy
+// the e4m3 row (H bytes) and its scales, replicated four times per word (one
+// copy per 32-K sub-block, the layout the MMA scale loads expect).
+__global__ void dispatch_kernel(const int* __restrict__ idx, int T, int topk, const int* __restrict__ offsets,
+                                int* __restrict__ cursor, const uint8_t* __restrict__ xq,
+                                const uint8_t* __restrict__ xs, int H, uint8_t* __restrict__ ap,
+                                uint32_t* __restrict__ aps32, int* __restrict__ pos_of, int* __restrict__ row_token) {
+  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= (int64_t)T * topk) return;
+  const int t = (int)(warp / topk);
+  const int e = idx[warp];
+  int pos = 0;
+  if (lane == 0) pos = offsets[e] + atomicAdd(&cursor[e], 1);
+  pos = __shfl_sync(0xffffffffu, pos, 0);
+  if (lane == 0) {
+    pos_of[warp] = pos;
+    if (row_token) row_token[pos] = t;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(xq + (int64_t)t * H);
+  uint4* dst = reinterpret_cast<uint4*>(ap + (int64_t)pos * H);
+  for (int i = lane; i < H / 16; i += 32) dst[i] = src[i];
+  const int nb = H / 128;
+  for (int i = lane; i < nb; i += 32) aps32[(int64_t)pos * nb + i] = 0x01010101u * xs[(int64_t)t * nb + i];
+}
+
+// out[t] = bf16( sum_k w[t,k] * y[pos_of[t,k]] ), fp32 accumulation in slot
+// order.  One block per token, 8 bf16 per thread.
+__global__ void combine_kernel(const __nv_bfloat16* __restrict__ y, const int* __restrict__ pos_of,
+                               const float* __restrict__ w, int topk, int H, __nv_bfloat16* __restrict__ out) {
+  const int t = blockIdx.x;
+  for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int k = 0; k < topk; ++k) {
+      const int p = pos_of[(int64_t)t * topk + k];
+      const float wk = w[(int64_t)t * topk + k];
+      const uint4 raw = *reinterpret_cast<const uint4*>(y + (int64_t)p * H + c);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(h[j]);
+        acc[2 * j] = fmaf(wk, f.x, acc[2 * j]);
+        acc[2 * j + 1] = fmaf(wk, f.y, acc[2 * j + 1]);
+      }
+    }
+    uint4 o;
+    __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) oh[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
+    *reinterpret_cast<uint4*>(out + (int64_t)t * H + c) = o;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// expert-parallel receive side: rows arrive grouped by source rank, then by
+// expert; the grouped GEMM wants them grouped by expert.
+// ---------------------------------------------------------------------------
+
+// Single block.  cnt[s*E + e] = rows from source s for local expert e.
+// src_off: exclusive prefix in (s, e) order (arrival position);
+// dst_off: exclusive prefix in (e, s) order (expert-major position), stored
+// transposed as dst_off[s*E + e]; plus the expert offsets / chunk prefix.
+__global__ void __launch_bounds__(1024) regroup_plan_kernel(const int* __restrict__ cnt, int S, int E,
+                                                            int* __restrict__ src_off, int* __restrict__ dst_off,
+                                                            int* __restrict__ offsets, int* __restrict__ chunk_prefix) {
+  __shared__ int sh[1025];
+  const int n = S * E;
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int i = 0; i < n; ++i) { sh[i] = acc; acc += cnt[i]; }
+    sh[n] = acc;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i <= n; i += blockDim.x) src_off[i] = sh[i];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0, chunks = 0;
+    for (int e = 0; e < E; ++e) {
+      offsets[e] = acc;
+      chunk_prefix[e] = chunks;
+      int tot = 0;
+      for (int s2 = 0; s2 < S; ++s2) {
+        sh[s2 * E + e] = acc;
+        acc += cnt[s2 * E + e];
+        tot += cnt[s2 * E + e];
+      }
+      chunks += (tot + kTok - 1) / kTok;
+    }
+    offsets[E] = acc;
+    chunk_prefix[E] = chunks;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) dst_off[i] = sh[i];
+}
+
+// One warp per arrived row j: find its (source, expert) group, move the row
+// and its scales to the expert-major position, record rowmap[dst] = j.
+__global__ void regroup_rows_kernel(const int* __restrict__ src_off, const int* __restrict__ dst_off, int n_groups,
+                                    int64_t capacity, const uint8_t* __restrict__ rows_in,
+                                    const uint32_t* __restrict__ sc_in, int H, uint8_t* __restrict__ rows_out,
+                                    uint32_t* __restrict__ sc_out, int* __restrict__ rowmap) {
+  const int64_t j = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (j >= capacity || j >= src_off[n_groups]) return;
+  int lo = 0, hi = n_groups;  // largest g with src_off[g] <= j
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (src_off[mid] <= j) lo = mid; else hi = mid;
+  }
+  const int64_t dst = dst_off[lo] + (j - src_off[lo]);
+  const uint4* src = reinterpret_cast<const uint4*>(rows_in + j * H);
+  uint4* d = reinterpret_cast<uint4*>(rows_out + dst * H);
+  for (int i = lane; i < H / 16; i += 32) d[i] = src[i];
+  const int nb = H / 128;
+  for (int i = lane; i < nb; i += 32) sc_out[dst * nb + i] = sc_in[j * nb + i];
+  if (lane == 0) rowmap[dst] = (int)j;
+}
+
+// ---------------------------------------------------------------------------
+// persistent grouped GEMM
+// ---------------------------------------------------------------------------
+
+struct GemmArgs {
+  int E;                     // experts in this launch
+  int K;                     // reduction size (hidden for W13, inter for W2)
+  int n_tiles;               // 128-row output tiles per expert
+  int w_rows;                // rows per expert in the weight tensor
+  int up_off;                // W13: row offset of W3 inside W13
+  const int* offsets;        // [E+1] token-row offsets
+  const int* chunk_prefix;   // [E+1] prefix of 128-token chunks
+  const uint8_t* w_s;        // [E, w_rows, K/32] ue8m0
+  const uint32_t* a_s32;     // [rows, K/128] ue8m0 x4
+  uint8_t* hq;               // W13: [rows, I] e4m3
+  uint32_t* hs32;            // W13: [rows, I/128] ue8m0 x4
+  int I;
+  __nv_bfloat16* y;          // W2: [rows, H] bf16
+  int H;
+  const int* y_rowmap;       // W2: optional output row map (EP: expert-major -> arrival order)
+};
+
+template <bool PAIRED>
+struct Cfg {
+  static constexpr int kXTiles = PAIRED ? 2 : 1;
+  static constexpr int kXBytes = kXTiles * 128 * 128;   // unpacked e2m1 in smem
+  static constexpr int kYBytes = kTok * 128;
+  static constexpr int kStageBytes = kXBytes + kYBytes;
+  static constexpr int kStages = PAIRED ? 4 : 6;
+  static constexpr int kSfBytes = 512 * (kXTiles + 1);
+  static constexpr int kAccBufs = PAIRED ? 1 : 2;
+  static constexpr int kAccCols = kXTiles * kTok;        // per accumulator buffer
+  static constexpr int kSfSlot = 4 * (kXTiles + 1);
+  static constexpr int kSfCol0 = kAccBufs * kAccCols;
+  static_assert(kSfCol0 + 2 * kSfSlot <= 512, "TMEM budget");
+  static constexpr int kTmemCols = 512;
+  static constexpr int kThreads = 192;
+  static constexpr int kMaxE = 1024;
+  static constexpr int kSmemBytes = 1024 + kStages * (kStageBytes + kSfBytes) + 2 * (kMaxE + 1) * 4 + 4 * 16 * 4 + 256;
+};
+
+BS_DEVINL void named_bar_epi() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+BS_DEVINL float silu(float g) { return g / (1.0f + expf(-g)); }
+BS_DEVINL float bf16_round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+template <bool PAIRED>
+__global__ void __launch_bounds__(192, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a, GemmArgs p) {
+  using C = Cfg<PAIRED>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stage_base = smem;
+  uint8_t* sf_base = smem + C::kStages * C::kStageBytes;
+  int* s_off = reinterpret_cast<int*>(sf_base + C::kStages * C::kSfBytes);
+  int* s_chunk = s_off + C::kMaxE + 1;
+  uint32_t* s_red = reinterpret_cast<uint32_t*>(s_chunk + C::kMaxE + 1);   // [4 warps][16 tokens]
+  uint64_t* full = reinterpret_cast<uint64_t*>(s_red + 64);
+  uint64_t* empty = full + C::kStages;
+  uint64_t* acc_full = empty + C::kStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int E = p.E;
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) {
+    s_off[i] = p.offsets[i];
+    s_chunk[i] = p.chunk_prefix[i];
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1 + 32);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_w);
+    tma_prefetch_desc(&tm_a);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int n_items = s_chunk[E] * p.n_tiles;
+  const int nkb = p.K / 128;
+
+  // work item -> (expert, first token row, token count, output tile)
+  auto decode = [&](int item, int& e, int& row0, int& cnt, int& nt) {
+    const int cg = item / p.n_tiles;
+    nt = item - cg * p.n_tiles;
+    int lo = 0, hi = E;  // largest e with s_chunk[e] <= cg
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (s_chunk[mid] <= cg) lo = mid; else hi = mid;
+    }
+    e = lo;
+    const int chunk = cg - s_chunk[e];
+    row0 = s_off[e] + chunk * kTok;
+    const int left = s_off[e + 1] - row0;
+    cnt = left < kTok ? left : kTok;
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    int it = 0;
+    bool ok = true;
+    const int64_t w_ld = p.K / 32;
+    const int a_ld = p.K / 128;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+      int e, row0, cnt, nt;
+      decode(item, e, row0, cnt, nt);
+      const int nbox = (cnt + 15) / 16;
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const int s = it % C::kStages;
+        const uint32_t ph = (it / C::kStages) & 1;
+        if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1, abort_flag))) { ok = false; break; }
+        uint8_t* sf = sf_base + s * C::kSfBytes;
+        for (int t = 0; t < C::kXTiles; ++t) {
+          const int wr0 = (t == 0 ? 0 : p.up_off) + nt * 128;
+          const uint8_t* src = p.w_s + ((int64_t)e * p.w_rows + wr0) * w_ld + kb * 4;
+          for (int r = lane; r < 128; r += 32)
+            cp_async_4(sf + t * 512 + (r % 32) * 16 + (r / 32) * 4, src + (int64_t)r * w_ld);
+        }
+        for (int r = lane; r < 128; r += 32) {
+          const int row = row0 + (r < cnt ? r : cnt - 1);
+          cp_async_4(sf + C::kXTiles * 512 + (r % 32) * 16 + (r / 32) * 4, p.a_s32 + (int64_t)row * a_ld + kb);
+        }
+        cp_async_mbar_arrive_noinc(&full[s]);
+        if (lane == 0) {
+          uint8_t* sx = stage_base + s * C::kStageBytes;
+          uint8_t* sy = sx + C::kXBytes;
+          mbar_arrive_expect_tx(&full[s], C::kXTiles * 8192 + nbox * 16 * 128);
+          for (int t = 0; t < C::kXTiles; ++t)
+            tma_load_3d(sx + t * 16384, &tm_w, &full[s], kb * 128, (t == 0 ? 0 : p.up_off) + nt * 128, e);
+          for (int b = 0; b < nbox; ++b) tma_load_2d(sy + b * 16 * 128, &tm_a, &full[s], kb * 128, row0 + b * 16);
+        }
+        __syncwarp();
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    int it = 0, acc_it = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++acc_it) {
+      int e, row0, cnt, nt;
+      decode(item, e, row0, cnt, nt);
+      const int n_mma = (cnt + 15) / 16 * 16;
+      const int buf = acc_it % C::kAccBufs;
+      const uint32_t aph = (acc_it / C::kAccBufs) & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&acc_empty[buf], aph ^ 1, abort_flag))) break;
+      tc_fence_after();
+      const uint32_t d0 = tmem_base + buf * C::kAccCols;
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const int s = it % C::kStages;
+        const uint32_t ph = (it / C::kStages) & 1;
+        if (!__all_sync(0xffffffffu, mbar_wait(&full[s], ph, abort_flag))) { ok = false; break; }
+        tc_fence_after();
+        fence_proxy_async_smem();
+        if (lane == 0) {
+          const uint32_t sx = smem_u32(stage_base + s * C::kStageBytes);
+          const uint32_t sy = sx + C::kXBytes;
+          const uint32_t slot = tmem_base + C::kSfCol0 + (it & 1) * C::kSfSlot;
+          const uint32_t sfs = smem_u32(sf_base + s * C::kSfBytes);
+          for (int t = 0; t <= C::kXTiles; ++t) tc_cp_32x128b_warpx4(slot + 4 * t, sdesc_sf_chunk(sfs + 512 * t));
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t idesc = idesc_mxf8f6f4(5, 0, 128, n_mma, k, k);
+            const uint64_t bdesc = sdesc_k128_sw128(sy + k * 32);
+            for (int t = 0; t < C::kXTiles; ++t)
+              tc_mma_mxf8f6f4(d0 + t * kTok, sdesc_k128_sw128(sx + t * 16384 + k * 32), bdesc, idesc,
+                              (slot + 4 * t) | ((uint32_t)k << 30), (slot + 4 * C::kXTiles) | ((uint32_t)k << 30),
+                              (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          tc_commit(&empty[s]);
+        }
+        __syncwarp();
+      }
+      if (!ok) break;
+      if (lane == 0) tc_commit(&acc_full[buf]);
+      __syncwarp();
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;
+    const int f = quad * 32 + lane;      // output feature within the 128-row tile
+    int acc_it = 0;
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++acc_it) {
+      int e, row0, cnt, nt;
+      decode(item, e, row0, cnt, nt);
+      const int buf = acc_it % C::kAccBufs;
+      const uint32_t aph = (acc_it / C::kAccBufs) & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[buf], aph, abort_flag))) break;
+      tc_fence_after();
+      const uint32_t tl = tmem_base + ((uint32_t)(quad * 32) << 16) + buf * C::kAccCols;
+      for (int c0 = 0; c0 < cnt; c0 += 16) {
+        uint32_t g[16];
+        BS_TMEM_LD16(tl + c0, g);
+        if constexpr (PAIRED) {
+          uint32_t u[16];
+          BS_TMEM_LD16(tl + kTok + c0, u);
+          tmem_ld_wait();
+          float z[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            z[j] = silu(bf16_round(__uint_as_float(g[j]))) * bf16_round(__uint_as_float(u[j]));
+            const uint32_t m = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(z[j])));
+            if (lane == 0) s_red[quad * 16 + j] = m;
+          }
+          named_bar_epi();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            uint32_t m = s_red[j];
+            m = max(m, s_red[16 + j]);
+            m = max(m, s_red[32 + j]);
+            m = max(m, s_red[48 + j]);
+            float amax = __uint_as_float(m);
+            amax = amax < 1e-4f ? 1e-4f : amax;
+            const float scale = bs_round_pow2(__fdiv_rn(amax, 448.0f));
+            const int tok = c0 + j;
+            if (tok < cnt) {
+              const float q = bs_clamp(__fdiv_rn(z[j], scale), -448.0f, 448.0f);
+              p.hq[(int64_t)(row0 + tok) * p.I + nt * 128 + f] = (uint8_t)(bs_cvt_e4m3x2(q, 0.0f) & 0xFF);
+              if (f == 0) p.hs32[(int64_t)(row0 + tok) * (p.I / 128) + nt] = 0x01010101u * bs_f32_to_e8m0(scale);
+            }
+          }
+          named_bar_epi();
+        } else {
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int tok = c0 + j;
+            if (tok < cnt) {
+              const int orow = p.y_rowmap ? p.y_rowmap[row0 + tok] : row0 + tok;
+              p.y[(int64_t)orow * p.H + nt * 128 + f] = __float2bfloat16_rn(__uint_as_float(g[j]));
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// weights [E, rows, K] packed e2m1; box 128 x 128 x 1
+bool make_weight_map(CUtensorMap* m, const void* w, int64_t E, int64_t rows, int64_t K) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)rows, (cuuint64_t)E};
+  cuuint64_t strides[2] = {(cuuint64_t)(K / 2), (cuuint64_t)(rows * K / 2)};
+  cuuint32_t box[3] = {128u, 128u, 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 3, const_cast<void*>(w), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// token rows [rows, K] e4m3; box 128 x 16
+bool make_act_map(CUtensorMap* m, const void* a, int64_t rows, int64_t K) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)K};
+  cuuint32_t box[2] = {128u, 16u};
+  cuuint32_t estr[2] = {1u, 1u};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(a), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <bool PAIRED>
+cudaError_t launch_grouped(const CUtensorMap& mw, const CUtensorMap& ma, const GemmArgs& a, cudaStream_t st) {
+  using C = Cfg<PAIRED>;
+  auto kern = grouped_gemm_kernel<PAIRED>;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  kern<<<sm_count(), C::kThreads, C::kSmemBytes, st>>>(mw, ma, a);
+  return cudaGetLastError();
+}
+
+}  // namespace moe
+
+// ---------------------------------------------------------------------------
+// launchers used by capi.cu
+// ---------------------------------------------------------------------------
+
+cudaError_t bs_launch_moe_route(const float* logits, int T, int E, int topk, int* idx, float* w, int* counts,
+                                cudaStream_t st) {
+  cudaError_t e = cudaMemsetAsync(counts, 0, sizeof(int) * E, st);
+  if (e != cudaSuccess) return e;
+  if (T == 0) return cudaSuccess;
+  const int threads = 256;
+  const int blocks = (int)(((int64_t)T * 32 + threads - 1) / threads);
+  moe::route_kernel<<<blocks, threads, 0, st>>>(logits, T, E, topk, idx, w, counts);
+  return cudaGetLastError();
+}
+
+cudaError_t bs_launch_moe_histogram(const int* idx, int64_t n, int E, int* counts, int* bad, cudaStream_t st) {
+  cudaError_t e = cudaMemsetAsync(counts, 0, sizeof(int) * E, st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(bad, 0, sizeof(int), st);
+  if (e != cudaSuccess || n == 0) return e;
+  moe::histogram_kernel<<<(int)((n + 255) / 256 < 1024 ? (n + 255) / 256 : 1024), 256, 0, st>>>(idx, n, E, counts, bad);
+  return cudaGetLastError();
+}
+
+cudaError_t bs_launch_moe_scan(const int* counts, int E, int* offsets, int* chunk_prefix, int* cursor,
+                               cudaStream_t st) {
+  moe::scan_kernel<<<1, 1024, 0, st>>>(counts, E, offsets, chunk_prefix, cursor);
+  return cudaGetLastError();
+}
+
+cudaError_t bs_launch_moe_dispatch(const int* idx, int T, int topk, const int* offsets, int* cursor,
+                                   const uint8_t* xq, const uint8_t* xs, int H, uint8_t* ap, uint32_t* aps32,
+                                   int* pos_of, int* row_token, cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  const int64_t warps = (int64_t)T * topk;
+  moe::dispatch_kernel<<<(int)((warps * 32 + 255) / 256), 256, 0, st>>>(idx, T, topk, offsets, cursor, xq, xs, H,
+                                                                        ap, aps32, pos_of, row_token);
+  return cudaGetLastError();
+}
+
+cudaError_t bs_launch_moe_combine(const __nv_bfloat16* y, const int* pos_of, const float* w, int T, int topk, int H,
+                                  __nv_bfloat16* out, cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  int threads = H / 8;
+  if (threads > 512) threads = 512;
+  moe::combine_kernel<<<T, threads, 0, st>>>(y, pos_of, w, topk, H, out);
+  return cudaGetLastError();
+}
+
+// Grouped expert FFN over expert-sorted rows: h = SwiGLU(W13 . a) quantised,
+// y = W2 . h.  rows = capacity of the row buffers (>= offsets[E]).
+int bs_launch_moe_experts(int E, int64_t rows, int H, int I, const uint8_t* ap, const uint32_t* aps32,
+                          const int* offsets, const int* chunk_prefix, const void* w13, const uint8_t* w13_s,
+                          const void* w2, const uint8_t* w2_s, const int* y_rowmap, uint8_t* hq, uint32_t* hs32,
+                          __nv_bfloat16* y, cudaStream_t st, cudaError_t* cerr) {
+  *cerr = cudaSuccess;
+  if (rows == 0) return 0;
+  CUtensorMap mw1, ma1, mw2, ma2;
+  if (!moe::make_weight_map(&mw1, w13, E, 2 * I, H) || !moe::make_act_map(&ma1, ap, rows, H) ||
+      !moe::make_weight_map(&mw2, w2, E, H, I) || !moe::make_act_map(&ma2, hq, rows, I))
+    return BS_ERR_UNSUPPORTED;
+  moe::GemmArgs a1 = {};
+  a1.E = E; a1.K = H; a1.n_tiles = I / 128; a1.w_rows = 2 * I; a1.up_off = I;
+  a1.offsets = offsets; a1.chunk_prefix = chunk_prefix; a1.w_s = w13_s; a1.a_s32 = aps32;
+  a1.hq = hq; a1.hs32 = hs32; a1.I = I; a1.y = nullptr; a1.H = H;
+  *cerr = moe::launch_grouped<true>(mw1, ma1, a1, st);
+  if (*cerr != cudaSuccess) return BS_ERR_CUDA;
+  moe::GemmArgs a2 = {};
+  a2.E = E; a2.K = I; a2.n_tiles = H / 128; a2.w_rows = H; a2.up_off = 0;
+  a2.offsets = offsets; a2.chunk_prefix = chunk_prefix; a2.w_s = w2_s; a2.a_s32 = hs32;
+  a2.hq = nullptr; a2.hs32 = nullptr; a2.I = I; a2.y = y; a2.H = H; a2.y_rowmap = y_rowmap;
+  *cerr = moe::launch_grouped<false>(mw2, ma2, a2, st);
+  return *cerr == cudaSuccess ? 0 : BS_ERR_CUDA;
+}
+
+cudaError_t bs_launch_moe_regroup(const int* cnt, int S, int E, int64_t capacity, const uint8_t* rows_in,
+                                  const uint32_t* sc_in, int H, uint8_t* rows_out, uint32_t* sc_out, int* rowmap,
+                                  int* offsets, int* chunk_prefix, int* scratch, cudaStream_t st) {
+  int* src_off = scratch;               // [S*E + 1]
+  int* dst_off = scratch + S * E + 1;   // [S*E]
+  moe::regroup_plan_kernel<<<1, 1024, 0, st>>>(cnt, S, E, src_off, dst_off, offsets, chunk_prefix);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || capacity == 0) return e;
+  moe::regroup_rows_kernel<<<(int)((capacity * 32 + 255) / 256), 256, 0, st>>>(src_off, dst_off, S * E, capacity,
+                                                                               rows_in, sc_in, H, rows_out, sc_out,
+                                                                               rowmap);
+  return cudaGetLastError();
+}

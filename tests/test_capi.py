@@ -17,7 +17,7 @@ HEADER = os.path.join(ROOT, "include", "bsgemm.h")
 
 def declared_symbols():
     src = open(HEADER).read()
-    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(bs_\w+)\s*\(", src, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|size_t|const char\*)\s+(bs_\w+)\s*\(", src, re.M)))
 
 
 @pytest.fixture(scope="module")
@@ -32,7 +32,9 @@ def lib():
 def test_header_declares_entry_points():
     syms = declared_symbols()
     for s in ["bs_version", "bs_last_error", "bs_device_error_check", "bs_act_quant", "bs_act_quant_inplace",
-              "bs_fp4_act_quant_inplace", "bs_fp8_gemm", "bs_fp4_gemm"]:
+              "bs_fp4_act_quant_inplace", "bs_fp8_gemm", "bs_fp4_gemm", "bs_moe_workspace_size",
+              "bs_moe_forward", "bs_moe_route", "bs_moe_scan", "bs_moe_dispatch", "bs_moe_regroup",
+              "bs_moe_experts", "bs_moe_combine"]:
         assert s in syms
 
 
@@ -63,6 +65,13 @@ def test_invalid_args_return_status(lib):
     # empty problems are a no-op
     assert lib.bs_fp8_gemm(None, None, L.DT_F32, None, None, L.DT_F32, 0, 256, 128, None, None) == L.BS_OK
     assert lib.bs_act_quant(None, L.DT_BF16, 0, 128, 128, 0, None, None, L.DT_F32, None) == L.BS_OK
+    # MoE: sizes
+    assert lib.bs_moe_workspace_size(1024, 4096, 2048, 256, 8) > 100 * 2**20
+    assert lib.bs_moe_workspace_size(16, 100, 2048, 256, 8) == 0
+    assert lib.bs_moe_forward(None, None, 16, 4096, 2048, 2000, 8, None, None, None, None, None, None, 0,
+                              None) == L.BS_ERR_UNSUPPORTED
+    assert lib.bs_moe_forward(None, None, 16, 4096, 2048, 256, 8, None, None, None, None, None, None, 0,
+                              None) == L.BS_ERR_INVALID_ARG
 
 
 def test_python_check_maps_status(lib):

@@ -301,7 +301,7 @@ def bench_moe_1gpu(args, torch, dist, ws, rank, dev):
     """Config-4 MoE layer on one GPU: T=1024, H=4096, I=2048, E=256, top-8."""
     pkg = __import__("importlib").import_module(PKG)
     moe = __import__("importlib").import_module(PKG + ".moe")
-    T, H, I, E, k = args.tokens, 4096, 2048, 256, 8
+    T, H, I, E, k = args.tokens, 4096, 2048, args.experts, 8
     g = torch.Generator(device=dev)
     g.manual_seed(4)
     x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
@@ -311,15 +311,16 @@ def bench_moe_1gpu(args, torch, dist, ws, rank, dev):
     w2 = torch.randint(0, 256, (E, H, I // 2), generator=g, device=dev, dtype=torch.uint8)
     w2_s = 127 - torch.randint(0, 7, (E, H, I // 32), generator=g, device=dev, dtype=torch.uint8)
     out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    weights = moe.MoEWeights(w13, w13_s, w2, w2_s)
     for _ in range(args.warmup):
-        moe.moe_forward(x, logits, w13, w13_s, w2, w2_s, k, out=out)
+        moe.moe_forward(x, logits, weights, k, out=out)
     torch.cuda.synchronize()
     clocks = Clocks(torch.cuda.current_device())
     clocks.start()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
     for _ in range(args.steps):
-        moe.moe_forward(x, logits, w13, w13_s, w2, w2_s, k, out=out)
+        moe.moe_forward(x, logits, weights, k, out=out)
     t1.record()
     torch.cuda.synchronize()
     clk = clocks.stop()
@@ -378,6 +379,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["fp8_prefill", "fp4_decode", "moe"], default="fp8_prefill")
     ap.add_argument("--tokens", type=int, default=1024)
+    ap.add_argument("--experts", type=int, default=256)
     ap.add_argument("--m", type=int, default=16)
     ap.add_argument("--n", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -30,20 +30,23 @@ SIGNATURES = {
     "bs_fp4_act_quant_inplace": [_c_void_p, _i32, _i64, _i64, _i32, _c_void_p],
     "bs_fp8_gemm": [_c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p, _i32, _i64, _i64, _i64, _c_void_p, _c_void_p],
     "bs_fp4_gemm": [_c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p, _i32, _i64, _i64, _i64, _c_void_p, _c_void_p],
+    "bs_moe_pack_scales": [_c_void_p, _i64, _i32, _i32, _c_void_p, _c_void_p],
+    "bs_moe_chunk_capacity": [_i64, _i32],
     "bs_moe_workspace_size": [_i64, _i32, _i32, _i32, _i32],
     "bs_moe_forward": [_c_void_p, _c_void_p, _i64, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p,
                        _c_void_p, _c_void_p, _c_void_p, ctypes.c_size_t, _c_void_p],
     "bs_moe_route": [_c_void_p, _i64, _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p],
     "bs_moe_scan": [_c_void_p, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p],
-    "bs_moe_dispatch": [_c_void_p, _i64, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _c_void_p,
-                        _c_void_p, _c_void_p, _c_void_p],
+    "bs_moe_dispatch": [_c_void_p, _i64, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32,
+                        _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p],
     "bs_moe_regroup": [_c_void_p, _i32, _i32, _i64, _c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p, _c_void_p,
                        _c_void_p, _c_void_p, _c_void_p, _c_void_p],
     "bs_moe_experts": [_i32, _i64, _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                        _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p],
     "bs_moe_combine": [_c_void_p, _c_void_p, _c_void_p, _i64, _i32, _i32, _c_void_p, _c_void_p],
 }
-RESTYPES = {"bs_last_error": ctypes.c_char_p, "bs_moe_workspace_size": ctypes.c_size_t}
+RESTYPES = {"bs_last_error": ctypes.c_char_p, "bs_moe_workspace_size": ctypes.c_size_t,
+            "bs_moe_chunk_capacity": ctypes.c_int64}
 
 
 class BsError(RuntimeError):

@@ -14,17 +14,19 @@ cudaError_t bs_launch_moe_route(const float* logits, int T, int E, int topk, int
                                 cudaStream_t st);
 cudaError_t bs_launch_moe_scan(const int* counts, int E, int* offsets, int* chunk_prefix, int* cursor,
                                cudaStream_t st);
-cudaError_t bs_launch_moe_dispatch(const int* idx, int T, int topk, const int* offsets, int* cursor,
-                                   const uint8_t* xq, const uint8_t* xs, int H, uint8_t* ap, uint32_t* aps32,
-                                   int* pos_of, int* row_token, cudaStream_t st);
+cudaError_t bs_launch_moe_dispatch(const int* idx, int T, int topk, const int* offsets, const int* chunk_prefix,
+                                   int* cursor, const uint8_t* xq, const uint8_t* xs, int H, uint8_t* ap,
+                                   uint8_t* asp, uint32_t* rows_sc, int* pos_of, cudaStream_t st);
+cudaError_t bs_launch_moe_pack_scales(const uint8_t* ws, int64_t E, int rows, int K, uint8_t* out, cudaStream_t st);
+int64_t bs_moe_max_chunks(int64_t rows, int E);
 cudaError_t bs_launch_moe_combine(const __nv_bfloat16* y, const int* pos_of, const float* w, int T, int topk, int H,
                                   __nv_bfloat16* out, cudaStream_t st);
-int bs_launch_moe_experts(int E, int64_t rows, int H, int I, const uint8_t* ap, const uint32_t* aps32,
-                          const int* offsets, const int* chunk_prefix, const void* w13, const uint8_t* w13_s,
-                          const void* w2, const uint8_t* w2_s, const int* y_rowmap, uint8_t* hq, uint32_t* hs32,
+int bs_launch_moe_experts(int E, int64_t rows, int H, int I, const uint8_t* ap, const uint8_t* asp,
+                          const int* offsets, const int* chunk_prefix, const void* w13, const uint8_t* w13_sp,
+                          const void* w2, const uint8_t* w2_sp, const int* y_rowmap, uint8_t* hq, uint8_t* hs_p,
                           __nv_bfloat16* y, cudaStream_t st, cudaError_t* cerr);
 cudaError_t bs_launch_moe_regroup(const int* cnt, int S, int E, int64_t capacity, const uint8_t* rows_in,
-                                  const uint32_t* sc_in, int H, uint8_t* rows_out, uint32_t* sc_out, int* rowmap,
+                                  const uint32_t* sc_in, int H, uint8_t* rows_out, uint8_t* asp, int* rowmap,
                                   int* offsets, int* chunk_prefix, int* scratch, cudaStream_t st);
 
 namespace {
@@ -166,12 +168,13 @@ static int check_moe_dims(int64_t T, int H, int I, int E, int topk) {
 
 namespace {
 struct MoeLayout {
-  size_t counts, cursor, offsets, chunks, idx, w, pos, xq, xs, ap, aps, hq, hs, y, total;
+  size_t counts, cursor, offsets, chunks, idx, w, pos, xq, xs, ap, asp, hq, hsp, y, total;
 };
 size_t up256(size_t v) { return (v + 255) & ~size_t(255); }
 MoeLayout moe_layout(int64_t T, int H, int I, int E, int topk) {
   MoeLayout L;
   const size_t R = (size_t)T * topk;
+  const size_t nch = (size_t)bs_moe_max_chunks((int64_t)R, E);
   size_t o = 0;
   auto take = [&](size_t bytes) { size_t at = o; o += up256(bytes); return at; };
   L.counts = take(4 * (size_t)E);
@@ -184,9 +187,9 @@ MoeLayout moe_layout(int64_t T, int H, int I, int E, int topk) {
   L.xq = take((size_t)T * H);
   L.xs = take((size_t)T * (H / 128));
   L.ap = take(R * H);
-  L.aps = take(R * (H / 128) * 4);
+  L.asp = take(nch * (H / 128) * 512);
   L.hq = take(R * I);
-  L.hs = take(R * (I / 128) * 4);
+  L.hsp = take(nch * (I / 128) * 512);
   L.y = take(R * H * 2);
   L.total = o;
   return L;
@@ -198,17 +201,27 @@ size_t bs_moe_workspace_size(int64_t T, int H, int I, int E, int topk) {
   return moe_layout(T, H, I, E, topk).total;
 }
 
+int bs_moe_pack_scales(const void* w_s, int64_t E, int rows, int K, void* out, void* stream) {
+  if (E <= 0 || rows <= 0 || rows % 128 || K <= 0 || K % 128)
+    return fail(BS_ERR_UNSUPPORTED, "moe_pack_scales: rows (%d) and K (%d) must be positive multiples of 128", rows, K);
+  if (!w_s || !out || !aligned(w_s, 4) || !aligned(out, 16)) return fail(BS_ERR_INVALID_ARG, "moe_pack_scales: pointers");
+  return cuda_status(bs_launch_moe_pack_scales((const uint8_t*)w_s, E, rows, K, (uint8_t*)out, (cudaStream_t)stream),
+                     "moe_pack_scales");
+}
+
+int64_t bs_moe_chunk_capacity(int64_t rows, int E) { return rows < 0 || E <= 0 ? 0 : bs_moe_max_chunks(rows, E); }
+
 int bs_moe_forward(const void* x, const float* logits, int64_t T, int H, int I, int E, int topk, const void* w13,
-                   const void* w13_s, const void* w2, const void* w2_s, void* out, void* workspace,
+                   const void* w13_sp, const void* w2, const void* w2_sp, void* out, void* workspace,
                    size_t workspace_bytes, void* stream) {
   int st = check_moe_dims(T, H, I, E, topk);
   if (st) return st;
   if (T == 0) return BS_OK;
-  if (!x || !logits || !w13 || !w13_s || !w2 || !w2_s || !out || !workspace)
+  if (!x || !logits || !w13 || !w13_sp || !w2 || !w2_sp || !out || !workspace)
     return fail(BS_ERR_INVALID_ARG, "moe: null pointer");
   if (!aligned(x, 16) || !aligned(out, 16) || !aligned(w13, 32) || !aligned(w2, 32) || !aligned(workspace, 256) ||
-      !aligned(w13_s, 4) || !aligned(w2_s, 4))
-    return fail(BS_ERR_INVALID_ARG, "moe: alignment (x,out 16 B; weights 32 B; scales 4 B; workspace 256 B)");
+      !aligned(w13_sp, 16) || !aligned(w2_sp, 16))
+    return fail(BS_ERR_INVALID_ARG, "moe: alignment (x,out,scales 16 B; weights 32 B; workspace 256 B)");
   const MoeLayout L = moe_layout(T, H, I, E, topk);
   if (workspace_bytes < L.total)
     return fail(BS_ERR_INVALID_ARG, "moe: workspace of %zu bytes, %zu needed", workspace_bytes, L.total);
@@ -225,12 +238,12 @@ int bs_moe_forward(const void* x, const float* logits, int64_t T, int H, int I, 
   if (e == cudaSuccess) e = bs_launch_moe_route(logits, (int)T, E, topk, idx, w, counts, s);
   if (e == cudaSuccess) e = bs_launch_moe_scan(counts, E, offsets, chunks, cursor, s);
   if (e == cudaSuccess)
-    e = bs_launch_moe_dispatch(idx, (int)T, topk, offsets, cursor, ws + L.xq, ws + L.xs, H, ws + L.ap,
-                               (uint32_t*)(ws + L.aps), pos, nullptr, s);
+    e = bs_launch_moe_dispatch(idx, (int)T, topk, offsets, chunks, cursor, ws + L.xq, ws + L.xs, H, ws + L.ap,
+                               ws + L.asp, nullptr, pos, s);
   if (e != cudaSuccess) return cuda_status(e, "moe front end");
-  int r = bs_launch_moe_experts(E, T * topk, H, I, ws + L.ap, (const uint32_t*)(ws + L.aps), offsets, chunks, w13,
-                                (const uint8_t*)w13_s, w2, (const uint8_t*)w2_s, nullptr, ws + L.hq,
-                                (uint32_t*)(ws + L.hs), (__nv_bfloat16*)(ws + L.y), s, &e);
+  int r = bs_launch_moe_experts(E, T * topk, H, I, ws + L.ap, ws + L.asp, offsets, chunks, w13,
+                                (const uint8_t*)w13_sp, w2, (const uint8_t*)w2_sp, nullptr, ws + L.hq, ws + L.hsp,
+                                (__nv_bfloat16*)(ws + L.y), s, &e);
   if (r == BS_ERR_UNSUPPORTED) return fail(r, "moe: could not build TMA descriptors");
   if (r) return cuda_status(e, "moe grouped GEMM");
   e = bs_launch_moe_combine((const __nv_bfloat16*)(ws + L.y), pos, w, (int)T, topk, H, (__nv_bfloat16*)out, s);
@@ -250,47 +263,52 @@ int bs_moe_scan(const int* counts, int E, int* offsets, int* chunk_prefix, int* 
   return cuda_status(bs_launch_moe_scan(counts, E, offsets, chunk_prefix, cursor, (cudaStream_t)stream), "moe_scan");
 }
 
-int bs_moe_dispatch(const int* idx, int64_t T, int topk, const int* offsets, int* cursor, const void* xq,
-                    const void* xs, int H, void* rows, void* row_scales, int* pos_of, void* stream) {
+int bs_moe_dispatch(const int* idx, int64_t T, int topk, const int* offsets, const int* chunk_prefix, int* cursor,
+                    const void* xq, const void* xs, int H, void* rows, void* rows_sp, void* rows_sc, int* pos_of,
+                    void* stream) {
   if (T < 0 || topk <= 0 || topk > 8 || H <= 0 || H % 128) return fail(BS_ERR_UNSUPPORTED, "moe_dispatch: bad sizes");
-  if (T > 0 && (!idx || !offsets || !cursor || !xq || !xs || !rows || !row_scales || !pos_of))
+  if (T > 0 && (!idx || !offsets || !chunk_prefix || !cursor || !xq || !xs || !rows || !pos_of ||
+                (!rows_sp && !rows_sc)))
     return fail(BS_ERR_INVALID_ARG, "moe_dispatch: null pointer");
-  if (T > 0 && (!aligned(xq, 16) || !aligned(rows, 16) || !aligned(row_scales, 4)))
+  if (T > 0 && (!aligned(xq, 16) || !aligned(rows, 16) || !aligned(rows_sp, 16) || !aligned(rows_sc, 4)))
     return fail(BS_ERR_INVALID_ARG, "moe_dispatch: alignment");
-  return cuda_status(bs_launch_moe_dispatch(idx, (int)T, topk, offsets, cursor, (const uint8_t*)xq,
-                                            (const uint8_t*)xs, H, (uint8_t*)rows, (uint32_t*)row_scales, pos_of,
-                                            nullptr, (cudaStream_t)stream),
+  return cuda_status(bs_launch_moe_dispatch(idx, (int)T, topk, offsets, chunk_prefix, cursor, (const uint8_t*)xq,
+                                            (const uint8_t*)xs, H, (uint8_t*)rows, (uint8_t*)rows_sp,
+                                            (uint32_t*)rows_sc, pos_of, (cudaStream_t)stream),
                      "moe_dispatch");
 }
 
 int bs_moe_regroup(const int* recv_counts, int n_src, int E, int64_t capacity, const void* rows_in,
-                   const void* scales_in, int H, void* rows_out, void* scales_out, int* rowmap, int* offsets,
+                   const void* scales_in, int H, void* rows_out, void* rows_sp, int* rowmap, int* offsets,
                    int* chunk_prefix, int* scratch, void* stream) {
   if (n_src <= 0 || E <= 0 || n_src * E > 1024 || H <= 0 || H % 128 || capacity < 0)
     return fail(BS_ERR_UNSUPPORTED, "moe_regroup: bad sizes");
   if (!recv_counts || !offsets || !chunk_prefix || !scratch ||
-      (capacity > 0 && (!rows_in || !scales_in || !rows_out || !scales_out || !rowmap)))
+      (capacity > 0 && (!rows_in || !scales_in || !rows_out || !rows_sp || !rowmap)))
     return fail(BS_ERR_INVALID_ARG, "moe_regroup: null pointer");
+  if (capacity > 0 && (!aligned(rows_in, 16) || !aligned(rows_out, 16) || !aligned(rows_sp, 16)))
+    return fail(BS_ERR_INVALID_ARG, "moe_regroup: alignment");
   return cuda_status(bs_launch_moe_regroup(recv_counts, n_src, E, capacity, (const uint8_t*)rows_in,
-                                           (const uint32_t*)scales_in, H, (uint8_t*)rows_out, (uint32_t*)scales_out,
+                                           (const uint32_t*)scales_in, H, (uint8_t*)rows_out, (uint8_t*)rows_sp,
                                            rowmap, offsets, chunk_prefix, scratch, (cudaStream_t)stream),
                      "moe_regroup");
 }
 
-int bs_moe_experts(int E, int64_t capacity, int H, int I, const void* rows, const void* row_scales,
-                   const int* offsets, const int* chunk_prefix, const void* w13, const void* w13_s, const void* w2,
-                   const void* w2_s, const int* y_rowmap, void* hq, void* hs, void* y, void* stream) {
+int bs_moe_experts(int E, int64_t capacity, int H, int I, const void* rows, const void* rows_sp,
+                   const int* offsets, const int* chunk_prefix, const void* w13, const void* w13_sp, const void* w2,
+                   const void* w2_sp, const int* y_rowmap, void* hq, void* hs_p, void* y, void* stream) {
   int st = check_moe_dims(capacity, H, I, E, 1);
   if (st) return st;
   if (capacity == 0) return BS_OK;
-  if (!rows || !row_scales || !offsets || !chunk_prefix || !w13 || !w13_s || !w2 || !w2_s || !hq || !hs || !y)
+  if (!rows || !rows_sp || !offsets || !chunk_prefix || !w13 || !w13_sp || !w2 || !w2_sp || !hq || !hs_p || !y)
     return fail(BS_ERR_INVALID_ARG, "moe_experts: null pointer");
-  if (!aligned(rows, 16) || !aligned(hq, 16) || !aligned(y, 16) || !aligned(w13, 32) || !aligned(w2, 32))
+  if (!aligned(rows, 16) || !aligned(hq, 16) || !aligned(y, 16) || !aligned(w13, 32) || !aligned(w2, 32) ||
+      !aligned(rows_sp, 16) || !aligned(hs_p, 16) || !aligned(w13_sp, 16) || !aligned(w2_sp, 16))
     return fail(BS_ERR_INVALID_ARG, "moe_experts: alignment");
   cudaError_t e;
-  int r = bs_launch_moe_experts(E, capacity, H, I, (const uint8_t*)rows, (const uint32_t*)row_scales, offsets,
-                                chunk_prefix, w13, (const uint8_t*)w13_s, w2, (const uint8_t*)w2_s, y_rowmap,
-                                (uint8_t*)hq, (uint32_t*)hs, (__nv_bfloat16*)y, (cudaStream_t)stream, &e);
+  int r = bs_launch_moe_experts(E, capacity, H, I, (const uint8_t*)rows, (const uint8_t*)rows_sp, offsets,
+                                chunk_prefix, w13, (const uint8_t*)w13_sp, w2, (const uint8_t*)w2_sp, y_rowmap,
+                                (uint8_t*)hq, (uint8_t*)hs_p, (__nv_bfloat16*)y, (cudaStream_t)stream, &e);
   if (r == BS_ERR_UNSUPPORTED) return fail(r, "moe_experts: could not build TMA descriptors");
   if (r) return cuda_status(e, "moe_experts");
   return BS_OK;

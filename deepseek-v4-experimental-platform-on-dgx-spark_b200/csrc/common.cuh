@@ -42,14 +42,22 @@ template <> BS_DEVINL float bs_from_f32<float>(float v) { return v; }
 template <> BS_DEVINL __nv_bfloat16 bs_from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
 template <> BS_DEVINL __half bs_from_f32<__half>(float v) { return __float2half_rn(v); }
 
-// ceil(fp32(log2(x))) for x > 0: exact for powers of two, otherwise the
-// float64 log2 rounded once to fp32 (which is what fp32 log2 returns on the
-// host), then the ceiling.  Only evaluated once per quantisation block.
+// ceil(fp32(log2(x))) for x > 0 (the reference's torch.ceil(torch.log2(x))).
+// x = 2^e * (1 + m/2^23).  m == 0: exactly e.  Otherwise the ceiling is e+1
+// unless fp32(e + log2(1 + m/2^23)) rounds back to e, which needs
+// log2(1 + m/2^23) below half an ulp of e -- only possible for m < 128
+// (|e| <= 149); that rare case is decided with a float64 log2 rounded once
+// to fp32, which reproduces the correctly rounded fp32 log2.
 BS_DEVINL int bs_ceil_log2(float x) {
-  uint32_t b = __float_as_uint(x);
-  uint32_t e = (b >> 23) & 0xFF;
-  if ((b & 0x7FFFFF) == 0 && e != 0) return (int)e - 127;
-  float l = (float)log2((double)x);
+  const uint32_t b = __float_as_uint(x);
+  const int ebits = (int)((b >> 23) & 0xFF);
+  const uint32_t m = b & 0x7FFFFF;
+  if (ebits != 0) {
+    const int e = ebits - 127;
+    if (m == 0) return e;
+    if (m >= 128 || e == 0) return e + 1;
+  }
+  const float l = (float)log2((double)x);
   return (int)ceilf(l);
 }
 
@@ -60,6 +68,9 @@ BS_DEVINL float bs_exp2i(int c) {
   if (c >= -149) return __uint_as_float(1u << (c + 149));
   return 0.0f;
 }
+
+// 1/s for an exact power of two s with 2^-126 <= s <= 2^126 (exact).
+BS_DEVINL float bs_inv_pow2(float s) { return __uint_as_float((uint32_t)(254 - ((__float_as_uint(s) >> 23) & 0xFF)) << 23); }
 
 // 2^ceil(log2(s)) with NaN passthrough (the reference's _round_scale_pow2).
 BS_DEVINL float bs_round_pow2(float s) {
@@ -153,6 +164,15 @@ BS_DEVINL void cp_async_4(void* smem_dst, const void* gmem_src) {
 }
 BS_DEVINL void cp_async_mbar_arrive_noinc(uint64_t* bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// 1-D bulk async copy global -> this CTA's shared memory, completing on an
+// mbarrier (addresses 16-byte aligned, size a multiple of 16).
+BS_DEVINL void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(smem_dst)),
+               "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
 }
 
 BS_DEVINL void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }

@@ -5,7 +5,7 @@
 // DeepSeek model file) with a fixed sequence of kernels and no host sync:
 //
 //   route     top-k over gate logits + softmax weights, expert histogram
-//   scan      histogram -> row offsets and 128-token chunk prefix per expert
+//   scan      histogram -> row offsets and token-chunk prefix per expert
 //   dispatch  expert-sorted copy of the e4m3 token rows and their ue8m0
 //             scales (the layout the grouped GEMM and the EP exchange read)
 //   gemm13    persistent grouped GEMM: W1|W3 (e2m1, ue8m0 1x32) x tokens
@@ -14,16 +14,29 @@
 //   combine   out[t] = sum_k w[t,k] * y[row(t,k)]   (fp32, deterministic)
 //
 // GEMM orientation: the expert's weight rows are the 128-row MMA operand and
-// the expert's tokens the MMA N dimension (16..128, set per work item in the
+// the expert's tokens the MMA N dimension (16..112, set per work item in the
 // runtime instruction descriptor), so a handful of tokens per expert still
-// streams each weight tile exactly once per 128-token chunk.  Both operands
+// streams each weight tile exactly once per token chunk.  Both operands
 // carry ue8m0 block scales in TMEM (kind::mxf8f6f4.block_scale), so the
 // accumulator stays in TMEM for the whole K loop.
+//
+// Scale factors reach the MMA through TMEM (tcgen05.cp of a 32-row x 16-byte
+// chunk).  Both operands' ue8m0 scales are kept in that chunk layout in
+// global memory, so one 512-byte bulk copy per operand and K block fetches
+// them: byte (r%32)*16 + (r/32)*4 + k holds the scale of row r for the k-th
+// 32-wide sub-block (0..3) of the 128-wide K block.
+//   weights:     [E][rows/128][K/128][512]   (bs_moe_pack_scales, once at load)
+//   activations: [chunk][K/128][512]         (written by dispatch / regroup /
+//                                             the W13 epilogue; a chunk is <= 112
+//                                             consecutive rows of one expert)
 #include "common.cuh"
 
 namespace moe {
 
-constexpr int kTok = 128;  // tokens per work item (MMA N <= 128)
+// Tokens per work item (MMA N <= 112).  112 lets W13 keep two gate+up
+// accumulator buffers (2 x 224 TMEM columns) plus the scale-factor slots, so
+// the SwiGLU epilogue of one item overlaps the MMAs of the next.
+constexpr int kTok = 112;
 
 // ---------------------------------------------------------------------------
 // routing
@@ -81,18 +94,8 @@ __global__ void route_kernel(const float* __restrict__ logits, int T, int E, int
   }
 }
 
-// Histogram of externally supplied expert ids (idx [n]) into counts[E].
-__global__ void histogram_kernel(const int* __restrict__ idx, int64_t n, int E, int* __restrict__ counts,
-                                 int* __restrict__ bad) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int e = idx[i];
-    if (e >= 0 && e < E) atomicAdd(&counts[e], 1);
-    else atomicExch(bad, 1);
-  }
-}
-
 // Single block of 1024 threads: exclusive scans of counts (row offsets) and
-// of 128-token chunks per expert (E <= 1024); zeroes the dispatch cursors.
+// of kTok-token chunks per expert (E <= 1024); zeroes the dispatch cursors.
 __global__ void __launch_bounds__(1024) scan_kernel(const int* __restrict__ counts, int E, int* __restrict__ offsets,
                                                     int* __restrict__ chunk_prefix, int* __restrict__ cursor) {
   __shared__ int w_rows[32], w_chunks[32];
@@ -133,13 +136,18 @@ __global__ void __launch_bounds__(1024) scan_kernel(const int* __restrict__ coun
   }
 }
 
-// One warp per (token, slot): claim a row in the expert's segment and copy
-// the e4m3 row (H bytes) and its scales, replicated four times per word (one
-// copy per 32-K sub-block, the layout the MMA scale loads expect).
+// Byte offset of row r's scale word inside a 512-byte scale chunk.
+BS_DEVINL int sf_word_off(int r) { return (r % 32) * 16 + (r / 32) * 4; }
+
+// One warp per (token, slot): claim a row in the expert's segment, copy the
+// e4m3 row (H bytes) and write its 1x128 scales into the packed chunk layout
+// (replicated for the four 32-wide sub-blocks); optionally also row-major
+// (rows_sc [rows, H/128] u32, the form the expert-parallel exchange sends).
 __global__ void dispatch_kernel(const int* __restrict__ idx, int T, int topk, const int* __restrict__ offsets,
-                                int* __restrict__ cursor, const uint8_t* __restrict__ xq,
-                                const uint8_t* __restrict__ xs, int H, uint8_t* __restrict__ ap,
-                                uint32_t* __restrict__ aps32, int* __restrict__ pos_of, int* __restrict__ row_token) {
+                                const int* __restrict__ chunk_prefix, int* __restrict__ cursor,
+                                const uint8_t* __restrict__ xq, const uint8_t* __restrict__ xs, int H,
+                                uint8_t* __restrict__ ap, uint8_t* __restrict__ asp, uint32_t* __restrict__ rows_sc,
+                                int* __restrict__ pos_of) {
   const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= (int64_t)T * topk) return;
@@ -148,15 +156,37 @@ __global__ void dispatch_kernel(const int* __restrict__ idx, int T, int topk, co
   int pos = 0;
   if (lane == 0) pos = offsets[e] + atomicAdd(&cursor[e], 1);
   pos = __shfl_sync(0xffffffffu, pos, 0);
-  if (lane == 0) {
-    pos_of[warp] = pos;
-    if (row_token) row_token[pos] = t;
-  }
+  if (lane == 0) pos_of[warp] = pos;
   const uint4* src = reinterpret_cast<const uint4*>(xq + (int64_t)t * H);
   uint4* dst = reinterpret_cast<uint4*>(ap + (int64_t)pos * H);
   for (int i = lane; i < H / 16; i += 32) dst[i] = src[i];
   const int nb = H / 128;
-  for (int i = lane; i < nb; i += 32) aps32[(int64_t)pos * nb + i] = 0x01010101u * xs[(int64_t)t * nb + i];
+  const int cin = pos - offsets[e];
+  const int64_t cg = chunk_prefix[e] + cin / kTok;
+  const int r = cin % kTok;
+  for (int i = lane; i < nb; i += 32) {
+    const uint32_t v = 0x01010101u * xs[(int64_t)t * nb + i];
+    if (asp) *reinterpret_cast<uint32_t*>(asp + (cg * nb + i) * 512 + sf_word_off(r)) = v;
+    if (rows_sc) rows_sc[(int64_t)pos * nb + i] = v;
+  }
+}
+
+// Weight scales [E, rows, K/32] -> packed chunk layout [E][rows/128][K/128][512].
+// One thread per 32-bit word of the output: word w of a chunk holds the four
+// sub-block scales of row r = w/4 + 32*(w%4) (byte w*4 = sf_word_off(r)).
+__global__ void pack_scales_kernel(const uint8_t* __restrict__ ws, int64_t E, int rows, int K,
+                                   uint8_t* __restrict__ out) {
+  const int nkb = K / 128, rt = rows / 128;
+  const int64_t words = E * rt * nkb * 128;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < words; i += (int64_t)gridDim.x * blockDim.x) {
+    const int w = (int)(i % 128);
+    const int64_t chunk = i / 128;             // (e, row tile, kb)
+    const int kb = (int)(chunk % nkb);
+    const int64_t ert = chunk / nkb;
+    const int r = (w / 4) + 32 * (w % 4);
+    const int64_t row = ert * 128 + r;         // row over all experts' tiles
+    reinterpret_cast<uint32_t*>(out)[i] = *reinterpret_cast<const uint32_t*>(ws + row * (K / 32) + kb * 4);
+  }
 }
 
 // out[t] = bf16( sum_k w[t,k] * y[pos_of[t,k]] ), fp32 accumulation in slot
@@ -194,7 +224,7 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ y, const int* _
 // Single block.  cnt[s*E + e] = rows from source s for local expert e.
 // src_off: exclusive prefix in (s, e) order (arrival position);
 // dst_off: exclusive prefix in (e, s) order (expert-major position), stored
-// transposed as dst_off[s*E + e]; plus the expert offsets / chunk prefix.
+// at [s*E + e]; plus the expert offsets / chunk prefix.
 __global__ void __launch_bounds__(1024) regroup_plan_kernel(const int* __restrict__ cnt, int S, int E,
                                                             int* __restrict__ src_off, int* __restrict__ dst_off,
                                                             int* __restrict__ offsets, int* __restrict__ chunk_prefix) {
@@ -229,11 +259,13 @@ __global__ void __launch_bounds__(1024) regroup_plan_kernel(const int* __restric
 }
 
 // One warp per arrived row j: find its (source, expert) group, move the row
-// and its scales to the expert-major position, record rowmap[dst] = j.
+// to its expert-major position, write its scales into the packed chunk
+// layout, record rowmap[dst] = j.
 __global__ void regroup_rows_kernel(const int* __restrict__ src_off, const int* __restrict__ dst_off, int n_groups,
+                                    int E, const int* __restrict__ offsets, const int* __restrict__ chunk_prefix,
                                     int64_t capacity, const uint8_t* __restrict__ rows_in,
                                     const uint32_t* __restrict__ sc_in, int H, uint8_t* __restrict__ rows_out,
-                                    uint32_t* __restrict__ sc_out, int* __restrict__ rowmap) {
+                                    uint8_t* __restrict__ asp, int* __restrict__ rowmap) {
   const int64_t j = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (j >= capacity || j >= src_off[n_groups]) return;
@@ -247,7 +279,12 @@ __global__ void regroup_rows_kernel(const int* __restrict__ src_off, const int* 
   uint4* d = reinterpret_cast<uint4*>(rows_out + dst * H);
   for (int i = lane; i < H / 16; i += 32) d[i] = src[i];
   const int nb = H / 128;
-  for (int i = lane; i < nb; i += 32) sc_out[dst * nb + i] = sc_in[j * nb + i];
+  const int e = lo % E;
+  const int cin = (int)(dst - offsets[e]);
+  const int64_t cg = chunk_prefix[e] + cin / kTok;
+  const int r = cin % kTok;
+  for (int i = lane; i < nb; i += 32)
+    *reinterpret_cast<uint32_t*>(asp + (cg * nb + i) * 512 + sf_word_off(r)) = sc_in[j * nb + i];
   if (lane == 0) rowmap[dst] = (int)j;
 }
 
@@ -262,11 +299,11 @@ struct GemmArgs {
   int w_rows;                // rows per expert in the weight tensor
   int up_off;                // W13: row offset of W3 inside W13
   const int* offsets;        // [E+1] token-row offsets
-  const int* chunk_prefix;   // [E+1] prefix of 128-token chunks
-  const uint8_t* w_s;        // [E, w_rows, K/32] ue8m0
-  const uint32_t* a_s32;     // [rows, K/128] ue8m0 x4
+  const int* chunk_prefix;   // [E+1] prefix of token chunks
+  const uint8_t* w_sp;       // weights' scales, packed [E][w_rows/128][K/128][512]
+  const uint8_t* a_sp;       // token scales, packed [chunk][K/128][512]
   uint8_t* hq;               // W13: [rows, I] e4m3
-  uint32_t* hs32;            // W13: [rows, I/128] ue8m0 x4
+  uint8_t* hs_p;             // W13: hidden scales, packed [chunk][I/128][512]
   int I;
   __nv_bfloat16* y;          // W2: [rows, H] bf16
   int H;
@@ -277,11 +314,11 @@ template <bool PAIRED>
 struct Cfg {
   static constexpr int kXTiles = PAIRED ? 2 : 1;
   static constexpr int kXBytes = kXTiles * 128 * 128;   // unpacked e2m1 in smem
-  static constexpr int kYBytes = kTok * 128;
+  static constexpr int kYBytes = 128 * 128;             // token tile: 32-row boxes, <= 128 rows
   static constexpr int kStageBytes = kXBytes + kYBytes;
   static constexpr int kStages = PAIRED ? 4 : 6;
   static constexpr int kSfBytes = 512 * (kXTiles + 1);
-  static constexpr int kAccBufs = PAIRED ? 1 : 2;
+  static constexpr int kAccBufs = 2;
   static constexpr int kAccCols = kXTiles * kTok;        // per accumulator buffer
   static constexpr int kSfSlot = 4 * (kXTiles + 1);
   static constexpr int kSfCol0 = kAccBufs * kAccCols;
@@ -289,7 +326,8 @@ struct Cfg {
   static constexpr int kTmemCols = 512;
   static constexpr int kThreads = 192;
   static constexpr int kMaxE = 1024;
-  static constexpr int kSmemBytes = 1024 + kStages * (kStageBytes + kSfBytes) + 2 * (kMaxE + 1) * 4 + 4 * 16 * 4 + 256;
+  static constexpr int kSmemBytes = 1024 + kStages * (kStageBytes + kSfBytes) + 2 * (kMaxE + 1) * 4 + 2 * 80 * 4 + 256;
+  static_assert(kStageBytes % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
 };
 
 BS_DEVINL void named_bar_epi() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
@@ -307,8 +345,10 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* sf_base = smem + C::kStages * C::kStageBytes;
   int* s_off = reinterpret_cast<int*>(sf_base + C::kStages * C::kSfBytes);
   int* s_chunk = s_off + C::kMaxE + 1;
-  uint32_t* s_red = reinterpret_cast<uint32_t*>(s_chunk + C::kMaxE + 1);   // [4 warps][16 tokens]
-  uint64_t* full = reinterpret_cast<uint64_t*>(s_red + 64);
+  // per 16-token epilogue chunk, double-buffered by chunk parity:
+  // [4 warps][16] amax bits, then [16] scales
+  uint32_t* s_red = reinterpret_cast<uint32_t*>(s_chunk + C::kMaxE + 1);
+  uint64_t* full = reinterpret_cast<uint64_t*>(s_red + 2 * 80);
   uint64_t* empty = full + C::kStages;
   uint64_t* acc_full = empty + C::kStages;
   uint64_t* acc_empty = acc_full + 2;
@@ -323,7 +363,7 @@ __global__ void __launch_bounds__(192, 1)
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(&full[s], 1 + 32);
+      mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -348,67 +388,70 @@ __global__ void __launch_bounds__(192, 1)
   const int n_items = s_chunk[E] * p.n_tiles;
   const int nkb = p.K / 128;
 
-  // work item -> (expert, first token row, token count, output tile)
-  auto decode = [&](int item, int& e, int& row0, int& cnt, int& nt) {
-    const int cg = item / p.n_tiles;
+  // work item -> (expert, first token row, token count, output tile, global chunk)
+  auto decode = [&](int item, int& e, int& row0, int& cnt, int& nt, int& cg) {
+    cg = item / p.n_tiles;
     nt = item - cg * p.n_tiles;
-    int lo = 0, hi = E;  // largest e with s_chunk[e] <= cg
+    int lo = 0, hi = E;  // largest e with s_chunk[e] <= cg (then s_chunk[e+1] > cg)
     while (hi - lo > 1) {
       const int mid = (lo + hi) >> 1;
       if (s_chunk[mid] <= cg) lo = mid; else hi = mid;
     }
     e = lo;
-    const int chunk = cg - s_chunk[e];
-    row0 = s_off[e] + chunk * kTok;
+    row0 = s_off[e] + (cg - s_chunk[e]) * kTok;
     const int left = s_off[e + 1] - row0;
     cnt = left < kTok ? left : kTok;
   };
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
+    // One lane issues everything as async-proxy copies: the weight tile(s)
+    // by TMA, the expert's token rows in 32-row TMA boxes, and both operands'
+    // scale chunks as 512-byte bulk copies.
     int it = 0;
     bool ok = true;
-    const int64_t w_ld = p.K / 32;
-    const int a_ld = p.K / 128;
+    const int w_tiles = p.w_rows / 128;
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-      int e, row0, cnt, nt;
-      decode(item, e, row0, cnt, nt);
-      const int nbox = (cnt + 15) / 16;
+      int e, row0, cnt, nt, cg;
+      decode(item, e, row0, cnt, nt, cg);
+      const int nbox = (cnt + 31) / 32;
       for (int kb = 0; kb < nkb; ++kb, ++it) {
         const int s = it % C::kStages;
         const uint32_t ph = (it / C::kStages) & 1;
         if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1, abort_flag))) { ok = false; break; }
-        uint8_t* sf = sf_base + s * C::kSfBytes;
-        for (int t = 0; t < C::kXTiles; ++t) {
-          const int wr0 = (t == 0 ? 0 : p.up_off) + nt * 128;
-          const uint8_t* src = p.w_s + ((int64_t)e * p.w_rows + wr0) * w_ld + kb * 4;
-          for (int r = lane; r < 128; r += 32)
-            cp_async_4(sf + t * 512 + (r % 32) * 16 + (r / 32) * 4, src + (int64_t)r * w_ld);
-        }
-        for (int r = lane; r < 128; r += 32) {
-          const int row = row0 + (r < cnt ? r : cnt - 1);
-          cp_async_4(sf + C::kXTiles * 512 + (r % 32) * 16 + (r / 32) * 4, p.a_s32 + (int64_t)row * a_ld + kb);
-        }
-        cp_async_mbar_arrive_noinc(&full[s]);
         if (lane == 0) {
           uint8_t* sx = stage_base + s * C::kStageBytes;
           uint8_t* sy = sx + C::kXBytes;
-          mbar_arrive_expect_tx(&full[s], C::kXTiles * 8192 + nbox * 16 * 128);
-          for (int t = 0; t < C::kXTiles; ++t)
-            tma_load_3d(sx + t * 16384, &tm_w, &full[s], kb * 128, (t == 0 ? 0 : p.up_off) + nt * 128, e);
-          for (int b = 0; b < nbox; ++b) tma_load_2d(sy + b * 16 * 128, &tm_a, &full[s], kb * 128, row0 + b * 16);
+          uint8_t* sf = sf_base + s * C::kSfBytes;
+          mbar_arrive_expect_tx(&full[s], C::kXTiles * (8192 + 512) + nbox * 32 * 128 + 512);
+          for (int t = 0; t < C::kXTiles; ++t) {
+            const int wr0 = (t == 0 ? 0 : p.up_off) + nt * 128;
+            tma_load_3d(sx + t * 16384, &tm_w, &full[s], kb * 128, wr0, e);
+            bulk_load(sf + t * 512, p.w_sp + (((int64_t)e * w_tiles + wr0 / 128) * nkb + kb) * 512, 512, &full[s]);
+          }
+          for (int b = 0; b < nbox; ++b) tma_load_2d(sy + b * 32 * 128, &tm_a, &full[s], kb * 128, row0 + b * 32);
+          bulk_load(sf + C::kXTiles * 512, p.a_sp + ((int64_t)cg * nkb + kb) * 512, 512, &full[s]);
         }
         __syncwarp();
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
+    // Descriptors are built once; per MMA only the 16-byte-unit start address
+    // advances (+2 per 32-byte K step).
+    const uint64_t dx0 = sdesc_k128_sw128(smem_u32(stage_base));
+    const uint64_t dsf0 = sdesc_sf_chunk(smem_u32(sf_base));
+    constexpr uint64_t kStageStep = (uint64_t)(C::kStageBytes >> 4);
+    constexpr uint64_t kSfStep = (uint64_t)(C::kSfBytes >> 4);
+    constexpr uint64_t kYOff = (uint64_t)(C::kXBytes >> 4);
+    const uint32_t sf_tmem0 = tmem_base + C::kSfCol0;
     int it = 0, acc_it = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++acc_it) {
-      int e, row0, cnt, nt;
-      decode(item, e, row0, cnt, nt);
+      int e, row0, cnt, nt, cg;
+      decode(item, e, row0, cnt, nt, cg);
       const int n_mma = (cnt + 15) / 16 * 16;
+      const uint32_t idesc0 = idesc_mxf8f6f4(5, 0, 128, n_mma, 0, 0);
       const int buf = acc_it % C::kAccBufs;
       const uint32_t aph = (acc_it / C::kAccBufs) & 1;
       if (!__all_sync(0xffffffffu, mbar_wait(&acc_empty[buf], aph ^ 1, abort_flag))) break;
@@ -419,21 +462,23 @@ __global__ void __launch_bounds__(192, 1)
         const uint32_t ph = (it / C::kStages) & 1;
         if (!__all_sync(0xffffffffu, mbar_wait(&full[s], ph, abort_flag))) { ok = false; break; }
         tc_fence_after();
-        fence_proxy_async_smem();
         if (lane == 0) {
-          const uint32_t sx = smem_u32(stage_base + s * C::kStageBytes);
-          const uint32_t sy = sx + C::kXBytes;
-          const uint32_t slot = tmem_base + C::kSfCol0 + (it & 1) * C::kSfSlot;
-          const uint32_t sfs = smem_u32(sf_base + s * C::kSfBytes);
-          for (int t = 0; t <= C::kXTiles; ++t) tc_cp_32x128b_warpx4(slot + 4 * t, sdesc_sf_chunk(sfs + 512 * t));
+          const uint64_t dx = dx0 + (uint64_t)s * kStageStep;
+          const uint64_t dy = dx + kYOff;
+          const uint64_t dsf = dsf0 + (uint64_t)s * kSfStep;
+          const uint32_t slot = sf_tmem0 + (it & 1) * C::kSfSlot;
+#pragma unroll
+          for (int t = 0; t <= C::kXTiles; ++t) tc_cp_32x128b_warpx4(slot + 4 * t, dsf + (uint64_t)(32 * t));
+          const uint32_t sfb = slot + 4 * C::kXTiles;
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            const uint32_t idesc = idesc_mxf8f6f4(5, 0, 128, n_mma, k, k);
-            const uint64_t bdesc = sdesc_k128_sw128(sy + k * 32);
+            const uint32_t idesc = idesc0 | ((uint32_t)k << 4) | ((uint32_t)k << 29);
+            const uint32_t kid = (uint32_t)k << 30;
+            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+#pragma unroll
             for (int t = 0; t < C::kXTiles; ++t)
-              tc_mma_mxf8f6f4(d0 + t * kTok, sdesc_k128_sw128(sx + t * 16384 + k * 32), bdesc, idesc,
-                              (slot + 4 * t) | ((uint32_t)k << 30), (slot + 4 * C::kXTiles) | ((uint32_t)k << 30),
-                              (kb > 0 || k > 0) ? 1u : 0u);
+              tc_mma_mxf8f6f4(d0 + t * kTok, dx + (uint64_t)(t * 1024 + 2 * k), dy + (uint64_t)(2 * k), idesc,
+                              (slot + 4 * t) | kid, sfb | kid, acc);
           }
           tc_commit(&empty[s]);
         }
@@ -449,8 +494,8 @@ __global__ void __launch_bounds__(192, 1)
     const int f = quad * 32 + lane;      // output feature within the 128-row tile
     int acc_it = 0;
     for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++acc_it) {
-      int e, row0, cnt, nt;
-      decode(item, e, row0, cnt, nt);
+      int e, row0, cnt, nt, cg;
+      decode(item, e, row0, cnt, nt, cg);
       const int buf = acc_it % C::kAccBufs;
       const uint32_t aph = (acc_it / C::kAccBufs) & 1;
       if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[buf], aph, abort_flag))) break;
@@ -463,31 +508,38 @@ __global__ void __launch_bounds__(192, 1)
           uint32_t u[16];
           BS_TMEM_LD16(tl + kTok + c0, u);
           tmem_ld_wait();
+          uint32_t* red = s_red + ((c0 >> 4) & 1) * 80;
           float z[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             z[j] = silu(bf16_round(__uint_as_float(g[j]))) * bf16_round(__uint_as_float(u[j]));
+            // |z| bit patterns order like the values (NaN above inf), so an
+            // unsigned max is the NaN-propagating amax
             const uint32_t m = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(z[j])));
-            if (lane == 0) s_red[quad * 16 + j] = m;
+            if (lane == 0) red[quad * 16 + j] = m;
+          }
+          named_bar_epi();
+          if (quad == 0 && lane < 16) {
+            const uint32_t m = max(max(red[lane], red[16 + lane]), max(red[32 + lane], red[48 + lane]));
+            float amax = __uint_as_float(m);
+            amax = amax < 1e-4f ? 1e-4f : amax;
+            const float scale = bs_round_pow2(__fdiv_rn(amax, 448.0f));
+            red[64 + lane] = __float_as_uint(scale);
+            const int r = c0 + lane;
+            if (r < cnt)
+              *reinterpret_cast<uint32_t*>(p.hs_p + ((int64_t)cg * (p.I / 128) + nt) * 512 + sf_word_off(r)) =
+                  0x01010101u * bs_f32_to_e8m0(scale);
           }
           named_bar_epi();
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            uint32_t m = s_red[j];
-            m = max(m, s_red[16 + j]);
-            m = max(m, s_red[32 + j]);
-            m = max(m, s_red[48 + j]);
-            float amax = __uint_as_float(m);
-            amax = amax < 1e-4f ? 1e-4f : amax;
-            const float scale = bs_round_pow2(__fdiv_rn(amax, 448.0f));
             const int tok = c0 + j;
             if (tok < cnt) {
-              const float q = bs_clamp(__fdiv_rn(z[j], scale), -448.0f, 448.0f);
+              // the scale is a power of two: x * (1/s) == x / s exactly
+              const float q = bs_clamp(z[j] * bs_inv_pow2(__uint_as_float(red[64 + j])), -448.0f, 448.0f);
               p.hq[(int64_t)(row0 + tok) * p.I + nt * 128 + f] = (uint8_t)(bs_cvt_e4m3x2(q, 0.0f) & 0xFF);
-              if (f == 0) p.hs32[(int64_t)(row0 + tok) * (p.I / 128) + nt] = 0x01010101u * bs_f32_to_e8m0(scale);
             }
           }
-          named_bar_epi();
         } else {
           tmem_ld_wait();
 #pragma unroll
@@ -547,13 +599,13 @@ bool make_weight_map(CUtensorMap* m, const void* w, int64_t E, int64_t rows, int
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// token rows [rows, K] e4m3; box 128 x 16
+// token rows [rows, K] e4m3; box 128 x 32
 bool make_act_map(CUtensorMap* m, const void* a, int64_t rows, int64_t K) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return false;
   cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)K};
-  cuuint32_t box[2] = {128u, 16u};
+  cuuint32_t box[2] = {128u, 32u};
   cuuint32_t estr[2] = {1u, 1u};
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(a), dims, strides, box, estr,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -601,29 +653,33 @@ cudaError_t bs_launch_moe_route(const float* logits, int T, int E, int topk, int
   return cudaGetLastError();
 }
 
-cudaError_t bs_launch_moe_histogram(const int* idx, int64_t n, int E, int* counts, int* bad, cudaStream_t st) {
-  cudaError_t e = cudaMemsetAsync(counts, 0, sizeof(int) * E, st);
-  if (e == cudaSuccess) e = cudaMemsetAsync(bad, 0, sizeof(int), st);
-  if (e != cudaSuccess || n == 0) return e;
-  moe::histogram_kernel<<<(int)((n + 255) / 256 < 1024 ? (n + 255) / 256 : 1024), 256, 0, st>>>(idx, n, E, counts, bad);
-  return cudaGetLastError();
-}
-
 cudaError_t bs_launch_moe_scan(const int* counts, int E, int* offsets, int* chunk_prefix, int* cursor,
                                cudaStream_t st) {
   moe::scan_kernel<<<1, 1024, 0, st>>>(counts, E, offsets, chunk_prefix, cursor);
   return cudaGetLastError();
 }
 
-cudaError_t bs_launch_moe_dispatch(const int* idx, int T, int topk, const int* offsets, int* cursor,
-                                   const uint8_t* xq, const uint8_t* xs, int H, uint8_t* ap, uint32_t* aps32,
-                                   int* pos_of, int* row_token, cudaStream_t st) {
+cudaError_t bs_launch_moe_dispatch(const int* idx, int T, int topk, const int* offsets, const int* chunk_prefix,
+                                   int* cursor, const uint8_t* xq, const uint8_t* xs, int H, uint8_t* ap,
+                                   uint8_t* asp, uint32_t* rows_sc, int* pos_of, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
   const int64_t warps = (int64_t)T * topk;
-  moe::dispatch_kernel<<<(int)((warps * 32 + 255) / 256), 256, 0, st>>>(idx, T, topk, offsets, cursor, xq, xs, H,
-                                                                        ap, aps32, pos_of, row_token);
+  moe::dispatch_kernel<<<(int)((warps * 32 + 255) / 256), 256, 0, st>>>(idx, T, topk, offsets, chunk_prefix, cursor,
+                                                                        xq, xs, H, ap, asp, rows_sc, pos_of);
   return cudaGetLastError();
 }
+
+cudaError_t bs_launch_moe_pack_scales(const uint8_t* ws, int64_t E, int rows, int K, uint8_t* out, cudaStream_t st) {
+  const int64_t words = E * (rows / 128) * (K / 128) * 128;
+  if (words == 0) return cudaSuccess;
+  int64_t blocks = (words + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  moe::pack_scales_kernel<<<(int)blocks, 256, 0, st>>>(ws, E, rows, K, out);
+  return cudaGetLastError();
+}
+
+// Upper bound on the number of token chunks over E experts and `rows` rows.
+int64_t bs_moe_max_chunks(int64_t rows, int E) { return rows / moe::kTok + E; }
 
 cudaError_t bs_launch_moe_combine(const __nv_bfloat16* y, const int* pos_of, const float* w, int T, int topk, int H,
                                   __nv_bfloat16* out, cudaStream_t st) {
@@ -636,9 +692,9 @@ cudaError_t bs_launch_moe_combine(const __nv_bfloat16* y, const int* pos_of, con
 
 // Grouped expert FFN over expert-sorted rows: h = SwiGLU(W13 . a) quantised,
 // y = W2 . h.  rows = capacity of the row buffers (>= offsets[E]).
-int bs_launch_moe_experts(int E, int64_t rows, int H, int I, const uint8_t* ap, const uint32_t* aps32,
-                          const int* offsets, const int* chunk_prefix, const void* w13, const uint8_t* w13_s,
-                          const void* w2, const uint8_t* w2_s, const int* y_rowmap, uint8_t* hq, uint32_t* hs32,
+int bs_launch_moe_experts(int E, int64_t rows, int H, int I, const uint8_t* ap, const uint8_t* asp,
+                          const int* offsets, const int* chunk_prefix, const void* w13, const uint8_t* w13_sp,
+                          const void* w2, const uint8_t* w2_sp, const int* y_rowmap, uint8_t* hq, uint8_t* hs_p,
                           __nv_bfloat16* y, cudaStream_t st, cudaError_t* cerr) {
   *cerr = cudaSuccess;
   if (rows == 0) return 0;
@@ -648,28 +704,27 @@ int bs_launch_moe_experts(int E, int64_t rows, int H, int I, const uint8_t* ap, 
     return BS_ERR_UNSUPPORTED;
   moe::GemmArgs a1 = {};
   a1.E = E; a1.K = H; a1.n_tiles = I / 128; a1.w_rows = 2 * I; a1.up_off = I;
-  a1.offsets = offsets; a1.chunk_prefix = chunk_prefix; a1.w_s = w13_s; a1.a_s32 = aps32;
-  a1.hq = hq; a1.hs32 = hs32; a1.I = I; a1.y = nullptr; a1.H = H;
+  a1.offsets = offsets; a1.chunk_prefix = chunk_prefix; a1.w_sp = w13_sp; a1.a_sp = asp;
+  a1.hq = hq; a1.hs_p = hs_p; a1.I = I; a1.y = nullptr; a1.H = H;
   *cerr = moe::launch_grouped<true>(mw1, ma1, a1, st);
   if (*cerr != cudaSuccess) return BS_ERR_CUDA;
   moe::GemmArgs a2 = {};
   a2.E = E; a2.K = I; a2.n_tiles = H / 128; a2.w_rows = H; a2.up_off = 0;
-  a2.offsets = offsets; a2.chunk_prefix = chunk_prefix; a2.w_s = w2_s; a2.a_s32 = hs32;
-  a2.hq = nullptr; a2.hs32 = nullptr; a2.I = I; a2.y = y; a2.H = H; a2.y_rowmap = y_rowmap;
+  a2.offsets = offsets; a2.chunk_prefix = chunk_prefix; a2.w_sp = w2_sp; a2.a_sp = hs_p;
+  a2.hq = nullptr; a2.hs_p = nullptr; a2.I = I; a2.y = y; a2.H = H; a2.y_rowmap = y_rowmap;
   *cerr = moe::launch_grouped<false>(mw2, ma2, a2, st);
   return *cerr == cudaSuccess ? 0 : BS_ERR_CUDA;
 }
 
 cudaError_t bs_launch_moe_regroup(const int* cnt, int S, int E, int64_t capacity, const uint8_t* rows_in,
-                                  const uint32_t* sc_in, int H, uint8_t* rows_out, uint32_t* sc_out, int* rowmap,
+                                  const uint32_t* sc_in, int H, uint8_t* rows_out, uint8_t* asp, int* rowmap,
                                   int* offsets, int* chunk_prefix, int* scratch, cudaStream_t st) {
   int* src_off = scratch;               // [S*E + 1]
   int* dst_off = scratch + S * E + 1;   // [S*E]
   moe::regroup_plan_kernel<<<1, 1024, 0, st>>>(cnt, S, E, src_off, dst_off, offsets, chunk_prefix);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || capacity == 0) return e;
-  moe::regroup_rows_kernel<<<(int)((capacity * 32 + 255) / 256), 256, 0, st>>>(src_off, dst_off, S * E, capacity,
-                                                                               rows_in, sc_in, H, rows_out, sc_out,
-                                                                               rowmap);
+  moe::regroup_rows_kernel<<<(int)((capacity * 32 + 255) / 256), 256, 0, st>>>(
+      src_off, dst_off, S * E, E, offsets, chunk_prefix, capacity, rows_in, sc_in, H, rows_out, asp, rowmap);
   return cudaGetLastError();
 }

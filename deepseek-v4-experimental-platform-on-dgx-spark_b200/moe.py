@@ -21,7 +21,40 @@ import torch
 
 from . import _lib
 
-__all__ = ["moe_forward", "MoEWorkspace"]
+__all__ = ["moe_forward", "MoEWeights", "MoEWorkspace", "pack_scales"]
+
+
+def pack_scales(w_s: torch.Tensor) -> torch.Tensor:
+    """ue8m0 weight scales [E, rows, K/32] -> the packed tcgen05 chunk layout
+    [E][rows/128][K/128][512 B] (same byte count), once at weight-load time."""
+    E, rows, kq = w_s.shape
+    src = w_s.contiguous().view(torch.uint8)
+    out = torch.empty(E * rows * kq, dtype=torch.uint8, device=w_s.device)
+    _lib.check(_lib.load().bs_moe_pack_scales(src.data_ptr(), E, rows, kq * 32, out.data_ptr(),
+                                              torch.cuda.current_stream(w_s.device).cuda_stream))
+    return out
+
+
+class MoEWeights:
+    """One MoE layer's expert weights in kernel-native form.
+
+    w13 [E, 2I, H/2] and w2 [E, H, I/2] stay as given (packed e2m1 bytes);
+    their ue8m0 scales are re-laid out once by :func:`pack_scales`.
+    """
+
+    def __init__(self, w13: torch.Tensor, w13_s: torch.Tensor, w2: torch.Tensor, w2_s: torch.Tensor):
+        if not (w13.is_cuda and w2.is_cuda):
+            raise RuntimeError("MoEWeights must live on a CUDA device")
+        self.E, two_i, h_half = w13.shape
+        self.I, self.H = two_i // 2, h_half * 2
+        if tuple(w2.shape) != (self.E, self.H, self.I // 2):
+            raise ValueError(f"w2 shape {tuple(w2.shape)} does not match w13 {tuple(w13.shape)}")
+        if tuple(w13_s.shape) != (self.E, two_i, self.H // 32) or tuple(w2_s.shape) != (self.E, self.H, self.I // 32):
+            raise ValueError("scale shapes do not match the weights")
+        self.w13 = w13.contiguous().view(torch.uint8)
+        self.w2 = w2.contiguous().view(torch.uint8)
+        self.w13_sp = pack_scales(w13_s)
+        self.w2_sp = pack_scales(w2_s)
 
 
 class MoEWorkspace:
@@ -49,29 +82,25 @@ def _u8(t: torch.Tensor) -> torch.Tensor:
     return t.contiguous().view(torch.uint8)
 
 
-def moe_forward(x: torch.Tensor, logits: torch.Tensor, w13: torch.Tensor, w13_s: torch.Tensor, w2: torch.Tensor,
-                w2_s: torch.Tensor, topk: int, out: torch.Tensor | None = None,
-                workspace: torch.Tensor | None = None) -> torch.Tensor:
+def moe_forward(x: torch.Tensor, logits: torch.Tensor, weights: MoEWeights, topk: int,
+                out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
     """MoE layer: x bf16 [T, H], logits fp32 [T, E] -> bf16 [T, H]."""
-    if not (x.is_cuda and logits.is_cuda and w13.is_cuda and w2.is_cuda):
+    if not (x.is_cuda and logits.is_cuda):
         raise RuntimeError("moe_forward runs on CUDA tensors only (no CPU fallback)")
     T, H = x.shape
     E = logits.shape[1]
-    I = w2.shape[2] * 2
     if x.dtype != torch.bfloat16 or logits.dtype != torch.float32:
         raise TypeError("moe_forward expects bf16 activations and fp32 logits")
-    if tuple(w13.shape) != (E, 2 * I, H // 2) or tuple(w2.shape) != (E, H, I // 2):
-        raise ValueError(f"moe_forward: weight shapes {tuple(w13.shape)} / {tuple(w2.shape)} do not match "
-                         f"E={E}, H={H}, I={I}")
+    if (E, H) != (weights.E, weights.H):
+        raise ValueError(f"moe_forward: x/logits ({H}, {E}) do not match the weights ({weights.H}, {weights.E})")
     if out is None:
         out = torch.empty(T, H, dtype=torch.bfloat16, device=x.device)
     if workspace is None:
-        workspace = _WS.get(x.device, T, H, I, E, topk)
+        workspace = _WS.get(x.device, T, H, weights.I, E, topk)
     lib = _lib.load()
     xc, lc = x.contiguous(), logits.contiguous()
-    w13u, w13s, w2u, w2s = _u8(w13), _u8(w13_s), _u8(w2), _u8(w2_s)
-    _lib.check(lib.bs_moe_forward(xc.data_ptr(), lc.data_ptr(), T, H, I, E, topk, w13u.data_ptr(),
-                                  w13s.data_ptr(), w2u.data_ptr(), w2s.data_ptr(), out.data_ptr(),
-                                  workspace.data_ptr(), workspace.numel(),
+    _lib.check(lib.bs_moe_forward(xc.data_ptr(), lc.data_ptr(), T, H, weights.I, E, topk, weights.w13.data_ptr(),
+                                  weights.w13_sp.data_ptr(), weights.w2.data_ptr(), weights.w2_sp.data_ptr(),
+                                  out.data_ptr(), workspace.data_ptr(), workspace.numel(),
                                   torch.cuda.current_stream(x.device).cuda_stream))
     return out

@@ -113,46 +113,61 @@ int bs_fp4_gemm(const void* a, const void* a_s, int as_dtype, const void* b, con
  * code, external to the reference; described in DevHistory.md:557, 754):
  * for every expert, act_quant + fp4_gemm(W1) + fp4_gemm(W3), SwiGLU,
  * act_quant + fp4_gemm(W2), weighted sum over the top-k experts.
- * Weights: w13 [E, 2I, H/2] packed e2m1 (rows [0,I) = W1, [I,2I) = W3) with
- * ue8m0 scales w13_s [E, 2I, H/32]; w2 [E, H, I/2] with w2_s [E, H, I/32].
+ * Weights: w13 [E, 2I, H/2] packed e2m1 (rows [0,I) = W1, [I,2I) = W3);
+ * w2 [E, H, I/2].  Their ue8m0 1x32 scales ([E, 2I, H/32], [E, H, I/32]) are
+ * converted once, at weight-load time, by bs_moe_pack_scales into the
+ * tcgen05 scale-chunk layout the kernels fetch with bulk copies.
  * Activations are quantised with power-of-two (ue8m0) 1x128 scales.
  * ------------------------------------------------------------------------ */
+
+/* Weight scales [E, rows, K/32] (ue8m0 bytes) -> packed [E][rows/128][K/128][512]
+ * (same byte count).  rows and K multiples of 128. */
+int bs_moe_pack_scales(const void* w_s, int64_t E, int rows, int K, void* out, void* stream);
 
 /* Bytes of workspace bs_moe_forward needs (0 if the sizes are unsupported). */
 size_t bs_moe_workspace_size(int64_t T, int H, int I, int E, int topk);
 
 /* Whole layer on one GPU: x bf16 [T,H], gate logits fp32 [T,E] -> out bf16
- * [T,H].  Routing: top-k logits, weights = softmax over the k selected. */
+ * [T,H].  Routing: top-k logits, weights = softmax over the k selected.
+ * w13_sp / w2_sp are the packed scales from bs_moe_pack_scales. */
 int bs_moe_forward(const void* x, const float* logits, int64_t T, int H, int I, int E, int topk, const void* w13,
-                   const void* w13_s, const void* w2, const void* w2_s, void* out, void* workspace,
+                   const void* w13_sp, const void* w2, const void* w2_sp, void* out, void* workspace,
                    size_t workspace_bytes, void* stream);
 
 /* Building blocks (expert-parallel form; the caller moves rows between
  * ranks).  route: idx/w [T,topk], counts [E] (zeroed, then filled). */
 int bs_moe_route(const float* logits, int64_t T, int E, int topk, int* idx, float* w, int* counts, void* stream);
 
-/* counts [E] -> offsets [E+1], chunk_prefix [E+1] (128-token chunks), cursor [E] = 0 */
+/* counts [E] -> offsets [E+1], chunk_prefix [E+1] (<=112-token chunks), cursor [E] = 0 */
 int bs_moe_scan(const int* counts, int E, int* offsets, int* chunk_prefix, int* cursor, void* stream);
 
-/* expert-sorted copy of quantised token rows: xq e4m3 [T,H], xs ue8m0 [T,H/128]
- * -> rows [T*topk, H], row_scales u32 [T*topk, H/128] (ue8m0 byte x4),
- * pos_of [T,topk] = row of each (token, slot). */
-int bs_moe_dispatch(const int* idx, int64_t T, int topk, const int* offsets, int* cursor, const void* xq,
-                    const void* xs, int H, void* rows, void* row_scales, int* pos_of, void* stream);
+/* Chunks of packed activation scales to allocate for `rows` rows over E
+ * experts: each chunk takes (K/128)*512 bytes. */
+int64_t bs_moe_chunk_capacity(int64_t rows, int E);
 
-/* receive side: rows grouped by (source, expert) with recv_counts [n_src, E]
- * -> expert-major rows/scales, rowmap [capacity] (expert-major row -> arrival
- * row), offsets/chunk_prefix [E+1]; scratch holds 2*n_src*E+1 ints. */
+/* Expert-sorted copy of quantised token rows: xq e4m3 [T,H], xs ue8m0
+ * [T,H/128] -> rows [T*topk, H]; scales packed per chunk into rows_sp
+ * ([chunks][H/128][512]) and/or row-major into rows_sc (u32 [T*topk, H/128],
+ * the ue8m0 byte replicated x4); pos_of [T,topk] = row of each (token, slot). */
+int bs_moe_dispatch(const int* idx, int64_t T, int topk, const int* offsets, const int* chunk_prefix, int* cursor,
+                    const void* xq, const void* xs, int H, void* rows, void* rows_sp, void* rows_sc, int* pos_of,
+                    void* stream);
+
+/* Receive side of the expert-parallel exchange: rows grouped by (source,
+ * expert) with recv_counts [n_src, E] and row-major scales (u32 x4) ->
+ * expert-major rows, packed scales rows_sp, rowmap [capacity] (expert-major
+ * row -> arrival row), offsets / chunk_prefix [E+1]; scratch: 2*n_src*E+1 ints. */
 int bs_moe_regroup(const int* recv_counts, int n_src, int E, int64_t capacity, const void* rows_in,
-                   const void* scales_in, int H, void* rows_out, void* scales_out, int* rowmap, int* offsets,
+                   const void* scales_in, int H, void* rows_out, void* rows_sp, int* rowmap, int* offsets,
                    int* chunk_prefix, int* scratch, void* stream);
 
-/* grouped expert FFN over expert-sorted rows: hq e4m3 [cap, I], hs u32
- * [cap, I/128] (quantised SwiGLU output), y bf16 [cap, H]; y row r is written
- * to y_rowmap[r] when y_rowmap is not NULL. */
-int bs_moe_experts(int E, int64_t capacity, int H, int I, const void* rows, const void* row_scales,
-                   const int* offsets, const int* chunk_prefix, const void* w13, const void* w13_s, const void* w2,
-                   const void* w2_s, const int* y_rowmap, void* hq, void* hs, void* y, void* stream);
+/* Grouped expert FFN over expert-sorted rows with packed scales: hq e4m3
+ * [cap, I] and packed hidden scales hs_p ([chunks][I/128][512]) (the
+ * quantised SwiGLU output), y bf16 [cap, H]; y row r goes to y_rowmap[r]
+ * when y_rowmap is not NULL. */
+int bs_moe_experts(int E, int64_t capacity, int H, int I, const void* rows, const void* rows_sp,
+                   const int* offsets, const int* chunk_prefix, const void* w13, const void* w13_sp, const void* w2,
+                   const void* w2_sp, const int* y_rowmap, void* hq, void* hs_p, void* y, void* stream);
 
 /* out[t] = bf16(sum_k w[t,k] * y[pos_of[t,k]]) */
 int bs_moe_combine(const void* y, const int* pos_of, const float* w, int64_t T, int topk, int H, void* out,

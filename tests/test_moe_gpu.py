@@ -31,9 +31,8 @@ def moe_mod():
 
 def run(m, topk):
     mm = moe_mod()
-    E = m["w13"].shape[0]
-    return mm.moe_forward(cuda_bf16(m["x"]), cuda_f32(m["logits"]), cuda_u8(m["w13"]), cuda_u8(m["w13_s"]),
-                          cuda_u8(m["w2"]), cuda_u8(m["w2_s"]), topk)
+    w = mm.MoEWeights(cuda_u8(m["w13"]), cuda_u8(m["w13_s"]), cuda_u8(m["w2"]), cuda_u8(m["w2_s"]))
+    return mm.moe_forward(cuda_bf16(m["x"]), cuda_f32(m["logits"]), w, topk)
 
 
 def check(out, ref, label):
@@ -48,7 +47,7 @@ def test_moe_golden_small(golden):
     check(out, golden["moe/small/out"], "moe golden small")
 
 
-@pytest.mark.parametrize("T,H,inter,E,topk", [(64, 512, 256, 16, 4), (300, 256, 256, 4, 2), (200, 1024, 512, 32, 8)])
+@pytest.mark.parametrize("T,H,inter,E,topk", [(64, 512, 256, 16, 4), (300, 256, 256, 4, 2), (200, 1024, 512, 32, 8), (500, 512, 256, 2, 1)])
 def test_moe_vs_oracle(T, H, inter, E, topk):
     m = cases.moe_case_small(T=T, H=H, inter=inter, E=E, topk=topk, seed=T + E)
     ref = ob.moe_layer(m["x"], m["idx"], m["w"], m["w13"], m["w13_s"], m["w2"], m["w2_s"])
@@ -91,8 +90,9 @@ def test_moe_config4_consistency():
     w13_s = 127 - torch.randint(0, 7, (E, 2 * I, H // 32), generator=g, device=dev, dtype=torch.uint8)
     w2 = torch.randint(0, 256, (E, H, I // 2), generator=g, device=dev, dtype=torch.uint8)
     w2_s = 127 - torch.randint(0, 7, (E, H, I // 32), generator=g, device=dev, dtype=torch.uint8)
-    out = mm.moe_forward(x, logits, w13, w13_s, w2, w2_s, k)
-    out2 = mm.moe_forward(x, logits, w13, w13_s, w2, w2_s, k)
+    wts_dev = mm.MoEWeights(w13, w13_s, w2, w2_s)
+    out = mm.moe_forward(x, logits, wts_dev, k)
+    out2 = mm.moe_forward(x, logits, wts_dev, k)
     torch.cuda.synchronize()
     assert torch.isfinite(out.float()).all()
     assert torch.equal(out, out2)
@@ -113,6 +113,22 @@ def test_moe_config4_consistency():
     e = (torch.linalg.norm(out[tok].float() - ref) / torch.linalg.norm(ref)).item()
     print(f"moe config4 sampled tokens: rel_fro={e:.3e}")
     assert e <= TOL
+
+
+def test_pack_scales_layout():
+    """Packed chunk byte (r%32)*16 + (r/32)*4 + k == scale[row r][kb*4 + k]."""
+    mm = moe_mod()
+    rng = np.random.default_rng(11)
+    E, rows, K = 3, 256, 512
+    ws = rng.integers(0, 256, size=(E, rows, K // 32), dtype=np.uint8)
+    packed = mm.pack_scales(cuda_u8(ws)).cpu().numpy().reshape(E, rows // 128, K // 128, 512)
+    r = np.arange(128)
+    for e in range(E):
+        for t in range(rows // 128):
+            for kb in range(K // 128):
+                for k in range(4):
+                    np.testing.assert_array_equal(packed[e, t, kb, (r % 32) * 16 + (r // 32) * 4 + k],
+                                                  ws[e, t * 128 + r, kb * 4 + k])
 
 
 def test_no_device_error():

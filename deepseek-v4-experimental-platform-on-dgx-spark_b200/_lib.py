@@ -35,6 +35,8 @@ SIGNATURES = {
     "bs_moe_workspace_size": [_i64, _i32, _i32, _i32, _i32],
     "bs_moe_forward": [_c_void_p, _c_void_p, _i64, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p,
                        _c_void_p, _c_void_p, _c_void_p, ctypes.c_size_t, _c_void_p],
+    "bs_moe_forward_noalloc": [_c_void_p, _c_void_p, _i64, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p,
+                               _c_void_p, _c_void_p, _c_void_p, _c_void_p],
     "bs_moe_route": [_c_void_p, _i64, _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p],
     "bs_moe_scan": [_c_void_p, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p],
     "bs_moe_dispatch": [_c_void_p, _i64, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32,

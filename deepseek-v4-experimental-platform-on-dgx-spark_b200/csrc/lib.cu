@@ -5,3 +5,4 @@
 #include "gemm.cu"
 #include "moe.cu"
 #include "capi.cu"
+#include "noalloc.cu"

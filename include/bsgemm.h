@@ -169,6 +169,22 @@ int bs_moe_experts(int E, int64_t capacity, int H, int I, const void* rows, cons
                    const int* offsets, const int* chunk_prefix, const void* w13, const void* w13_sp, const void* w2,
                    const void* w2_sp, const int* y_rowmap, void* hq, void* hs_p, void* y, void* stream);
 
+/* bs_moe_forward for callers that cannot allocate device memory (a host
+ * framework that owns all device memory and exposes no allocator, a plugin
+ * that must not call cudaMalloc, a path that must not synchronise).  Same
+ * inputs and output, no workspace: the scratch is a fixed 64 MiB array in the
+ * library's device image, held by every GPU that loads the library until the
+ * process exits.  Sizes needing more scratch than that are rejected with
+ * BS_ERR_UNSUPPORTED (bs_moe_workspace_size gives the need; hidden 4096,
+ * inter 2048, 256 experts, top-8 fits up to about 500 tokens).  All calls on
+ * a device share the array: calls whose GPU work overlaps race and must be
+ * serialised by the caller.  The first call on each device looks up the
+ * array's device address with that device current; make it before any stream
+ * capture.  This entry point has no counterpart in the reference. */
+int bs_moe_forward_noalloc(const void* x, const float* logits, int64_t T, int H, int I, int E, int topk,
+                           const void* w13, const void* w13_sp, const void* w2, const void* w2_sp, void* out,
+                           void* stream);
+
 /* out[t] = bf16(sum_k w[t,k] * y[pos_of[t,k]]) */
 int bs_moe_combine(const void* y, const int* pos_of, const float* w, int64_t T, int topk, int H, void* out,
                    void* stream);

@@ -297,46 +297,73 @@ def bench_fp4_decode(args, torch, dist, ws, rank, dev):
             "gpu_launches": steps, "clocks": clk}
 
 
-def bench_moe_1gpu(args, torch, dist, ws, rank, dev):
-    """Config-4 MoE layer on one GPU: T=1024, H=4096, I=2048, E=256, top-8."""
-    pkg = __import__("importlib").import_module(PKG)
-    moe = __import__("importlib").import_module(PKG + ".moe")
+def bench_moe(args, torch, dist, ws, rank, dev):
+    """Config-4 MoE layer: T=1024 tokens in total, H=4096, I=2048, E=256, top-8.
+
+    One GPU: the whole layer in one call.  N GPUs: expert parallel -- rank r
+    owns tokens [r*T/N, (r+1)*T/N) and experts [r*E/N, (r+1)*E/N); rows travel
+    to the expert owners and back by NCCL all-to-all (strong scaling: the
+    total batch is fixed).
+    """
+    import importlib
+    moe = importlib.import_module(PKG + ".moe")
     T, H, I, E, k = args.tokens, 4096, 2048, args.experts, 8
+    if T % ws or E % ws:
+        raise SystemExit("tokens and experts must split evenly over the ranks")
     g = torch.Generator(device=dev)
     g.manual_seed(4)
-    x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)        # same on every rank
     logits = torch.randn(T, E, generator=g, device=dev)
-    w13 = torch.randint(0, 256, (E, 2 * I, H // 2), generator=g, device=dev, dtype=torch.uint8)
-    w13_s = 127 - torch.randint(0, 7, (E, 2 * I, H // 32), generator=g, device=dev, dtype=torch.uint8)
-    w2 = torch.randint(0, 256, (E, H, I // 2), generator=g, device=dev, dtype=torch.uint8)
-    w2_s = 127 - torch.randint(0, 7, (E, H, I // 32), generator=g, device=dev, dtype=torch.uint8)
-    out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    El, tl = E // ws, T // ws
+    g.manual_seed(1000 + rank)                                                  # this rank's experts
+    w13 = torch.randint(0, 256, (El, 2 * I, H // 2), generator=g, device=dev, dtype=torch.uint8)
+    w13_s = 127 - torch.randint(0, 7, (El, 2 * I, H // 32), generator=g, device=dev, dtype=torch.uint8)
+    w2 = torch.randint(0, 256, (El, H, I // 2), generator=g, device=dev, dtype=torch.uint8)
+    w2_s = 127 - torch.randint(0, 7, (El, H, I // 32), generator=g, device=dev, dtype=torch.uint8)
     weights = moe.MoEWeights(w13, w13_s, w2, w2_s)
+    xl, ll = x[rank * tl:(rank + 1) * tl].contiguous(), logits[rank * tl:(rank + 1) * tl].contiguous()
+    out = torch.empty(tl, H, dtype=torch.bfloat16, device=dev)
+    if ws == 1:
+        def step():
+            moe.moe_forward(xl, ll, weights, k, out=out)
+        launches = 8
+    else:
+        ep = importlib.import_module(PKG + ".ep")
+        layer = ep.EPMoE(weights, E, k, max_tokens=tl)
+
+        def step():
+            layer.forward(xl, ll, out=out)
+        launches = 9
     for _ in range(args.warmup):
-        moe.moe_forward(x, logits, weights, k, out=out)
+        step()
     torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
     clocks = Clocks(torch.cuda.current_device())
     clocks.start()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
     for _ in range(args.steps):
-        moe.moe_forward(x, logits, weights, k, out=out)
+        step()
     t1.record()
     torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
     clk = clocks.stop()
-    ms = t0.elapsed_time(t1) / args.steps
-    wbytes = w13.numel() + w13_s.numel() + w2.numel() + w2_s.numel()
+    ms = max_over_ranks(torch, dist, t0.elapsed_time(t1) / args.steps)
+    wbytes = w13.numel() + w13_s.numel() + w2.numel() + w2_s.numel()          # per rank
     peaks, src = load_peaks()
     gbs = wbytes / (ms * 1e-3) / 1e9
     return {"metric": "MoE-layer tokens/s", "value": round(T / (ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "e4m3 x e2m1", "data": "synthetic",
-            "config": {"workload": f"MoE layer T={T} H={H} I={I} E={E} top-{k}", "parallelism": "none",
-                       "l2": f"weights {wbytes / 2**30:.2f} GiB >> L2"},
+            "config": {"workload": f"MoE layer T={T} H={H} I={I} E={E} top-{k}",
+                       "parallelism": f"ep{ws}" if ws > 1 else "none",
+                       "l2": f"weights {wbytes * ws / 2**30:.2f} GiB >> L2"},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(gbs / peaks["hbm_gbs"], 3), "traffic": None,
-                         "note": "expert weight bytes per layer / layer time", "peak_source": src},
-            "gpu_launches": args.steps * 8, "clocks": clk}
+                         "note": "this rank's expert weight bytes per layer / layer time", "peak_source": src},
+            "gpu_launches": args.steps * launches, "clocks": clk}
 
 
 def max_over_ranks(torch, dist, v):
@@ -423,7 +450,7 @@ def main():
     if args.workload == "fp8_prefill":
         line = bench_fp8_prefill(args, torch, dist, ws, rank, dev)
     elif args.workload == "moe":
-        line = bench_moe_1gpu(args, torch, dist, ws, rank, dev)
+        line = bench_moe(args, torch, dist, ws, rank, dev)
     else:
         line = bench_fp4_decode(args, torch, dist, ws, rank, dev)
 

@@ -40,6 +40,14 @@ struct GemmArgs {
   int kb_per_split;
 };
 
+// c0 += a0 * b, c1 += a1 * b as one packed fp32x2 FMA (sm_100).
+BS_DEVINL void ffma2(float& c0, float& c1, float a0, float a1, float b) {
+  asm("{\n\t.reg .b64 pa, pb, pc;\n\tmov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %4};\n\tmov.b64 pc, {%0, %1};\n\t"
+      "fma.rn.f32x2 pc, pa, pb, pc;\n\tmov.b64 {%0, %1}, pc;\n\t}"
+      : "+f"(c0), "+f"(c1)
+      : "f"(a0), "f"(a1), "f"(b));
+}
+
 BS_DEVINL float load_scale(const void* p, int dtype, int64_t idx) {
   if (dtype == BS_DT_F32) return __ldg(reinterpret_cast<const float*>(p) + idx);
   return bs_e8m0_to_f32(__ldg(reinterpret_cast<const uint8_t*>(p) + idx));
@@ -48,19 +56,28 @@ BS_DEVINL float load_scale(const void* p, int dtype, int64_t idx) {
 template <bool SWAP, bool FP4, int BN>
 struct Cfg {
   static constexpr int kBM = 128;                       // MMA M (rows of X)
-  static constexpr int kBK = 128;                       // K per stage
-  static constexpr int kStages = SWAP ? 4 : (BN == 256 ? 4 : 6);
-  static constexpr int kXBytes = kBM * kBK;             // smem bytes (e2m1 unpacked to 1 B/elem)
-  static constexpr int kYBytes = BN * kBK;
+  // Each pipeline stage carries two 128-wide K blocks, fetched by one 3-D TMA
+  // box per operand: measured L2->SM throughput is ~100 B/clk/SM with two K
+  // blocks per box against ~50-75 with one (per-copy cost dominates).
+  static constexpr int kKps = 2;                        // K blocks per stage
+  static constexpr int kStages = SWAP ? 2 : (BN == 256 ? 2 : 3);
+  static constexpr int kXSub = kBM * 128;               // one K block of X in smem (e2m1 unpacked to 1 B/elem)
+  static constexpr int kYSub = BN * 128;
+  static constexpr int kXBytes = kXSub * kKps;
+  static constexpr int kYBytes = kYSub * kKps;
   static constexpr int kStageBytes = kXBytes + kYBytes;
   static constexpr bool kXFp4 = SWAP && FP4;
   static constexpr bool kYFp4 = !SWAP && FP4;
   static constexpr int kXTx = kXFp4 ? kXBytes / 2 : kXBytes;   // TMA transaction bytes (packed)
   static constexpr int kYTx = kYFp4 ? kYBytes / 2 : kYBytes;
   static constexpr int kSfYBlocks = (BN + 127) / 128;
-  static constexpr int kSfBytes = FP4 ? 512 * (1 + kSfYBlocks) : 0;   // per stage: X chunk + Y chunks
-  static constexpr int kEpiWarps = BN > 128 ? 8 : 4;
-  static constexpr int kCols = BN > 128 ? 128 : BN;     // columns per epilogue warp
+  static constexpr int kSfSub = FP4 ? 512 * (1 + kSfYBlocks) : 0;    // per K block: X chunk + Y chunks
+  static constexpr int kSfBytes = kSfSub * kKps;
+  // normal mode: one epilogue warp per (TMEM lane quadrant, 64-column group),
+  // so BN=256 has 16 epilogue warps, 4 per SM sub-partition, to keep the
+  // per-K-block promotion (TMEM load + FMA of the partial) ahead of the MMA
+  static constexpr int kEpiWarps = SWAP ? 4 : 4 * (BN / 64);
+  static constexpr int kCols = SWAP ? BN : 64;          // columns per epilogue warp
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
   static constexpr int kSfCols = FP4 ? 4 * (1 + kSfYBlocks) : 0;  // TMEM columns per SF slot
   static constexpr int kTmemNeed = 2 * BN + 2 * kSfCols;
@@ -120,13 +137,13 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN>::kThreads, 1)
     // The activation operand's block scales are 1.0 (its fp32 scales are
     // applied in the epilogue): fill its SF chunk once in every stage.
     const int act_chunk = SWAP ? 1 : 0;  // X chunk at 0, Y chunks from 512
-    for (int i = threadIdx.x; i < C::kStages * 128; i += blockDim.x) {
-      const int s = i / 128, w = i % 128;
-      uint32_t* chunk = reinterpret_cast<uint32_t*>(sf_base + s * C::kSfBytes + act_chunk * 512);
+    for (int i = threadIdx.x; i < C::kStages * C::kKps * 128; i += blockDim.x) {
+      const int sub = i / 128, w = i % 128;   // sub = stage * kKps + K block
+      uint32_t* chunk = reinterpret_cast<uint32_t*>(sf_base + sub * C::kSfSub + act_chunk * 512);
       chunk[w] = 0x7F7F7F7Fu;
       if (SWAP && C::kSfYBlocks > 1) {
         for (int b = 1; b < C::kSfYBlocks; ++b)
-          reinterpret_cast<uint32_t*>(sf_base + s * C::kSfBytes + (1 + b) * 512)[w] = 0x7F7F7F7Fu;
+          reinterpret_cast<uint32_t*>(sf_base + sub * C::kSfSub + (1 + b) * 512)[w] = 0x7F7F7F7Fu;
       }
     }
     fence_proxy_async_smem();
@@ -154,22 +171,26 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN>::kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    for (int it = 0; it < n_kb; ++it) {
-      const int s = it % C::kStages;
-      const uint32_t ph = (it / C::kStages) & 1;
+    const int n_st = (n_kb + C::kKps - 1) / C::kKps;
+    for (int st = 0; st < n_st; ++st) {
+      const int s = st % C::kStages;
+      const uint32_t ph = (st / C::kStages) & 1;
       if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1, abort_flag))) break;
-      const int kb = kb_begin + it;
+      const int kb0 = kb_begin + st * C::kKps;
       if (FP4) {
         // weights' per-32 scales: row r of the 128(+)-row operand lands at
         // (r%32)*16 + ((r/32)%4)*4 + (r/128)*512, the tcgen05 scale layout.
-        uint8_t* chunk = sf_base + s * C::kSfBytes + (SWAP ? 0 : 512);
         const int rows = SWAP ? 128 : BN;
         const uint8_t* bs = reinterpret_cast<const uint8_t*>(p.b_s);
         const int64_t ld = p.K / 32;
-        for (int r = lane; r < rows; r += 32) {
-          int n = n0 + r;
-          n = n < p.N ? n : p.N - 1;
-          cp_async_4(chunk + (r % 32) * 16 + ((r / 32) % 4) * 4 + (r / 128) * 512, bs + n * ld + kb * 4);
+        for (int sub = 0; sub < C::kKps; ++sub) {
+          const int kb = kb0 + sub < kb_end ? kb0 + sub : kb_end - 1;
+          uint8_t* chunk = sf_base + (s * C::kKps + sub) * C::kSfSub + (SWAP ? 0 : 512);
+          for (int r = lane; r < rows; r += 32) {
+            int n = n0 + r;
+            n = n < p.N ? n : p.N - 1;
+            cp_async_4(chunk + (r % 32) * 16 + ((r / 32) % 4) * 4 + (r / 128) * 512, bs + n * ld + kb * 4);
+          }
         }
         cp_async_mbar_arrive_noinc(&full[s]);
       }
@@ -177,8 +198,8 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN>::kThreads, 1)
         uint8_t* sx = stage_base + s * C::kStageBytes;
         uint8_t* sy = sx + C::kXBytes;
         mbar_arrive_expect_tx(&full[s], C::kXTx + C::kYTx);
-        tma_load_2d(sx, &tm_x, &full[s], kb * 128, x0);
-        tma_load_2d(sy, &tm_y, &full[s], kb * 128, y0);
+        tma_load_3d(sx, &tm_x, &full[s], 0, x0, kb0);
+        tma_load_3d(sy, &tm_y, &full[s], 0, y0, kb0);
       }
       __syncwarp();
     }
@@ -186,24 +207,25 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN>::kThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     const uint32_t sf_col0 = 2 * BN;
     for (int it = 0; it < n_kb; ++it) {
-      const int s = it % C::kStages;
-      const uint32_t ph = (it / C::kStages) & 1;
+      const int st = it / C::kKps, sub = it % C::kKps;
+      const int s = st % C::kStages;
+      const uint32_t ph = (st / C::kStages) & 1;
       const int buf = it & 1;
       const uint32_t pph = (it >> 1) & 1;
-      bool ok = mbar_wait(&full[s], ph, abort_flag);
+      bool ok = sub != 0 || mbar_wait(&full[s], ph, abort_flag);
       ok = ok && mbar_wait(&pempty[buf], pph ^ 1, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      if (FP4) fence_proxy_async_smem();
+      if (FP4 && sub == 0) fence_proxy_async_smem();
       if (lane == 0) {
-        const uint32_t sx = smem_u32(stage_base + s * C::kStageBytes);
-        const uint32_t sy = sx + C::kXBytes;
+        const uint32_t sx = smem_u32(stage_base + s * C::kStageBytes) + sub * C::kXSub;
+        const uint32_t sy = smem_u32(stage_base + s * C::kStageBytes) + C::kXBytes + sub * C::kYSub;
         const uint32_t d = tmem_base + buf * BN;
         if constexpr (FP4) {
           const uint32_t slot = sf_col0 + (it & 1) * C::kSfCols;
           const uint32_t sfa = tmem_base + slot;
           const uint32_t sfb = tmem_base + slot + 4;
-          const uint32_t sfs = smem_u32(sf_base + s * C::kSfBytes);
+          const uint32_t sfs = smem_u32(sf_base + (s * C::kKps + sub) * C::kSfSub);
           tc_cp_32x128b_warpx4(sfa, sdesc_sf_chunk(sfs));
           for (int b = 0; b < C::kSfYBlocks; ++b) tc_cp_32x128b_warpx4(sfb + 4 * b, sdesc_sf_chunk(sfs + 512 * (1 + b)));
 #pragma unroll
@@ -219,7 +241,7 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN>::kThreads, 1)
           for (int k = 0; k < 4; ++k)
             tc_mma_f8f6f4(d, sdesc_k128_sw128(sx + k * 32), sdesc_k128_sw128(sy + k * 32), idesc, k > 0 ? 1u : 0u);
         }
-        tc_commit(&empty[s]);
+        if (sub == C::kKps - 1 || it == n_kb - 1) tc_commit(&empty[s]);
         tc_commit(&pfull[buf]);
       }
       __syncwarp();
@@ -265,18 +287,23 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN>::kThreads, 1)
       if (!__all_sync(0xffffffffu, mbar_wait(&pfull[buf], pph, abort_flag))) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + buf * BN + col0;
+      // two 16-column TMEM loads per wait, then the FMAs of both
 #pragma unroll
-      for (int c = 0; c < C::kCols / 16; ++c) {
-        uint32_t r[16];
+      for (int c = 0; c < C::kCols / 16; c += 2) {
+        uint32_t r[32];
         BS_TMEM_LD16(taddr + c * 16, r);
+        if (c + 1 < C::kCols / 16) BS_TMEM_LD16(taddr + (c + 1) * 16, (r + 16));
         tmem_ld_wait();
+        const int nj = (c + 1 < C::kCols / 16) ? 32 : 16;
         if constexpr (SWAP) {
           const float* cs = col_scale + it * BN + c * 16;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) acc[c * 16 + j] = fmaf(__uint_as_float(r[j]), rs * cs[j], acc[c * 16 + j]);
+          for (int j = 0; j < 32; ++j)
+            if (j < nj) acc[c * 16 + j] = fmaf(__uint_as_float(r[j]), rs * cs[j], acc[c * 16 + j]);
         } else {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) acc[c * 16 + j] = fmaf(__uint_as_float(r[j]), rs, acc[c * 16 + j]);
+          for (int j = 0; j < 32; j += 2)
+            if (j < nj) ffma2(acc[c * 16 + j], acc[c * 16 + j + 1], __uint_as_float(r[j]), __uint_as_float(r[j + 1]), rs);
         }
       }
       tc_fence_before();
@@ -387,15 +414,17 @@ EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-// 2-D K-major map: inner dim K (elements), outer dim rows; box 128 x box_rows.
+// K-major operand [rows, K] viewed as 3-D (128 K elements, rows, K/128 blocks);
+// one box = 128 x box_rows x 2 K blocks (two 128-byte-row tiles back to back
+// in shared memory).
 bool make_map(CUtensorMap* m, const void* base, bool fp4, int64_t K, int64_t rows, int box_rows) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return false;
-  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)(fp4 ? K / 2 : K)};
-  cuuint32_t box[2] = {128u, (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1u, 1u};
-  CUresult r = enc(m, fp4 ? CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+  cuuint64_t dims[3] = {128u, (cuuint64_t)rows, (cuuint64_t)(K / 128)};
+  cuuint64_t strides[2] = {(cuuint64_t)(fp4 ? K / 2 : K), (cuuint64_t)(fp4 ? 64 : 128)};
+  cuuint32_t box[3] = {128u, (cuuint32_t)box_rows, 2u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = enc(m, fp4 ? CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B : CU_TENSOR_MAP_DATA_TYPE_UINT8, 3,
                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;

@@ -305,6 +305,61 @@ __host__ __device__ constexpr uint32_t idesc_mxf8f6f4(int a_fmt, int b_fmt, int 
 }
 
 // ---------------------------------------------------------------------------
+// 2-SM (CTA pair) forms: one MMA spans the two SMs of a cluster pair.  Each
+// CTA holds half of the A rows and half of the B columns in its own shared
+// memory; the pair's leader (even rank) issues the MMA; accumulator rows
+// live in each CTA's own TMEM.
+// ---------------------------------------------------------------------------
+
+BS_DEVINL void tmem_alloc_pair(uint32_t* smem_result, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_result)),
+               "r"(ncols)
+               : "memory");
+}
+BS_DEVINL void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+BS_DEVINL void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// TMA load into this CTA's shared memory whose completion is counted on the
+// pair leader's mbarrier (bar_cluster: a shared::cluster address).  Not a
+// multicast load: each CTA reads its own tile.
+BS_DEVINL void tma_load_3d_pair(void* smem_dst, const CUtensorMap* map, uint32_t bar_cluster, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+      "%5}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+// D(tmem, both SMs) (+)= A . B^T for a 256 x N tile, e4m3 operands, issued by
+// the pair leader.
+BS_DEVINL void tc_mma_f8f6f4_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accum)
+      : "memory");
+}
+
+// Arrive on the mbarrier at the same shared-memory offset in every CTA of
+// cta_mask once the pair's tcgen05 ops issued so far have completed.
+BS_DEVINL void tc_commit_pair_mc(uint64_t* bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(cta_mask)
+      : "memory");
+}
+
+// Arrive on an mbarrier of another CTA of the cluster (shared::cluster address).
+BS_DEVINL void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+
+// ---------------------------------------------------------------------------
 // thread-block cluster helpers (split-K reduction through DSMEM)
 // ---------------------------------------------------------------------------
 

@@ -26,6 +26,8 @@
 //
 // Every wait is bounded (common.cuh); a stuck pipeline records
 // BS_ERR_DEVICE_TIMEOUT and the CTA exits.
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace {
@@ -472,6 +474,23 @@ cudaError_t launch(const CUtensorMap& mx, const CUtensorMap& my, const GemmArgs&
 
 }  // namespace
 
+int bs_launch_fp8_gemm_pair(const void* a, const void* a_s, int as_dtype, const void* b, const void* b_s,
+                            int bs_dtype, int64_t M, int64_t N, int64_t K, void* c, cudaStream_t st,
+                            cudaError_t* cerr);
+
+// The CTA-pair fp8 kernel (gemm_pair.cu) halves each SM's operand traffic
+// but, with two 256-column TMEM partial buffers, its leader waits on the
+// peer's epilogue every K block; measured at 0.64 PFLOP/s on 4096^3 against
+// 1.25 for the single-SM kernel, so it is opt-in (BS_FP8_GEMM_PAIR=1).
+static bool fp8_pair_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("BS_FP8_GEMM_PAIR");
+    v = (e && e[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
+}
+
 // Returns 0 on success, BS_ERR_UNSUPPORTED if a tensor map could not be
 // built, or BS_ERR_CUDA with the CUDA error in *cerr.
 int bs_launch_gemm(bool fp4, const void* a, const void* a_s, int as_dtype, const void* b, const void* b_s,
@@ -510,6 +529,8 @@ int bs_launch_gemm(bool fp4, const void* a, const void* a_s, int as_dtype, const
       if (bn == 16) BS_DEC(false, 16); else if (bn == 32) BS_DEC(false, 32); else BS_DEC(false, 64);
     }
 #undef BS_DEC
+  } else if (!fp4 && fp8_pair_enabled()) {
+    return bs_launch_fp8_gemm_pair(a, a_s, as_dtype, b, b_s, bs_dtype, M, N, K, c, st, cerr);
   } else {
     const int bn = fp4 ? 128 : 256;
     if (!make_map(&mx, a, false, K, M, 128) || !make_map(&my, b, fp4, K, N, bn)) return BS_ERR_UNSUPPORTED;

@@ -113,3 +113,27 @@ def test_gemm_leading_dims(pkg):
 
 def test_no_device_error(pkg):
     pkg._lib.device_error_check()
+
+
+def test_fp8_pair_kernel_parity():
+    """The opt-in CTA-pair fp8 kernel (BS_FP8_GEMM_PAIR=1) against the oracle,
+    run in a child process so the switch is read fresh."""
+    import os
+    import subprocess
+    import sys
+    code = (
+        "import sys, numpy as np, torch, importlib; sys.path[:0] = [%r, %r]\n"
+        "import cases\nfrom oracle import blockscaled as ob\nfrom conftest import rel_fro\n"
+        "from gpu_util import bits, cuda_u8, cuda_f32\n"
+        "pkg = importlib.import_module('deepseek-v4-experimental-platform-on-dgx-spark_b200')\n"
+        "for (M, N, K) in [(256, 512, 1024), (300, 200, 384), (4096, 4096, 4096)]:\n"
+        "    c = cases.cfg2_fp8(M=M, N=N, K=K, seed=M + N)\n"
+        "    out = pkg.fp8_gemm(cuda_u8(c['a'], torch.float8_e4m3fn), cuda_f32(c['a_s']),\n"
+        "                       cuda_u8(c['b'], torch.float8_e4m3fn), cuda_f32(c['b_s']))\n"
+        "    o = bits(out)[::64]; r = ob.fp8_gemm(c['a'], c['a_s'], c['b'], c['b_s'])[::64]\n"
+        "    e = rel_fro(o, r); print(M, N, K, e); assert e <= 1e-2\n"
+    ) % (os.path.join(os.path.dirname(__file__), "golden"), os.path.dirname(__file__))
+    env = dict(os.environ, BS_FP8_GEMM_PAIR="1")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
+    print(r.stdout, r.stderr[-2000:])
+    assert r.returncode == 0

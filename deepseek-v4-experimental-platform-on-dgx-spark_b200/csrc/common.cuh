@@ -360,6 +360,34 @@ BS_DEVINL void mbar_arrive_cluster(uint32_t bar_cluster) {
 }
 
 // ---------------------------------------------------------------------------
+// The lowest lane of a converged warp, chosen with elect.sync.  tcgen05 and
+// TMA issue blocks guarded by it (rather than by `lane == 0`) keep their
+// operands on the uniform datapath: a K-block loop issuing four M=128 MMAs
+// ran at ~147 cycles per MMA under `lane == 0` against ~115 (N=16) and ~129
+// (N=256, the tensor-pipe rate) under elect.sync on B200.  Every lane of the
+// warp must reach the call; with the whole warp converged it is lane 0, so
+// MMAs and the commits that track them come from the same thread.
+// ---------------------------------------------------------------------------
+
+BS_DEVINL bool elect_one() {
+  uint32_t pred;
+  asm volatile("{\n\t.reg .pred P1;\n\telect.sync _|P1, 0xffffffff;\n\tselp.b32 %0, 1, 0, P1;\n\t}" : "=r"(pred));
+  return pred != 0;
+}
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialisation may start while the previous kernel in the stream is still
+// running; griddepcontrol.wait blocks the calling thread until that kernel
+// has completed and its memory is visible.  Everything that reads data a
+// previous kernel may produce, or writes data it may still read, comes after
+// the wait; static weights can be streamed before it.
+// ---------------------------------------------------------------------------
+
+BS_DEVINL void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+BS_DEVINL void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
 // thread-block cluster helpers (split-K reduction through DSMEM)
 // ---------------------------------------------------------------------------
 

@@ -62,7 +62,7 @@ struct Cfg {
   // box per operand: measured L2->SM throughput is ~100 B/clk/SM with two K
   // blocks per box against ~50-75 with one (per-copy cost dominates).
   static constexpr int kKps = 2;                        // K blocks per stage
-  static constexpr int kStages = SWAP ? 2 : (BN == 256 ? 2 : 3);
+  static constexpr int kStages = SWAP ? 4 : (BN == 256 ? 2 : 3);
   static constexpr int kXSub = kBM * 128;               // one K block of X in smem (e2m1 unpacked to 1 B/elem)
   static constexpr int kYSub = BN * 128;
   static constexpr int kXBytes = kXSub * kKps;
@@ -82,7 +82,11 @@ struct Cfg {
   static constexpr int kCols = SWAP ? BN : 64;          // columns per epilogue warp
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
   static constexpr int kSfCols = FP4 ? 4 * (1 + kSfYBlocks) : 0;  // TMEM columns per SF slot
-  static constexpr int kTmemNeed = 2 * BN + 2 * kSfCols;
+  // TMEM partial buffers: normal mode double-buffers its wide tile; the
+  // narrow decode tile keeps 4-8 so the MMA runs through a whole split-K
+  // range without waiting for the per-K-block promotion.
+  static constexpr int kPBufs = SWAP ? (BN <= 32 ? 8 : 4) : 2;
+  static constexpr int kTmemNeed = kPBufs * BN + 2 * kSfCols;
   static constexpr int kTmemCols = kTmemNeed <= 32 ? 32 : kTmemNeed <= 64 ? 64 : kTmemNeed <= 128 ? 128
                                    : kTmemNeed <= 256 ? 256 : 512;
   static_assert(kTmemNeed <= 512, "TMEM budget");
@@ -105,8 +109,8 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN>::kThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(tail);
   uint64_t* empty = full + C::kStages;
   uint64_t* pfull = empty + C::kStages;
-  uint64_t* pempty = pfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pempty + 2);
+  uint64_t* pempty = pfull + C::kPBufs;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pempty + C::kPBufs);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -128,7 +132,7 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN>::kThreads, 1)
       mbar_init(&full[s], 1 + (FP4 ? 32 : 0));
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < C::kPBufs; ++b) {
       mbar_init(&pfull[b], 1);
       mbar_init(&pempty[b], C::kEpiWarps);
     }
@@ -158,26 +162,26 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN>::kThreads, 1)
     tma_prefetch_desc(&tm_x);
     tma_prefetch_desc(&tm_y);
   }
-  // swap mode: fp32 column scales (one per token) for every K block of this split
-  if (SWAP) {
-    for (int i = threadIdx.x; i < n_kb * BN; i += blockDim.x) {
-      const int kbl = i / BN, j = i % BN;
-      const int m = m0 + j;
-      col_scale[kbl * BN + j] = m < p.M ? load_scale(p.a_s, p.as_dtype, (int64_t)m * num_kb_total + kb_begin + kbl) : 0.0f;
-    }
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_launch_dependents();
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
+    // The first stages' weight tiles (and their scales) are requested before
+    // griddepcontrol.wait -- weights are never written by a previous kernel --
+    // so the weight stream overlaps the tail of the previous kernel; the
+    // activation tiles follow once it has finished.
     const int n_st = (n_kb + C::kKps - 1) / C::kKps;
-    for (int st = 0; st < n_st; ++st) {
-      const int s = st % C::kStages;
-      const uint32_t ph = (st / C::kStages) & 1;
-      if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1, abort_flag))) break;
+    const int n_pre = n_st < C::kStages ? n_st : C::kStages;
+    const CUtensorMap* tm_w = SWAP ? &tm_x : &tm_y;
+    const CUtensorMap* tm_act = SWAP ? &tm_y : &tm_x;
+    const int w_row = SWAP ? x0 : y0, act_row = SWAP ? y0 : x0;
+    constexpr int kWOff = SWAP ? 0 : C::kXBytes;       // weights' offset inside a stage
+    constexpr int kActOff = SWAP ? C::kXBytes : 0;
+    auto issue_weights = [&](int st, int s) {
       const int kb0 = kb_begin + st * C::kKps;
       if (FP4) {
         // weights' per-32 scales: row r of the 128(+)-row operand lands at
@@ -196,30 +200,44 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN>::kThreads, 1)
         }
         cp_async_mbar_arrive_noinc(&full[s]);
       }
-      if (lane == 0) {
-        uint8_t* sx = stage_base + s * C::kStageBytes;
-        uint8_t* sy = sx + C::kXBytes;
+      __syncwarp();
+      if (elect_one()) {
         mbar_arrive_expect_tx(&full[s], C::kXTx + C::kYTx);
-        tma_load_3d(sx, &tm_x, &full[s], 0, x0, kb0);
-        tma_load_3d(sy, &tm_y, &full[s], 0, y0, kb0);
+        tma_load_3d(stage_base + s * C::kStageBytes + kWOff, tm_w, &full[s], 0, w_row, kb0);
       }
+    };
+    auto issue_act = [&](int st, int s) {
+      if (elect_one())
+        tma_load_3d(stage_base + s * C::kStageBytes + kActOff, tm_act, &full[s], 0, act_row, kb_begin + st * C::kKps);
+    };
+    for (int st = 0; st < n_pre; ++st) issue_weights(st, st);   // the ring starts empty
+    if (lane == 0) pdl_wait();
+    __syncwarp();
+    for (int st = 0; st < n_pre; ++st) issue_act(st, st);
+    __syncwarp();
+    for (int st = n_pre; st < n_st; ++st) {
+      const int s = st % C::kStages;
+      const uint32_t ph = (st / C::kStages) & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1, abort_flag))) break;
+      issue_weights(st, s);
+      issue_act(st, s);
       __syncwarp();
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    const uint32_t sf_col0 = 2 * BN;
+    const uint32_t sf_col0 = C::kPBufs * BN;
     for (int it = 0; it < n_kb; ++it) {
       const int st = it / C::kKps, sub = it % C::kKps;
       const int s = st % C::kStages;
       const uint32_t ph = (st / C::kStages) & 1;
-      const int buf = it & 1;
-      const uint32_t pph = (it >> 1) & 1;
+      const int buf = it % C::kPBufs;
+      const uint32_t pph = (it / C::kPBufs) & 1;
       bool ok = sub != 0 || mbar_wait(&full[s], ph, abort_flag);
       ok = ok && mbar_wait(&pempty[buf], pph ^ 1, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
       if (FP4 && sub == 0) fence_proxy_async_smem();
-      if (lane == 0) {
+      if (elect_one()) {
         const uint32_t sx = smem_u32(stage_base + s * C::kStageBytes) + sub * C::kXSub;
         const uint32_t sy = smem_u32(stage_base + s * C::kStageBytes) + C::kXBytes + sub * C::kYSub;
         const uint32_t d = tmem_base + buf * BN;
@@ -280,10 +298,22 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN>::kThreads, 1)
       return 1.0f;
     };
 
+    // activation scales and the output may belong to the previous kernel
+    pdl_wait();
+    if (SWAP) {
+      // fp32 column scales (one per token) for every K block of this split
+      for (int i = threadIdx.x - 64; i < n_kb * BN; i += 32 * C::kEpiWarps) {
+        const int kbl = i / BN, j = i % BN;
+        const int m = m0 + j;
+        col_scale[kbl * BN + j] =
+            m < p.M ? load_scale(p.a_s, p.as_dtype, (int64_t)m * num_kb_total + kb_begin + kbl) : 0.0f;
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(32 * C::kEpiWarps) : "memory");
+    }
     float rs_next = n_kb > 0 ? row_scale(kb_begin) * blk_scale(kb_begin) : 0.0f;
     for (int it = 0; it < n_kb; ++it) {
-      const int buf = it & 1;
-      const uint32_t pph = (it >> 1) & 1;
+      const int buf = it % C::kPBufs;
+      const uint32_t pph = (it / C::kPBufs) & 1;
       const float rs = rs_next;
       if (it + 1 < n_kb) rs_next = row_scale(kb_begin + it + 1) * blk_scale(kb_begin + it + 1);
       if (!__all_sync(0xffffffffu, mbar_wait(&pfull[buf], pph, abort_flag))) break;
@@ -459,17 +489,54 @@ cudaError_t launch(const CUtensorMap& mx, const CUtensorMap& my, const GemmArgs&
   cfg.blockDim = dim3(C::kThreads, 1, 1);
   cfg.dynamicSmemBytes = C::kSmemBytes;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  cfg.numAttrs = 0;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   if (split > 1) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = split;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = split;
+    cfg.numAttrs = 2;
   }
   return cudaLaunchKernelEx(&cfg, kern, mx, my, a);
+}
+
+// Co-resident clusters of `split` swap-mode CTAs (cached per configuration).
+template <bool FP4, int BN>
+int max_clusters_t(int split) {
+  static int cache[9] = {0};
+  if (cache[split]) return cache[split];
+  using C = Cfg<true, FP4, BN>;
+  auto kern = bsg_kernel<true, FP4, BN>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1, 1, split);
+  cfg.blockDim = dim3(C::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = split;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    n = num_sms() / split;
+  }
+  cache[split] = n;
+  return n;
+}
+
+int max_clusters(bool fp4, int bn, int split) {
+  if (fp4) return bn == 16 ? max_clusters_t<true, 16>(split) : bn == 32 ? max_clusters_t<true, 32>(split)
+                                                                        : max_clusters_t<true, 64>(split);
+  return bn == 16 ? max_clusters_t<false, 16>(split) : bn == 32 ? max_clusters_t<false, 32>(split)
+                                                               : max_clusters_t<false, 64>(split);
 }
 
 }  // namespace
@@ -513,10 +580,14 @@ int bs_launch_gemm(bool fp4, const void* a, const void* a_s, int as_dtype, const
     if (!make_map(&mx, b, fp4, K, N, 128) || !make_map(&my, a, false, K, M, bn)) return BS_ERR_UNSUPPORTED;
     const int x_tiles = (int)((N + 127) / 128);
     const int y_tiles = (int)((M + bn - 1) / bn);
+    // Largest split-K (2..8, a thread-block cluster along K) whose clusters
+    // all fit on the GPU at once, so the grid runs in one wave; at least two
+    // K blocks per CTA.
     int split = 1;
-    const int slots = 2 * num_sms();
-    while (split < 8 && x_tiles * y_tiles * split * 2 <= slots && nkb % (split * 2) == 0 && nkb / (split * 2) >= 2)
-      split *= 2;
+    for (int sp = 8; sp >= 2; sp /= 2) {
+      if (nkb % sp || nkb / sp < 2) continue;
+      if (x_tiles * y_tiles <= max_clusters(fp4, bn, sp)) { split = sp; break; }
+    }
     // the column scales of one split are cached in shared memory (32 K blocks)
     while (split < 8 && (nkb + split - 1) / split > 32) split *= 2;
     args.kb_per_split = (nkb + split - 1) / split;

@@ -95,7 +95,7 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
       const int s = st % C::kStages;
       const uint32_t ph = (st / C::kStages) & 1;
       if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1, abort_flag))) break;
-      if (lane == 0) {
+      if (elect_one()) {
         uint8_t* sa = stage_base + s * C::kStageBytes;
         uint8_t* sb = sa + C::kXBytes;
         if (leader) mbar_arrive_expect_tx(&full[s], 2 * C::kStageBytes);
@@ -123,7 +123,7 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
         ok = ok && mbar_wait(&pempty[buf], pph ^ 1, abort_flag);
         if (!__all_sync(0xffffffffu, ok)) break;
         tc_fence_after();
-        if (lane == 0) {
+        if (elect_one()) {
           const uint64_t da = da0 + (uint64_t)s * kStageStep + (uint64_t)sub * kSubStep;
           const uint64_t db = da0 + (uint64_t)s * kStageStep + kBOff + (uint64_t)sub * kSubStep;
           const uint32_t d = tmem_base + buf * C::kN;

@@ -419,7 +419,7 @@ __global__ void __launch_bounds__(192, 1)
         const int s = it % C::kStages;
         const uint32_t ph = (it / C::kStages) & 1;
         if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1, abort_flag))) { ok = false; break; }
-        if (lane == 0) {
+        if (elect_one()) {
           uint8_t* sx = stage_base + s * C::kStageBytes;
           uint8_t* sy = sx + C::kXBytes;
           uint8_t* sf = sf_base + s * C::kSfBytes;
@@ -462,7 +462,7 @@ __global__ void __launch_bounds__(192, 1)
         const uint32_t ph = (it / C::kStages) & 1;
         if (!__all_sync(0xffffffffu, mbar_wait(&full[s], ph, abort_flag))) { ok = false; break; }
         tc_fence_after();
-        if (lane == 0) {
+        if (elect_one()) {
           const uint64_t dx = dx0 + (uint64_t)s * kStageStep;
           const uint64_t dy = dx + kYOff;
           const uint64_t dsf = dsf0 + (uint64_t)s * kSfStep;
@@ -485,7 +485,7 @@ __global__ void __launch_bounds__(192, 1)
         __syncwarp();
       }
       if (!ok) break;
-      if (lane == 0) tc_commit(&acc_full[buf]);
+      if (elect_one()) tc_commit(&acc_full[buf]);
       __syncwarp();
     }
   } else {

@@ -145,6 +145,28 @@ BS_DEVINL bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-suspending probe of an mbarrier phase.
+BS_DEVINL bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded spin on an mbarrier whose phase completes through remote
+// transaction bytes (st.async from peer CTAs).  test_wait polls without
+// suspending the thread; a suspended try_wait was measured to wake
+// microseconds after such a phase completed.
+BS_DEVINL bool mbar_spin(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < BS_SPIN_LIMIT; ++i)
+    if (mbar_test_wait(bar, parity)) return true;
+  bs_set_error(BS_ERR_DEVICE_TIMEOUT);
+  return false;
+}
+
 // Bounded wait.  Returns false (and records the error) after BS_SPIN_LIMIT
 // polls, or as soon as *abort is set by another role of the same CTA.
 BS_DEVINL bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
@@ -162,6 +184,7 @@ BS_DEVINL bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
 BS_DEVINL void cp_async_4(void* smem_dst, const void* gmem_src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
 }
+BS_DEVINL void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 BS_DEVINL void cp_async_mbar_arrive_noinc(uint64_t* bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -403,6 +426,26 @@ BS_DEVINL uint32_t mapa_shared(uint32_t smem_addr, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
   return r;
+}
+// Split cluster barrier: arrive once every thread has initialised what its
+// peers will touch, wait before the first access to a peer's shared memory.
+BS_DEVINL void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+BS_DEVINL void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+// 16-byte store into a peer CTA's shared memory that completes as
+// transaction bytes on the peer's mbarrier (both shared::cluster addresses).
+BS_DEVINL void st_async_f4(uint32_t addr, float a, float b, float c, float d, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(addr),
+               "f"(a), "f"(b), "f"(c), "f"(d), "r"(bar)
+               : "memory");
+}
+// Shared-memory load by 32-bit shared address.  Buffers carved out of the
+// 1 KB-aligned dynamic shared memory are generic pointers to the compiler;
+// generic loads issued after generic global stores wait for those stores, so
+// loops that interleave the two read shared memory through this instead.
+BS_DEVINL float4 ld_shared_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+  return v;
 }
 BS_DEVINL float4 ld_shared_cluster_f4(uint32_t addr) {
   float4 v;

@@ -72,28 +72,43 @@ struct Cfg {
   static constexpr bool kYFp4 = !SWAP && FP4;
   static constexpr int kXTx = kXFp4 ? kXBytes / 2 : kXBytes;   // TMA transaction bytes (packed)
   static constexpr int kYTx = kYFp4 ? kYBytes / 2 : kYBytes;
+  // fp4 block scales: the weights' per-32 ue8m0 scales come with every K
+  // block (512-byte chunks in the tcgen05 scale layout, one per 128 rows);
+  // the activations' block scales are all 1.0 (their fp32 scales are applied
+  // in the epilogue), so one constant chunk set serves every K block.
   static constexpr int kSfYBlocks = (BN + 127) / 128;
-  static constexpr int kSfSub = FP4 ? 512 * (1 + kSfYBlocks) : 0;    // per K block: X chunk + Y chunks
-  static constexpr int kSfBytes = kSfSub * kKps;
+  static constexpr int kWChunks = SWAP ? 1 : kSfYBlocks;          // weights' chunks per K block
+  static constexpr int kAChunks = SWAP ? kSfYBlocks : 1;          // constant activation chunks
+  static constexpr int kSfSub = FP4 ? 512 * kWChunks : 0;         // per K block
+  static constexpr int kSfBytes = kSfSub * kKps;                  // per stage
+  static constexpr int kSfConst = FP4 ? 512 * kAChunks : 0;
   // normal mode: one epilogue warp per (TMEM lane quadrant, 64-column group),
   // so BN=256 has 16 epilogue warps, 4 per SM sub-partition, to keep the
   // per-K-block promotion (TMEM load + FMA of the partial) ahead of the MMA
   static constexpr int kEpiWarps = SWAP ? 4 : 4 * (BN / 64);
   static constexpr int kCols = SWAP ? BN : 64;          // columns per epilogue warp
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
-  static constexpr int kSfCols = FP4 ? 4 * (1 + kSfYBlocks) : 0;  // TMEM columns per SF slot
+  static constexpr int kSfWCols = FP4 ? 4 * kWChunks : 0;   // TMEM columns per weights' SF slot (2 slots)
+  static constexpr int kSfACols = FP4 ? 4 * kAChunks : 0;   // TMEM columns of the constant activation SF
   // TMEM partial buffers: normal mode double-buffers its wide tile; the
   // narrow decode tile keeps 4-8 so the MMA runs through a whole split-K
   // range without waiting for the per-K-block promotion.
   static constexpr int kPBufs = SWAP ? (BN <= 32 ? 8 : 4) : 2;
-  static constexpr int kTmemNeed = kPBufs * BN + 2 * kSfCols;
+  static constexpr int kTmemNeed = kPBufs * BN + 2 * kSfWCols + kSfACols;
   static constexpr int kTmemCols = kTmemNeed <= 32 ? 32 : kTmemNeed <= 64 ? 64 : kTmemNeed <= 128 ? 128
                                    : kTmemNeed <= 256 ? 256 : 512;
   static_assert(kTmemNeed <= 512, "TMEM budget");
-  static constexpr int kMaxKbSmem = 32;                 // swap mode: column scales cached in smem
-  static constexpr int kColScaleBytes = SWAP ? BN * kMaxKbSmem * 4 : 0;
-  static constexpr int kSmemBytes = 1024 /*align slack*/ + kStages * (kStageBytes + kSfBytes) + kColScaleBytes + 256;
-  static_assert(!SWAP || kStages * kStageBytes >= kBM * BN * 4, "reduction buffer reuses the stage ring");
+  // Shared memory: [align slack | operand ring | SF ring | constant SF |
+  // column scales | receive buffer | barriers].  The last two variable parts
+  // are sized per launch (smem_bytes): swap mode caches the fp32 column
+  // scales of its K range ([kb_per_split][BN]) and, under split-K, receives
+  // the partial rows pushed by the other S-1 CTAs of its cluster
+  // ([S-1][128/S rows][BN] fp32).
+  static constexpr int kTailBytes = 256;
+  static constexpr int kFixedBytes = 1024 + kStages * (kStageBytes + kSfBytes) + kSfConst + kTailBytes;
+  static constexpr int smem_bytes(int split, int kb_per_split) {
+    return kFixedBytes + (SWAP ? kb_per_split * BN * 4 + (split - 1) * (kBM / split) * BN * 4 : 0);
+  }
 };
 
 template <bool SWAP, bool FP4, int BN>
@@ -101,16 +116,22 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN>::kThreads, 1)
     bsg_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_y, GemmArgs p) {
   using C = Cfg<SWAP, FP4, BN>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1 KB alignment by offsetting smem_raw itself, so that every buffer
+  // carved from it stays in the shared address space for the compiler
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* stage_base = smem;
   uint8_t* sf_base = smem + C::kStages * C::kStageBytes;
-  float* col_scale = reinterpret_cast<float*>(sf_base + C::kStages * C::kSfBytes);
-  uint8_t* tail = reinterpret_cast<uint8_t*>(col_scale) + C::kColScaleBytes;
+  uint8_t* sf_const = sf_base + C::kStages * C::kSfBytes;
+  float* col_scale = reinterpret_cast<float*>(sf_const + C::kSfConst);
+  float* recv = col_scale + (SWAP ? p.kb_per_split * BN : 0);
+  const int n_peers = (int)gridDim.z - 1;
+  uint8_t* tail = reinterpret_cast<uint8_t*>(recv + (SWAP ? n_peers * (C::kBM / (int)gridDim.z) * BN : 0));
   uint64_t* full = reinterpret_cast<uint64_t*>(tail);
   uint64_t* empty = full + C::kStages;
   uint64_t* pfull = empty + C::kStages;
   uint64_t* pempty = pfull + C::kPBufs;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pempty + C::kPBufs);
+  uint64_t* recv_bar = pempty + C::kPBufs;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -136,22 +157,17 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN>::kThreads, 1)
       mbar_init(&pfull[b], 1);
       mbar_init(&pempty[b], C::kEpiWarps);
     }
+    mbar_init(recv_bar, 1);
     *abort_flag = 0;
     fence_barrier_init();
+    // split-K: the bytes the other CTAs of the cluster push into this one
+    if (gridDim.z > 1)
+      mbar_arrive_expect_tx(recv_bar, (uint32_t)((gridDim.z - 1) * (C::kBM / gridDim.z) * BN * 4));
   }
   if (FP4) {
-    // The activation operand's block scales are 1.0 (its fp32 scales are
-    // applied in the epilogue): fill its SF chunk once in every stage.
-    const int act_chunk = SWAP ? 1 : 0;  // X chunk at 0, Y chunks from 512
-    for (int i = threadIdx.x; i < C::kStages * C::kKps * 128; i += blockDim.x) {
-      const int sub = i / 128, w = i % 128;   // sub = stage * kKps + K block
-      uint32_t* chunk = reinterpret_cast<uint32_t*>(sf_base + sub * C::kSfSub + act_chunk * 512);
-      chunk[w] = 0x7F7F7F7Fu;
-      if (SWAP && C::kSfYBlocks > 1) {
-        for (int b = 1; b < C::kSfYBlocks; ++b)
-          reinterpret_cast<uint32_t*>(sf_base + sub * C::kSfSub + (1 + b) * 512)[w] = 0x7F7F7F7Fu;
-      }
-    }
+    // the constant activation block scales (ue8m0 1.0)
+    for (int i = threadIdx.x; i < C::kSfConst / 4; i += blockDim.x)
+      reinterpret_cast<uint32_t*>(sf_const)[i] = 0x7F7F7F7Fu;
     fence_proxy_async_smem();
   }
   if (warp == 1) {
@@ -165,6 +181,7 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN>::kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if (gridDim.z > 1) cluster_arrive();   // receive barriers are initialised
   pdl_launch_dependents();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -181,6 +198,17 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN>::kThreads, 1)
     const int w_row = SWAP ? x0 : y0, act_row = SWAP ? y0 : x0;
     constexpr int kWOff = SWAP ? 0 : C::kXBytes;       // weights' offset inside a stage
     constexpr int kActOff = SWAP ? C::kXBytes : 0;
+    // The weights' scales are gathered with cp.async (generic proxy) and read
+    // by tcgen05.cp (async proxy): each lane waits for its own gathers and
+    // fences before its arrive on full[s], so the MMA issuer needs no proxy
+    // fence.  The prefetched stages share one wait.
+    auto sf_publish = [&](int s0, int n) {
+      if (FP4) {
+        cp_async_wait_all();
+        fence_proxy_async_smem();
+        for (int i = 0; i < n; ++i) mbar_arrive(&full[s0 + i]);
+      }
+    };
     auto issue_weights = [&](int st, int s) {
       const int kb0 = kb_begin + st * C::kKps;
       if (FP4) {
@@ -191,14 +219,13 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN>::kThreads, 1)
         const int64_t ld = p.K / 32;
         for (int sub = 0; sub < C::kKps; ++sub) {
           const int kb = kb0 + sub < kb_end ? kb0 + sub : kb_end - 1;
-          uint8_t* chunk = sf_base + (s * C::kKps + sub) * C::kSfSub + (SWAP ? 0 : 512);
+          uint8_t* chunk = sf_base + (s * C::kKps + sub) * C::kSfSub;
           for (int r = lane; r < rows; r += 32) {
             int n = n0 + r;
             n = n < p.N ? n : p.N - 1;
             cp_async_4(chunk + (r % 32) * 16 + ((r / 32) % 4) * 4 + (r / 128) * 512, bs + n * ld + kb * 4);
           }
         }
-        cp_async_mbar_arrive_noinc(&full[s]);
       }
       __syncwarp();
       if (elect_one()) {
@@ -211,6 +238,7 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN>::kThreads, 1)
         tma_load_3d(stage_base + s * C::kStageBytes + kActOff, tm_act, &full[s], 0, act_row, kb_begin + st * C::kKps);
     };
     for (int st = 0; st < n_pre; ++st) issue_weights(st, st);   // the ring starts empty
+    sf_publish(0, n_pre);
     if (lane == 0) pdl_wait();
     __syncwarp();
     for (int st = 0; st < n_pre; ++st) issue_act(st, st);
@@ -221,11 +249,19 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN>::kThreads, 1)
       if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1, abort_flag))) break;
       issue_weights(st, s);
       issue_act(st, s);
+      sf_publish(s, 1);
       __syncwarp();
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    const uint32_t sf_col0 = C::kPBufs * BN;
+    const uint32_t sfw_col0 = C::kPBufs * BN;                  // two slots of the weights' scales
+    const uint32_t sfa_col = sfw_col0 + 2 * C::kSfWCols;        // constant activation scales
+    if (FP4) {
+      if (elect_one())
+        for (int b = 0; b < C::kAChunks; ++b)
+          tc_cp_32x128b_warpx4(tmem_base + sfa_col + 4 * b, sdesc_sf_chunk(smem_u32(sf_const) + 512 * b));
+      __syncwarp();
+    }
     for (int it = 0; it < n_kb; ++it) {
       const int st = it / C::kKps, sub = it % C::kKps;
       const int s = st % C::kStages;
@@ -236,18 +272,17 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN>::kThreads, 1)
       ok = ok && mbar_wait(&pempty[buf], pph ^ 1, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      if (FP4 && sub == 0) fence_proxy_async_smem();
       if (elect_one()) {
         const uint32_t sx = smem_u32(stage_base + s * C::kStageBytes) + sub * C::kXSub;
         const uint32_t sy = smem_u32(stage_base + s * C::kStageBytes) + C::kXBytes + sub * C::kYSub;
         const uint32_t d = tmem_base + buf * BN;
         if constexpr (FP4) {
-          const uint32_t slot = sf_col0 + (it & 1) * C::kSfCols;
-          const uint32_t sfa = tmem_base + slot;
-          const uint32_t sfb = tmem_base + slot + 4;
+          const uint32_t wslot = tmem_base + sfw_col0 + (it & 1) * C::kSfWCols;
           const uint32_t sfs = smem_u32(sf_base + (s * C::kKps + sub) * C::kSfSub);
-          tc_cp_32x128b_warpx4(sfa, sdesc_sf_chunk(sfs));
-          for (int b = 0; b < C::kSfYBlocks; ++b) tc_cp_32x128b_warpx4(sfb + 4 * b, sdesc_sf_chunk(sfs + 512 * (1 + b)));
+          for (int b = 0; b < C::kWChunks; ++b) tc_cp_32x128b_warpx4(wslot + 4 * b, sdesc_sf_chunk(sfs + 512 * b));
+          // X is the weights in swap mode, the activations otherwise
+          const uint32_t sfa = SWAP ? wslot : tmem_base + sfa_col;
+          const uint32_t sfb = SWAP ? tmem_base + sfa_col : wslot;
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const uint32_t idesc =
@@ -296,6 +331,27 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN>::kThreads, 1)
         return load_scale(p.b_s, p.bs_dtype, (int64_t)(n / 128) * nkb_all + kb);
       }
       return 1.0f;
+    };
+
+    // swap mode: write a staged bf16 tile [BN][rows] (rows consecutive
+    // weight rows from n_base, a multiple of 8) to C[m, n] in 16-byte chunks
+    // along n, shared by all epilogue threads
+    auto write_tile = [&](const __nv_bfloat16* tile, int rows, int n_base) {
+      const int cpm = rows / 8;
+      const bool vec = (p.N % 8) == 0 && (reinterpret_cast<uintptr_t>(p.c) & 15) == 0;
+      for (int c = threadIdx.x - 64; c < BN * cpm; c += 32 * C::kEpiWarps) {
+        const int j = c / cpm, ch = c - j * cpm;
+        const int m = y0 + j, n = n_base + ch * 8;
+        if (m >= p.M) continue;
+        const __nv_bfloat16* src = tile + j * rows + ch * 8;
+        __nv_bfloat16* dst = p.c + (int64_t)m * p.N + n;
+        if (vec && n + 8 <= p.N) {
+          *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+        } else {
+          for (int u = 0; u < 8; ++u)
+            if (n + u < p.N) dst[u] = src[u];
+        }
+      }
     };
 
     // activation scales and the output may belong to the previous kernel
@@ -366,57 +422,65 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN>::kThreads, 1)
           }
         }
       } else {
-        const int n = x0 + row;
-        if (n < p.N) {
+        // the operand ring is idle once the last partial has been read:
+        // stage the bf16 tile there, transposed, and write it out in
+        // 16-byte row chunks
+        __nv_bfloat16* tile = reinterpret_cast<__nv_bfloat16*>(stage_base);
 #pragma unroll
-          for (int j = 0; j < BN; ++j) {
-            const int m = y0 + j;
-            if (m < p.M) p.c[(int64_t)m * p.N + n] = __float2bfloat16_rn(acc[j]);
-          }
-        }
+        for (int j = 0; j < BN; ++j) tile[j * C::kBM + row] = __float2bfloat16_rn(acc[j]);
+        asm volatile("bar.sync 1, %0;" ::"r"(32 * C::kEpiWarps) : "memory");
+        write_tile(tile, C::kBM, x0);
       }
-    } else {
-      // split-K: park the fp32 tile in this CTA's (now idle) stage ring
-      float* red = reinterpret_cast<float*>(stage_base);
-#pragma unroll
-      for (int j = 0; j < C::kCols; j += 4)
-        *reinterpret_cast<float4*>(red + row * BN + col0 + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
-    }
-  }
-
-  if (gridDim.z > 1) {
-    // every thread of every CTA in the cluster takes part in both barriers
-    __syncthreads();
-    cluster_sync();
-    if (SWAP && warp >= 2) {
+    } else if (SWAP) {
+      // split-K across the cluster: the 128 weight rows are divided among
+      // the S CTAs.  Each CTA pushes the partial rows it does not own into
+      // the owner's receive buffer (st.async, completing as transaction
+      // bytes on the owner's recv_bar) and sums the rows it owns in rank
+      // order, so no CTA reads another's shared memory and none waits for a
+      // peer to finish reading its own.
       const int S = gridDim.z;
-      const int rank = (int)cluster_ctarank();
+      const int me = (int)cluster_ctarank();
       const int rows_per = C::kBM / S;
-      const int t = threadIdx.x - 64;
-      const int nthr = blockDim.x - 64;
-      const uint32_t red_local = smem_u32(stage_base);
-      // this CTA reduces rows [rank*rows_per, (rank+1)*rows_per) over all S tiles
-      for (int e = t; e < rows_per * (BN / 4); e += nthr) {
-        const int rr = rank * rows_per + e % rows_per;
-        const int j4 = (e / rows_per) * 4;
-        float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int q = 0; q < S; ++q) {
-          float4 v = ld_shared_cluster_f4(mapa_shared(red_local + (uint32_t)(rr * BN + j4) * 4, q));
-          sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
-        }
-        const int n = x0 + rr;
-        if (n < p.N) {
-          const float vals[4] = {sum.x, sum.y, sum.z, sum.w};
+      const int owner = row / rows_per;
+      const int rl = row - owner * rows_per;
+      // the owner's receive buffer has one slot per peer (ranks other than
+      // the owner, in rank order); the summed rows are staged in this CTA's
+      // operand ring, idle once its last partial has been read
+      __nv_bfloat16* tile = reinterpret_cast<__nv_bfloat16*>(stage_base);
+      cluster_wait();
+      if (owner != me) {
+        const int slot = me < owner ? me : me - 1;
+        const uint32_t dst = mapa_shared(smem_u32(recv + (slot * rows_per + rl) * BN), (uint32_t)owner);
+        const uint32_t bar = mapa_shared(smem_u32(recv_bar), (uint32_t)owner);
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int m = y0 + j4 + u;
-            if (m < p.M) p.c[(int64_t)m * p.N + n] = __float2bfloat16_rn(vals[u]);
+        for (int j = 0; j < BN; j += 4) st_async_f4(dst + j * 4, acc[j], acc[j + 1], acc[j + 2], acc[j + 3], bar);
+      } else {
+        // every peer always pushes (also after an abort), so this wait does
+        // not take the abort flag: the CTA must not exit while peers write
+        // into its shared memory
+        mbar_spin(recv_bar, 0);
+        const uint32_t rbase = smem_u32(recv) + (uint32_t)(rl * BN) * 4u;
+#pragma unroll
+        for (int j = 0; j < BN; j += 4) {
+          float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int q = 0; q < S; ++q) {
+            const int slot = q < me ? q : q - 1;
+            const float4 v = q == me ? make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3])
+                                     : ld_shared_f4(rbase + (uint32_t)(slot * rows_per * BN + j) * 4u);
+            t.x += v.x; t.y += v.y; t.z += v.z; t.w += v.w;
           }
+          tile[(j + 0) * rows_per + rl] = __float2bfloat16_rn(t.x);
+          tile[(j + 1) * rows_per + rl] = __float2bfloat16_rn(t.y);
+          tile[(j + 2) * rows_per + rl] = __float2bfloat16_rn(t.z);
+          tile[(j + 3) * rows_per + rl] = __float2bfloat16_rn(t.w);
         }
       }
+      asm volatile("bar.sync 1, %0;" ::"r"(32 * C::kEpiWarps) : "memory");
+      write_tile(tile, rows_per, x0 + me * rows_per);
     }
-    cluster_sync();
   }
+  __syncwarp();
+  if (gridDim.z > 1 && warp < 2) cluster_wait();
 
   tc_fence_before();
   __syncthreads();
@@ -472,22 +536,40 @@ int num_sms() {
   return g_num_sms;
 }
 
+int max_dyn_smem() {
+  static int v = 0;
+  if (!v) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  }
+  return v;
+}
+
+template <bool SWAP, bool FP4, int BN>
+cudaError_t prepare_kernel() {
+  static bool done = false;
+  if (!done) {
+    auto kern = bsg_kernel<SWAP, FP4, BN>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, max_dyn_smem());
+    if (e != cudaSuccess) return e;
+    if (SWAP) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    done = true;
+  }
+  return cudaSuccess;
+}
+
 template <bool SWAP, bool FP4, int BN>
 cudaError_t launch(const CUtensorMap& mx, const CUtensorMap& my, const GemmArgs& a, dim3 grid, int split,
                    cudaStream_t st) {
   using C = Cfg<SWAP, FP4, BN>;
   auto kern = bsg_kernel<SWAP, FP4, BN>;
-  static bool attr_done = false;
-  if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
-    if (e != cudaSuccess) return e;
-    if (SWAP) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    attr_done = true;
-  }
+  cudaError_t e = prepare_kernel<SWAP, FP4, BN>();
+  if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(C::kThreads, 1, 1);
-  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.dynamicSmemBytes = C::smem_bytes(split, a.kb_per_split);
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -511,11 +593,11 @@ int max_clusters_t(int split) {
   if (cache[split]) return cache[split];
   using C = Cfg<true, FP4, BN>;
   auto kern = bsg_kernel<true, FP4, BN>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  prepare_kernel<true, FP4, BN>();
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(1, 1, split);
   cfg.blockDim = dim3(C::kThreads, 1, 1);
-  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.dynamicSmemBytes = C::smem_bytes(split, 1);   // one CTA per SM at any split
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
@@ -530,6 +612,18 @@ int max_clusters_t(int split) {
   }
   cache[split] = n;
   return n;
+}
+
+// Does a swap-mode launch with this split fit in shared memory?
+bool decode_smem_fits(bool fp4, int bn, int split, int kb_per_split) {
+  int need;
+  if (fp4) need = bn == 16 ? Cfg<true, true, 16>::smem_bytes(split, kb_per_split)
+                : bn == 32 ? Cfg<true, true, 32>::smem_bytes(split, kb_per_split)
+                           : Cfg<true, true, 64>::smem_bytes(split, kb_per_split);
+  else need = bn == 16 ? Cfg<true, false, 16>::smem_bytes(split, kb_per_split)
+              : bn == 32 ? Cfg<true, false, 32>::smem_bytes(split, kb_per_split)
+                         : Cfg<true, false, 64>::smem_bytes(split, kb_per_split);
+  return need <= max_dyn_smem();
 }
 
 int max_clusters(bool fp4, int bn, int split) {
@@ -588,10 +682,14 @@ int bs_launch_gemm(bool fp4, const void* a, const void* a_s, int as_dtype, const
       if (nkb % sp || nkb / sp < 2) continue;
       if (x_tiles * y_tiles <= max_clusters(fp4, bn, sp)) { split = sp; break; }
     }
-    // the column scales of one split are cached in shared memory (32 K blocks)
-    while (split < 8 && (nkb + split - 1) / split > 32) split *= 2;
+    // shared memory holds the column scales of a split's K range and the
+    // receive buffer of the split-K reduction: the first shrinks with the
+    // split, the second grows with it
+    auto fits = [&](int sp) { return decode_smem_fits(fp4, bn, sp, (nkb + sp - 1) / sp); };
+    while (split > 1 && !fits(split)) split /= 2;
+    while (!fits(split) && split < 8 && nkb % (2 * split) == 0) split *= 2;
+    if (!fits(split)) return BS_ERR_UNSUPPORTED;
     args.kb_per_split = (nkb + split - 1) / split;
-    if (args.kb_per_split > 32) return BS_ERR_UNSUPPORTED;
     dim3 grid(x_tiles, y_tiles, split);
 #define BS_DEC(F, B) *cerr = launch<true, F, B>(mx, my, args, grid, split, st)
     if (fp4) {

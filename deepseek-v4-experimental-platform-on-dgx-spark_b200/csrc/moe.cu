@@ -340,7 +340,9 @@ __global__ void __launch_bounds__(192, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a, GemmArgs p) {
   using C = Cfg<PAIRED>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1 KB alignment by offsetting smem_raw itself, so that every buffer
+  // carved from it stays in the shared address space for the compiler
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* stage_base = smem;
   uint8_t* sf_base = smem + C::kStages * C::kStageBytes;
   int* s_off = reinterpret_cast<int*>(sf_base + C::kStages * C::kSfBytes);

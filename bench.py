@@ -143,13 +143,29 @@ def bench_fp8_prefill(args, torch, dist, ws, rank, dev):
     full = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
     lib = pkg._lib.load()
     stream = torch.cuda.current_stream()
+    # N > 1: the GEMM epilogue stores every tile into all ranks' C over NVLink
+    # (fused), or the shard is gathered afterwards with NCCL (nccl)
+    fused = ws > 1 and args.tp_gather == "fused"
+    tpg = None
+    if fused:
+        tpg = __import__("importlib").import_module(PKG + ".tp").TPGemm(M, N, K, device=dev)
 
     def gemm(i, out):
         a, a_s, b, s = shards[i % n_sets]
+        if fused:
+            # the fused kernel alone (no barrier): timing of the GEMM + peer stores
+            pkg._lib.check(lib.bs_fp8_gemm_allgather(
+                a.data_ptr(), a_s.data_ptr(), pkg._lib.DT_F32, b.data_ptr(), s.data_ptr(), pkg._lib.DT_F32,
+                M, n_local, K, tpg.ptrs[i & 1], ws, N, tpg.col0, stream.cuda_stream))
+            return
         pkg._lib.check(lib.bs_fp8_gemm(a.data_ptr(), a_s.data_ptr(), pkg._lib.DT_F32, b.data_ptr(), s.data_ptr(),
                                        pkg._lib.DT_F32, M, n_local, K, out.data_ptr(), stream.cuda_stream))
 
     def step(i):
+        if fused:
+            a, a_s, b, s = shards[i % n_sets]
+            tpg(a, a_s, b, s)
+            return
         out = outs[i & 1]
         gemm(i, out)
         if ws > 1:
@@ -199,6 +215,9 @@ def bench_fp8_prefill(args, torch, dist, ws, rank, dev):
     def e2e_step():
         x_dev.copy_(x_host, non_blocking=True)
         a, a_s = pkg.act_quant(x_dev, 128)
+        if fused:
+            o_host.copy_(tpg(a, a_s, b_loc, s_loc), non_blocking=True)
+            return
         c = pkg.fp8_gemm(a, a_s, b_loc, s_loc)
         if ws > 1:
             dist.all_gather_into_tensor(gathered, c)
@@ -219,10 +238,26 @@ def bench_fp8_prefill(args, torch, dist, ws, rank, dev):
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(torch, dist, e0.elapsed_time(e1) / args.steps)
 
+    if tpg is not None:
+        torch.cuda.synchronize()
+        pkg._lib.device_error_check()
+        tpg.close()
     peaks, src = load_peaks()
     peak = 2.0 * peaks["bf16_tflops"]  # dense e4m3 rate = 2x the measured dense bf16 rate
     local_flops = 2.0 * M * n_local * K
     achieved = local_flops / (kern_ms * 1e-3) / 1e12
+    nvlink = None
+    if fused:
+        # fused GEMM + all-gather: the kernel cannot beat the slower of its math
+        # at the tensor peak and the gathered bytes it must receive (and send)
+        # over NVLink at the measured 770 GB/s per direction
+        gathered_bytes = (ws - 1) * M * n_local * 2
+        t_math = local_flops / (peak * 1e12)
+        t_link = gathered_bytes / 770e9
+        peak = local_flops / max(t_math, t_link) / 1e12
+        nvlink = {"bytes_per_gpu": gathered_bytes, "gbs_per_direction": 770.0,
+                  "target_ms": round(max(t_math, t_link) * 1e3, 4),
+                  "bound_by": "nvlink" if t_link > t_math else "tensor"}
     traffic = None
     tfile = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tfile):
@@ -233,7 +268,9 @@ def bench_fp8_prefill(args, torch, dist, ws, rank, dev):
         "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong" if ws > 1 else "weak",
         "vs_baseline": None, "dtype": "e4m3", "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights)",
-        "config": {"workload": f"fp8_gemm M=N=K={M}" + (f", column-sharded TP{ws} + all-gather" if ws > 1 else ""),
+        "config": {"workload": f"fp8_gemm M=N=K={M}" + (
+                       (f", column-sharded TP{ws}, all-gather fused into the GEMM epilogue (NVLink peer stores)"
+                        if fused else f", column-sharded TP{ws} + NCCL all-gather") if ws > 1 else ""),
                    "M": M, "N": N, "K": K, "parallelism": f"tp{ws}" if ws > 1 else "none",
                    "l2": f"{n_sets} rotating input sets ({n_sets * (M * K + n_local * K) // 2**20} MiB) > L2"},
         "e2e": {"value": round(flops / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
@@ -241,9 +278,13 @@ def bench_fp8_prefill(args, torch, dist, ws, rank, dev):
                 "ms_per_step": round(e2e_ms, 4), "path": "act_quant + fp8_gemm public API, pinned host I/O"},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 3), "traffic": traffic,
-                     "kernel": "bsg_kernel<normal,fp8,BN=256>", "kernel_ms": round(kern_ms, 4),
-                     "peak_source": f"2 x bf16_tflops of {src} MEASURED_PEAKS.json (dense e4m3 rate)"},
-        "gpu_launches": args.steps * (1 if ws == 1 else 1),
+                     "kernel": "bsg_kernel<normal,fp8,BN=256>" + (" + peer stores" if fused else ""),
+                     "kernel_ms": round(kern_ms, 4),
+                     "peak_source": f"2 x bf16_tflops of {src} MEASURED_PEAKS.json (dense e4m3 rate)"
+                                    + ("; min with NVLink 770 GB/s per direction for the gathered bytes"
+                                       if fused else ""),
+                     "nvlink": nvlink},
+        "gpu_launches": args.steps * (2 if fused else 1),
         "clocks": clk,
     }
     return line
@@ -439,6 +480,8 @@ def main():
     ap.add_argument("--m", type=int, default=16)
     ap.add_argument("--n", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tp-gather", choices=["fused", "nccl"], default="fused",
+                    help="fp8_prefill at N>1: all-gather fused into the GEMM epilogue, or NCCL after it")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     ws, rank, local = dist_env()

@@ -9,7 +9,8 @@ cudaError_t bs_launch_act_quant(const void* x, int x_dtype, int64_t rows, int64_
                                 void* s, int s_dtype, bool inplace, cudaStream_t st);
 cudaError_t bs_launch_fp4_act_quant(void* x, int x_dtype, int64_t rows, int64_t K, int bs, cudaStream_t st);
 int bs_launch_gemm(bool fp4, const void* a, const void* a_s, int as_dtype, const void* b, const void* b_s,
-                   int bs_dtype, int64_t M, int64_t N, int64_t K, void* c, cudaStream_t st, cudaError_t* cerr);
+                   int bs_dtype, int64_t M, int64_t N, int64_t K, void* const* c, int n_out, int64_t ldc,
+                   int64_t col0, cudaStream_t st, cudaError_t* cerr);
 cudaError_t bs_launch_moe_route(const float* logits, int T, int E, int topk, int* idx, float* w, int* counts,
                                 cudaStream_t st);
 cudaError_t bs_launch_moe_scan(const int* counts, int E, int* offsets, int* chunk_prefix, int* cursor,
@@ -19,6 +20,8 @@ cudaError_t bs_launch_moe_dispatch(const int* idx, int T, int topk, const int* o
                                    uint8_t* asp, uint32_t* rows_sc, int* pos_of, cudaStream_t st);
 cudaError_t bs_launch_moe_pack_scales(const uint8_t* ws, int64_t E, int rows, int K, uint8_t* out, cudaStream_t st);
 int64_t bs_moe_max_chunks(int64_t rows, int E);
+cudaError_t bs_launch_peer_barrier(void* const* flags, int n_ranks, int rank, unsigned long long epoch,
+                                   cudaStream_t st);
 cudaError_t bs_launch_moe_combine(const __nv_bfloat16* y, const int* pos_of, const float* w, int T, int topk, int H,
                                   __nv_bfloat16* out, cudaStream_t st);
 int bs_launch_moe_experts(int E, int64_t rows, int H, int I, const uint8_t* ap, const uint8_t* asp,
@@ -123,8 +126,8 @@ int bs_fp4_act_quant_inplace(void* x, int x_dtype, int64_t rows, int64_t K, int 
 }
 
 static int gemm_common(bool fp4, const void* a, const void* a_s, int as_dtype, const void* b, const void* b_s,
-                       int bs_dtype, int64_t M, int64_t N, int64_t K, void* c, void* stream) {
-  const char* name = fp4 ? "fp4_gemm" : "fp8_gemm";
+                       int bs_dtype, int64_t M, int64_t N, int64_t K, void* const* c, int n_out, int64_t ldc,
+                       int64_t col0, void* stream, const char* name) {
   if (M < 0 || N <= 0 || K <= 0) return fail(BS_ERR_INVALID_ARG, "%s: bad shape M=%lld N=%lld K=%lld", name, (long long)M, (long long)N, (long long)K);
   if (K % 128 != 0) return fail(BS_ERR_UNSUPPORTED, "%s: K=%lld must be a multiple of 128", name, (long long)K);
   if (M > 0x7fffffff || N > 0x7fffffff || K > 0x7fffffff) return fail(BS_ERR_UNSUPPORTED, "%s: dimension too large", name);
@@ -132,12 +135,19 @@ static int gemm_common(bool fp4, const void* a, const void* a_s, int as_dtype, c
     return fail(BS_ERR_UNSUPPORTED, "%s: a_s dtype tag %d: expected f32 or e8m0", name, as_dtype);
   if (fp4 ? bs_dtype != BS_DT_E8M0 : (bs_dtype != BS_DT_F32 && bs_dtype != BS_DT_E8M0))
     return fail(BS_ERR_UNSUPPORTED, "%s: b_s dtype tag %d not supported", name, bs_dtype);
+  if (n_out < 1 || n_out > 8) return fail(BS_ERR_UNSUPPORTED, "%s: %d output buffers (1..8 supported)", name, n_out);
+  if (col0 < 0 || ldc < col0 + N || col0 > 0x7fffffff)
+    return fail(BS_ERR_INVALID_ARG, "%s: columns [%lld, %lld) do not fit rows of %lld", name, (long long)col0,
+                (long long)(col0 + N), (long long)ldc);
   if (M == 0) return BS_OK;
   if (!a || !a_s || !b || !b_s || !c) return fail(BS_ERR_INVALID_ARG, "%s: null pointer", name);
-  if (!aligned(a, 16) || !aligned(b, fp4 ? 32 : 16) || !aligned(c, 16) || !aligned(a_s, 4) || !aligned(b_s, 4))
-    return fail(BS_ERR_INVALID_ARG, "%s: operand alignment (a,c: 16 B; b: %d B; scales: 4 B)", name, fp4 ? 32 : 16);
+  for (int q = 0; q < n_out; ++q)
+    if (!c[q] || !aligned(c[q], 2)) return fail(BS_ERR_INVALID_ARG, "%s: output buffer %d null or misaligned", name, q);
+  if (!aligned(a, 16) || !aligned(b, fp4 ? 32 : 16) || !aligned(a_s, 4) || !aligned(b_s, 4))
+    return fail(BS_ERR_INVALID_ARG, "%s: operand alignment (a: 16 B; b: %d B; scales: 4 B)", name, fp4 ? 32 : 16);
   cudaError_t ce;
-  int r = bs_launch_gemm(fp4, a, a_s, as_dtype, b, b_s, bs_dtype, M, N, K, c, (cudaStream_t)stream, &ce);
+  int r = bs_launch_gemm(fp4, a, a_s, as_dtype, b, b_s, bs_dtype, M, N, K, c, n_out, ldc, col0,
+                         (cudaStream_t)stream, &ce);
   if (r == BS_ERR_UNSUPPORTED) return fail(r, "%s: could not build TMA descriptors for M=%lld N=%lld K=%lld", name, (long long)M, (long long)N, (long long)K);
   if (r == BS_ERR_CUDA) return cuda_status(ce, name);
   return r;
@@ -145,12 +155,41 @@ static int gemm_common(bool fp4, const void* a, const void* a_s, int as_dtype, c
 
 int bs_fp8_gemm(const void* a, const void* a_s, int as_dtype, const void* b, const void* b_s, int bs_dtype,
                 int64_t M, int64_t N, int64_t K, void* c, void* stream) {
-  return gemm_common(false, a, a_s, as_dtype, b, b_s, bs_dtype, M, N, K, c, stream);
+  if (M > 0 && !aligned(c, 16)) return fail(BS_ERR_INVALID_ARG, "fp8_gemm: c must be 16-byte aligned");
+  return gemm_common(false, a, a_s, as_dtype, b, b_s, bs_dtype, M, N, K, &c, 1, N, 0, stream, "fp8_gemm");
 }
 
 int bs_fp4_gemm(const void* a, const void* a_s, int as_dtype, const void* b, const void* b_s, int bs_dtype,
                 int64_t M, int64_t N, int64_t K, void* c, void* stream) {
-  return gemm_common(true, a, a_s, as_dtype, b, b_s, bs_dtype, M, N, K, c, stream);
+  if (M > 0 && !aligned(c, 16)) return fail(BS_ERR_INVALID_ARG, "fp4_gemm: c must be 16-byte aligned");
+  return gemm_common(true, a, a_s, as_dtype, b, b_s, bs_dtype, M, N, K, &c, 1, N, 0, stream, "fp4_gemm");
+}
+
+int bs_fp8_gemm_allgather(const void* a, const void* a_s, int as_dtype, const void* b, const void* b_s,
+                          int bs_dtype, int64_t M, int64_t N, int64_t K, void* const* c_ranks, int n_ranks,
+                          int64_t ldc, int64_t col0, void* stream) {
+  if (!c_ranks) return fail(BS_ERR_INVALID_ARG, "fp8_gemm_allgather: null output list");
+  return gemm_common(false, a, a_s, as_dtype, b, b_s, bs_dtype, M, N, K, c_ranks, n_ranks, ldc, col0, stream,
+                     "fp8_gemm_allgather");
+}
+
+int bs_fp4_gemm_allgather(const void* a, const void* a_s, int as_dtype, const void* b, const void* b_s,
+                          int bs_dtype, int64_t M, int64_t N, int64_t K, void* const* c_ranks, int n_ranks,
+                          int64_t ldc, int64_t col0, void* stream) {
+  if (!c_ranks) return fail(BS_ERR_INVALID_ARG, "fp4_gemm_allgather: null output list");
+  return gemm_common(true, a, a_s, as_dtype, b, b_s, bs_dtype, M, N, K, c_ranks, n_ranks, ldc, col0, stream,
+                     "fp4_gemm_allgather");
+}
+
+int bs_peer_barrier(void* const* flags_ranks, int n_ranks, int rank, int64_t epoch, void* stream) {
+  if (!flags_ranks || n_ranks < 1 || n_ranks > 8 || rank < 0 || rank >= n_ranks || epoch <= 0)
+    return fail(BS_ERR_INVALID_ARG, "peer_barrier: %d ranks, rank %d, epoch %lld", n_ranks, rank, (long long)epoch);
+  for (int q = 0; q < n_ranks; ++q)
+    if (!flags_ranks[q] || !aligned(flags_ranks[q], 8))
+      return fail(BS_ERR_INVALID_ARG, "peer_barrier: flag array %d null or not 8-byte aligned", q);
+  return cuda_status(bs_launch_peer_barrier(flags_ranks, n_ranks, rank, (unsigned long long)epoch,
+                                            (cudaStream_t)stream),
+                     "peer_barrier launch");
 }
 
 // ---------------------------------------------------------------------------

@@ -32,13 +32,22 @@
 
 namespace {
 
+// Up to this many output buffers per launch: the tensor-parallel form
+// stores its column slice into every rank's copy of C.
+constexpr int kMaxOut = 8;
+
 struct GemmArgs {
   int M, N, K;
   const void* a_s;
   int as_dtype;
   const void* b_s;
   int bs_dtype;
-  __nv_bfloat16* c;
+  // C[m, col0 + n] (row stride ldc) goes to each of the n_out buffers c[0..n_out)
+  __nv_bfloat16* c[kMaxOut];
+  int n_out;
+  int col0;
+  int64_t ldc;
+  int vec;          // 16-byte stores allowed: buffers, ldc, col0 and N all 8-element aligned
   int kb_per_split;
 };
 
@@ -98,6 +107,7 @@ struct Cfg {
   static constexpr int kTmemCols = kTmemNeed <= 32 ? 32 : kTmemNeed <= 64 ? 64 : kTmemNeed <= 128 ? 128
                                    : kTmemNeed <= 256 ? 256 : 512;
   static_assert(kTmemNeed <= 512, "TMEM budget");
+  static_assert(SWAP || kStages * (kXBytes + kYBytes) >= kBM * (BN + 8) * 2, "output staging fits the ring");
   // Shared memory: [align slack | operand ring | SF ring | constant SF |
   // column scales | receive buffer | barriers].  The last two variable parts
   // are sized per launch (smem_bytes): swap mode caches the fp32 column
@@ -338,18 +348,22 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN>::kThreads, 1)
     // along n, shared by all epilogue threads
     auto write_tile = [&](const __nv_bfloat16* tile, int rows, int n_base) {
       const int cpm = rows / 8;
-      const bool vec = (p.N % 8) == 0 && (reinterpret_cast<uintptr_t>(p.c) & 15) == 0;
       for (int c = threadIdx.x - 64; c < BN * cpm; c += 32 * C::kEpiWarps) {
         const int j = c / cpm, ch = c - j * cpm;
         const int m = y0 + j, n = n_base + ch * 8;
         if (m >= p.M) continue;
         const __nv_bfloat16* src = tile + j * rows + ch * 8;
-        __nv_bfloat16* dst = p.c + (int64_t)m * p.N + n;
-        if (vec && n + 8 <= p.N) {
-          *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+        const int64_t off = (int64_t)m * p.ldc + p.col0 + n;
+        if (p.vec && n + 8 <= p.N) {
+          const uint4 u = *reinterpret_cast<const uint4*>(src);
+#pragma unroll
+          for (int q = 0; q < kMaxOut; ++q)
+            if (q < p.n_out) *reinterpret_cast<uint4*>(p.c[q] + off) = u;
         } else {
-          for (int u = 0; u < 8; ++u)
-            if (n + u < p.N) dst[u] = src[u];
+          for (int t = 0; t < 8 && n + t < p.N; ++t)
+#pragma unroll
+            for (int q = 0; q < kMaxOut; ++q)
+              if (q < p.n_out) p.c[q][off + t] = src[t];
         }
       }
     };
@@ -401,24 +415,39 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN>::kThreads, 1)
 
     if (gridDim.z == 1) {
       if (!SWAP) {
-        const int m = x0 + row;
-        if (m < p.M) {
-          __nv_bfloat16* out = p.c + (int64_t)m * p.N;
-          const bool vec_ok = (p.N % 8) == 0;
+        // Stage the bf16 tile in the operand ring (idle once every epilogue
+        // warp has seen the last partial, i.e. all MMAs are done) and write it
+        // out row by row: a warp then stores 512 contiguous bytes per
+        // instruction instead of 16 bytes in each of 32 rows -- the difference
+        // matters most for the peers' copies, written over NVLink.
+        constexpr int kLd = BN + 8;            // padded row, 16-byte aligned
+        constexpr int kChunks = BN / 8;        // 16-byte chunks per row
+        __nv_bfloat16* tile = reinterpret_cast<__nv_bfloat16*>(stage_base);
 #pragma unroll
-          for (int j = 0; j < C::kCols; j += 8) {
-            const int n = y0 + col0 + j;
-            if (vec_ok && n + 8 <= p.N) {
-              uint4 v;
-              __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&v);
+        for (int j = 0; j < C::kCols; j += 8) {
+          uint4 u;
+          __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
 #pragma unroll
-              for (int t = 0; t < 4; ++t) h[t] = __floats2bfloat162_rn(acc[j + 2 * t], acc[j + 2 * t + 1]);
-              *reinterpret_cast<uint4*>(out + n) = v;
-            } else {
+          for (int t = 0; t < 4; ++t) h[t] = __floats2bfloat162_rn(acc[j + 2 * t], acc[j + 2 * t + 1]);
+          *reinterpret_cast<uint4*>(tile + row * kLd + col0 + j) = u;
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(32 * C::kEpiWarps) : "memory");
+        for (int c = threadIdx.x - 64; c < C::kBM * kChunks; c += 32 * C::kEpiWarps) {
+          const int r = c / kChunks, ch = c - r * kChunks;
+          const int m = x0 + r, n = y0 + ch * 8;
+          if (m >= p.M) continue;
+          const __nv_bfloat16* src = tile + r * kLd + ch * 8;
+          const int64_t off = (int64_t)m * p.ldc + p.col0 + n;
+          if (p.vec && n + 8 <= p.N) {
+            const uint4 u = *reinterpret_cast<const uint4*>(src);
 #pragma unroll
-              for (int t = 0; t < 8; ++t)
-                if (n + t < p.N) out[n + t] = __float2bfloat16_rn(acc[j + t]);
-            }
+            for (int q = 0; q < kMaxOut; ++q)
+              if (q < p.n_out) *reinterpret_cast<uint4*>(p.c[q] + off) = u;
+          } else {
+            for (int t = 0; t < 8 && n + t < p.N; ++t)
+#pragma unroll
+              for (int q = 0; q < kMaxOut; ++q)
+                if (q < p.n_out) p.c[q][off + t] = src[t];
           }
         }
       } else {
@@ -655,9 +684,10 @@ static bool fp8_pair_enabled() {
 // Returns 0 on success, BS_ERR_UNSUPPORTED if a tensor map could not be
 // built, or BS_ERR_CUDA with the CUDA error in *cerr.
 int bs_launch_gemm(bool fp4, const void* a, const void* a_s, int as_dtype, const void* b, const void* b_s,
-                   int bs_dtype, int64_t M, int64_t N, int64_t K, void* c, cudaStream_t st, cudaError_t* cerr) {
+                   int bs_dtype, int64_t M, int64_t N, int64_t K, void* const* c, int n_out, int64_t ldc,
+                   int64_t col0, cudaStream_t st, cudaError_t* cerr) {
   *cerr = cudaSuccess;
-  GemmArgs args;
+  GemmArgs args = {};
   args.M = (int)M;
   args.N = (int)N;
   args.K = (int)K;
@@ -665,7 +695,15 @@ int bs_launch_gemm(bool fp4, const void* a, const void* a_s, int as_dtype, const
   args.as_dtype = as_dtype;
   args.b_s = b_s;
   args.bs_dtype = bs_dtype;
-  args.c = reinterpret_cast<__nv_bfloat16*>(c);
+  args.n_out = n_out;
+  args.col0 = (int)col0;
+  args.ldc = ldc;
+  bool vec = (N % 8) == 0 && (ldc % 8) == 0 && (col0 % 8) == 0;
+  for (int q = 0; q < n_out; ++q) {
+    args.c[q] = reinterpret_cast<__nv_bfloat16*>(c[q]);
+    vec = vec && (reinterpret_cast<uintptr_t>(c[q]) & 15) == 0;
+  }
+  args.vec = vec ? 1 : 0;
   const int nkb = (int)(K / 128);
   CUtensorMap mx, my;
   if (M <= 64) {
@@ -698,8 +736,8 @@ int bs_launch_gemm(bool fp4, const void* a, const void* a_s, int as_dtype, const
       if (bn == 16) BS_DEC(false, 16); else if (bn == 32) BS_DEC(false, 32); else BS_DEC(false, 64);
     }
 #undef BS_DEC
-  } else if (!fp4 && fp8_pair_enabled()) {
-    return bs_launch_fp8_gemm_pair(a, a_s, as_dtype, b, b_s, bs_dtype, M, N, K, c, st, cerr);
+  } else if (!fp4 && n_out == 1 && ldc == N && col0 == 0 && fp8_pair_enabled()) {
+    return bs_launch_fp8_gemm_pair(a, a_s, as_dtype, b, b_s, bs_dtype, M, N, K, c[0], st, cerr);
   } else {
     const int bn = fp4 ? 128 : 256;
     if (!make_map(&mx, a, false, K, M, 128) || !make_map(&my, b, fp4, K, N, bn)) return BS_ERR_UNSUPPORTED;

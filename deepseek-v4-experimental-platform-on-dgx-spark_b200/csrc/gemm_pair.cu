@@ -182,7 +182,7 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
       }
     }
     if (m < p.M) {
-      __nv_bfloat16* out = p.c + (int64_t)m * p.N;
+      __nv_bfloat16* out = p.c[0] + (int64_t)m * p.N;
       const bool vec_ok = (p.N % 8) == 0;
 #pragma unroll
       for (int j = 0; j < C::kCols; j += 8) {
@@ -244,7 +244,7 @@ int bs_launch_fp8_gemm_pair(const void* a, const void* a_s, int as_dtype, const 
                             int bs_dtype, int64_t M, int64_t N, int64_t K, void* c, cudaStream_t st,
                             cudaError_t* cerr) {
   *cerr = cudaSuccess;
-  GemmArgs args;
+  GemmArgs args = {};
   args.M = (int)M;
   args.N = (int)N;
   args.K = (int)K;
@@ -252,7 +252,9 @@ int bs_launch_fp8_gemm_pair(const void* a, const void* a_s, int as_dtype, const 
   args.as_dtype = as_dtype;
   args.b_s = b_s;
   args.bs_dtype = bs_dtype;
-  args.c = reinterpret_cast<__nv_bfloat16*>(c);
+  args.c[0] = reinterpret_cast<__nv_bfloat16*>(c);
+  args.n_out = 1;
+  args.ldc = N;
   args.kb_per_split = (int)(K / 128);
   CUtensorMap ma, mb;
   if (!make_map(&ma, a, false, K, M, 128) || !make_map(&mb, b, false, K, N, 128)) return BS_ERR_UNSUPPORTED;

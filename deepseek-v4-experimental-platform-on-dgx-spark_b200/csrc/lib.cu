@@ -5,5 +5,6 @@
 #include "gemm.cu"
 #include "gemm_pair.cu"
 #include "moe.cu"
+#include "peer.cu"
 #include "capi.cu"
 #include "noalloc.cu"

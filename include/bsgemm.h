@@ -106,6 +106,41 @@ int bs_fp8_gemm(const void* a, const void* a_s, int as_dtype, const void* b, con
 int bs_fp4_gemm(const void* a, const void* a_s, int as_dtype, const void* b, const void* b_s, int bs_dtype,
                 int64_t M, int64_t N, int64_t K, void* c, void* stream);
 
+/*
+ * Tensor-parallel GEMM with the all-gather fused into its epilogue.  This
+ * rank holds the weight rows [col0, col0+N) (b, b_s as for bs_fp8_gemm /
+ * bs_fp4_gemm) and computes the column slice C[:, col0:col0+N]; every output
+ * tile is stored into each of the n_ranks (1..8) buffers of c_ranks -- a
+ * host array of device pointers, this rank's C and its peers' C mapped into
+ * this process (CUDA IPC or symmetric memory), each [M, ldc] bf16 -- so the
+ * transfer over NVLink overlaps the math.  The peers' copies are complete
+ * once every rank's call has finished: the caller orders them with a
+ * cross-rank barrier before reading C, and must not start a call that
+ * overwrites a C some rank is still reading.
+ * Replaces fp8_gemm / fp4_gemm on a column shard followed by an NCCL
+ * all-gather and the column interleave (the TP form of
+ * kernel_sm121.py:190-255 and :343-421).
+ */
+int bs_fp8_gemm_allgather(const void* a, const void* a_s, int as_dtype, const void* b, const void* b_s,
+                          int bs_dtype, int64_t M, int64_t N, int64_t K, void* const* c_ranks, int n_ranks,
+                          int64_t ldc, int64_t col0, void* stream);
+int bs_fp4_gemm_allgather(const void* a, const void* a_s, int as_dtype, const void* b, const void* b_s,
+                          int bs_dtype, int64_t M, int64_t N, int64_t K, void* const* c_ranks, int n_ranks,
+                          int64_t ldc, int64_t col0, void* stream);
+
+/*
+ * Cross-rank barrier over peer memory (no counterpart in the reference,
+ * which synchronises inside NCCL).  flags_ranks[q] is rank q's array of
+ * n_ranks (1..8) uint64 flags mapped into this process, zero before the
+ * first barrier; epoch is the same on every rank and increases by at least
+ * one per barrier.  One small kernel on `stream` release-stores `epoch` into
+ * every peer's flags[rank] (system scope, after the kernels before it on the
+ * stream) and waits until each of this rank's flags holds >= epoch.  The wait
+ * is bounded: a peer that never arrives makes the kernel record
+ * BS_ERR_DEVICE_TIMEOUT (see bs_device_error_check) and return.
+ */
+int bs_peer_barrier(void* const* flags_ranks, int n_ranks, int rank, int64_t epoch, void* stream);
+
 /* ------------------------------------------------------------------------
  * Grouped per-expert MoE layer.
  *

@@ -372,8 +372,9 @@ def bench_moe(args, torch, dist, ws, rank, dev):
 
     One GPU: the whole layer in one call.  N GPUs: expert parallel -- rank r
     owns tokens [r*T/N, (r+1)*T/N) and experts [r*E/N, (r+1)*E/N); rows travel
-    to the expert owners and back by NCCL all-to-all (strong scaling: the
-    total batch is fixed).
+    to the expert owners and back over NVLink peer memory (or, with
+    --ep-transport nccl, by NCCL all-to-all); strong scaling: the total batch
+    is fixed.
     """
     import importlib
     moe = importlib.import_module(PKG + ".moe")
@@ -399,11 +400,11 @@ def bench_moe(args, torch, dist, ws, rank, dev):
         launches = 8
     else:
         ep = importlib.import_module(PKG + ".ep")
-        layer = ep.EPMoE(weights, E, k, max_tokens=tl)
+        layer = ep.EPMoE(weights, E, k, max_tokens=tl, transport=args.ep_transport)
 
         def step():
             layer.forward(xl, ll, out=out)
-        launches = 9
+        launches = 14 if args.ep_transport == "peer" else 9
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
@@ -421,6 +422,10 @@ def bench_moe(args, torch, dist, ws, rank, dev):
         dist.barrier()
     clk = clocks.stop()
     ms = max_over_ranks(torch, dist, t0.elapsed_time(t1) / args.steps)
+    if ws > 1:
+        pkg_lib = importlib.import_module(PKG + "._lib")
+        pkg_lib.device_error_check()
+        layer.close()
     wbytes = w13.numel() + w13_s.numel() + w2.numel() + w2_s.numel()          # per rank
     peaks, src = load_peaks()
     gbs = wbytes / (ms * 1e-3) / 1e9
@@ -429,6 +434,8 @@ def bench_moe(args, torch, dist, ws, rank, dev):
             "scaling": "strong", "vs_baseline": None, "dtype": "e4m3 x e2m1", "data": "synthetic",
             "config": {"workload": f"MoE layer T={T} H={H} I={I} E={E} top-{k}",
                        "parallelism": f"ep{ws}" if ws > 1 else "none",
+                       "exchange": (("NVLink peer memory (no NCCL, no host sync)" if args.ep_transport == "peer"
+                                     else "NCCL all-to-all") if ws > 1 else None),
                        "l2": f"weights {wbytes * ws / 2**30:.2f} GiB >> L2"},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(gbs / peaks["hbm_gbs"], 3), "traffic": None,
@@ -480,6 +487,8 @@ def main():
     ap.add_argument("--m", type=int, default=16)
     ap.add_argument("--n", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ep-transport", choices=["peer", "nccl"], default="peer",
+                    help="moe at N>1: rows exchanged over NVLink peer memory, or by NCCL all-to-all")
     ap.add_argument("--tp-gather", choices=["fused", "nccl"], default="fused",
                     help="fp8_prefill at N>1: all-gather fused into the GEMM epilogue, or NCCL after it")
     args = ap.parse_args()

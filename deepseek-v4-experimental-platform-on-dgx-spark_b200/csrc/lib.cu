@@ -6,5 +6,6 @@
 #include "gemm_pair.cu"
 #include "moe.cu"
 #include "peer.cu"
+#include "ep.cu"
 #include "capi.cu"
 #include "noalloc.cu"

@@ -42,16 +42,18 @@ def _problem(dev, T, H, I, E, seed):
     return x, logits, w13, w13_s, w2, w2_s
 
 
-def _worker(rank, world, port, q, T, H, I, E, topk):
+def _worker(rank, world, port, q, T, H, I, E, topk, transport):
     import datetime
     import torch.distributed as dist
     sys.path.insert(0, os.path.dirname(HERE))
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=dev)
+    layer = None
     try:
         ep = importlib.import_module(PKG + ".ep")
         moe = importlib.import_module(PKG + ".moe")
@@ -59,7 +61,7 @@ def _worker(rank, world, port, q, T, H, I, E, topk):
         e0, e1 = ep.expert_range(E, world, rank)
         W = moe.MoEWeights(w13[e0:e1], w13_s[e0:e1], w2[e0:e1], w2_s[e0:e1])
         tl = T // world
-        layer = ep.EPMoE(W, E, topk, max_tokens=tl)
+        layer = ep.EPMoE(W, E, topk, max_tokens=tl, transport=transport)
         outs = []
         for _ in range(2):
             outs.append(layer.forward(x[rank * tl:(rank + 1) * tl], logits[rank * tl:(rank + 1) * tl]).clone())
@@ -68,20 +70,24 @@ def _worker(rank, world, port, q, T, H, I, E, topk):
         if rank == 0:
             full = moe.moe_forward(x, logits, moe.MoEWeights(w13, w13_s, w2, w2_s), topk)
             res["ref"] = full.cpu().view(torch.int16).numpy()
+        importlib.import_module(PKG + "._lib").device_error_check()
         q.put((rank, res))
         dist.barrier()
     finally:
+        if layer is not None and hasattr(layer, "close"):
+            layer.close()
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("transport", ["peer", "nccl"])
 @pytest.mark.parametrize("T,H,I,E,topk", [(64, 512, 256, 16, 4), (256, 4096, 2048, 32, 8)])
-def test_ep_two_gpus_match_single_gpu(T, H, I, E, topk):
+def test_ep_two_gpus_match_single_gpu(T, H, I, E, topk, transport):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, T, H, I, E, topk)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, T, H, I, E, topk, transport)) for r in range(2)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=240) for _ in range(2))
@@ -94,5 +100,6 @@ def test_ep_two_gpus_match_single_gpu(T, H, I, E, topk):
         r = (ref.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
         o = (ep.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
         err = np.linalg.norm(o - r) / np.linalg.norm(r)
-        print(f"EP2 T={T} H={H} E={E} call {call}: rel_fro={err:.3e}, identical={np.array_equal(ep, ref)}")
+        print(f"EP2 ({transport}) T={T} H={H} E={E} call {call}: rel_fro={err:.3e}, "
+              f"identical={np.array_equal(ep, ref)}")
         assert err <= 1e-2

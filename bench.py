@@ -402,9 +402,25 @@ def bench_moe(args, torch, dist, ws, rank, dev):
         ep = importlib.import_module(PKG + ".ep")
         layer = ep.EPMoE(weights, E, k, max_tokens=tl, transport=args.ep_transport)
 
-        def step():
-            layer.forward(xl, ll, out=out)
         launches = 14 if args.ep_transport == "peer" else 9
+        if args.ep_transport == "peer":
+            # no host sync inside the layer: capture it once, replay one graph per step
+            for _ in range(2):
+                layer.forward(xl, ll, out=out)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            cap = torch.cuda.Stream()
+            cap.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(cap):
+                with torch.cuda.graph(graph, stream=cap):
+                    layer.forward(xl, ll, out=out)
+            torch.cuda.current_stream().wait_stream(cap)
+
+            def step():
+                graph.replay()
+        else:
+            def step():
+                layer.forward(xl, ll, out=out)
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
@@ -422,7 +438,37 @@ def bench_moe(args, torch, dist, ws, rank, dev):
         dist.barrier()
     clk = clocks.stop()
     ms = max_over_ranks(torch, dist, t0.elapsed_time(t1) / args.steps)
+
+    # end to end through the public API: pinned host bf16 tokens and fp32 gate
+    # logits -> device -> the layer (eager) -> pinned host output
+    x_host, l_host = xl.cpu().pin_memory(), ll.cpu().pin_memory()
+    o_host = torch.empty(tl, H, dtype=torch.bfloat16).pin_memory()
+    x_dev, l_dev = torch.empty_like(xl), torch.empty_like(ll)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        l_dev.copy_(l_host, non_blocking=True)
+        if ws == 1:
+            moe.moe_forward(x_dev, l_dev, weights, k, out=out)
+        else:
+            layer.forward(x_dev, l_dev, out=out)
+        o_host.copy_(out, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(torch, dist, e0.elapsed_time(e1) / args.steps)
     if ws > 1:
+        if args.ep_transport == "peer":
+            del graph
         pkg_lib = importlib.import_module(PKG + "._lib")
         pkg_lib.device_error_check()
         layer.close()
@@ -440,6 +486,10 @@ def bench_moe(args, torch, dist, ws, rank, dev):
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(gbs / peaks["hbm_gbs"], 3), "traffic": None,
                          "note": "this rank's expert weight bytes per layer / layer time", "peak_source": src},
+            "e2e": {"value": round(T / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": ws * tl * (H * 2 + E * 4), "d2h_bytes_per_step": ws * tl * H * 2,
+                    "ms_per_step": round(e2e_ms, 4),
+                    "path": "moe_forward / EPMoE.forward public API, pinned host tokens + logits in, output out"},
             "gpu_launches": args.steps * launches, "clocks": clk}
 
 

@@ -35,6 +35,7 @@ SIGNATURES = {
     "bs_fp4_gemm_allgather": [_c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p, _i32, _i64, _i64, _i64,
                               ctypes.POINTER(_c_void_p), _i32, _i64, _i64, _c_void_p],
     "bs_peer_barrier": [ctypes.POINTER(_c_void_p), _i32, _i32, _i64, _c_void_p],
+    "bs_peer_barrier_counted": [ctypes.POINTER(_c_void_p), _i32, _i32, _c_void_p, _c_void_p],
     "bs_moe_pack_scales": [_c_void_p, _i64, _i32, _i32, _c_void_p, _c_void_p],
     "bs_moe_chunk_capacity": [_i64, _i32],
     "bs_moe_workspace_size": [_i64, _i32, _i32, _i32, _i32],

@@ -21,7 +21,7 @@ cudaError_t bs_launch_moe_dispatch(const int* idx, int T, int topk, const int* o
 cudaError_t bs_launch_moe_pack_scales(const uint8_t* ws, int64_t E, int rows, int K, uint8_t* out, cudaStream_t st);
 int64_t bs_moe_max_chunks(int64_t rows, int E);
 cudaError_t bs_launch_peer_barrier(void* const* flags, int n_ranks, int rank, unsigned long long epoch,
-                                   cudaStream_t st);
+                                   unsigned long long* counter, cudaStream_t st);
 cudaError_t bs_launch_moe_combine(const __nv_bfloat16* y, const int* pos_of, const float* w, int T, int topk, int H,
                                   __nv_bfloat16* out, cudaStream_t st);
 int bs_launch_moe_experts(int E, int64_t rows, int H, int I, const uint8_t* ap, const uint8_t* asp,
@@ -198,9 +198,21 @@ int bs_peer_barrier(void* const* flags_ranks, int n_ranks, int rank, int64_t epo
   for (int q = 0; q < n_ranks; ++q)
     if (!flags_ranks[q] || !aligned(flags_ranks[q], 8))
       return fail(BS_ERR_INVALID_ARG, "peer_barrier: flag array %d null or not 8-byte aligned", q);
-  return cuda_status(bs_launch_peer_barrier(flags_ranks, n_ranks, rank, (unsigned long long)epoch,
+  return cuda_status(bs_launch_peer_barrier(flags_ranks, n_ranks, rank, (unsigned long long)epoch, nullptr,
                                             (cudaStream_t)stream),
                      "peer_barrier launch");
+}
+
+int bs_peer_barrier_counted(void* const* flags_ranks, int n_ranks, int rank, int64_t* counter, void* stream) {
+  if (!flags_ranks || n_ranks < 1 || n_ranks > 8 || rank < 0 || rank >= n_ranks || !counter || !aligned(counter, 8))
+    return fail(BS_ERR_INVALID_ARG, "peer_barrier_counted: %d ranks, rank %d, counter %p", n_ranks, rank,
+                (void*)counter);
+  for (int q = 0; q < n_ranks; ++q)
+    if (!flags_ranks[q] || !aligned(flags_ranks[q], 8))
+      return fail(BS_ERR_INVALID_ARG, "peer_barrier_counted: flag array %d null or not 8-byte aligned", q);
+  return cuda_status(bs_launch_peer_barrier(flags_ranks, n_ranks, rank, 0,
+                                            reinterpret_cast<unsigned long long*>(counter), (cudaStream_t)stream),
+                     "peer_barrier_counted launch");
 }
 
 // ---------------------------------------------------------------------------

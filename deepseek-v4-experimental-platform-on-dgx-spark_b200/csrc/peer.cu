@@ -21,7 +21,19 @@ struct Flags {
   unsigned long long* f[kMaxRanks];   // f[q]: rank q's flag array, mapped here
 };
 
-__global__ void barrier_kernel(Flags fl, int n_ranks, int rank, unsigned long long epoch) {
+// counter != nullptr: the epoch is this rank's barrier count, kept in device
+// memory (*counter + 1, stored back), so a captured launch replays correctly.
+__global__ void barrier_kernel(Flags fl, int n_ranks, int rank, unsigned long long epoch,
+                               unsigned long long* counter) {
+  if (counter) {
+    __shared__ unsigned long long e;
+    if (threadIdx.x == 0) {
+      e = *counter + 1;
+      *counter = e;
+    }
+    __syncthreads();
+    epoch = e;
+  }
   const int q = threadIdx.x;
   if (q >= n_ranks || q == rank) return;
   __threadfence_system();
@@ -39,9 +51,9 @@ __global__ void barrier_kernel(Flags fl, int n_ranks, int rank, unsigned long lo
 }  // namespace peer
 
 cudaError_t bs_launch_peer_barrier(void* const* flags, int n_ranks, int rank, unsigned long long epoch,
-                                   cudaStream_t st) {
+                                   unsigned long long* counter, cudaStream_t st) {
   peer::Flags fl = {};
   for (int q = 0; q < n_ranks; ++q) fl.f[q] = reinterpret_cast<unsigned long long*>(flags[q]);
-  peer::barrier_kernel<<<1, 32, 0, st>>>(fl, n_ranks, rank, epoch);
+  peer::barrier_kernel<<<1, 32, 0, st>>>(fl, n_ranks, rank, epoch, counter);
   return cudaGetLastError();
 }

@@ -132,8 +132,9 @@ class CudaOps:
                                                  weights.w2.data_ptr(), weights.w2_sp.data_ptr(), ret.data_ptr(),
                                                  y_ptrs, n_ranks, hq.data_ptr(), hs_p.data_ptr(), self._st()))
 
-    def barrier(self, flag_ptrs, rank, n_ranks, epoch):
-        _lib.check(self.lib.bs_peer_barrier(flag_ptrs, n_ranks, rank, epoch, self._st()))
+    def barrier(self, flag_ptrs, rank, n_ranks, counter):
+        # epoch kept on the device (counter), so the layer can be captured in a CUDA graph
+        _lib.check(self.lib.bs_peer_barrier_counted(flag_ptrs, n_ranks, rank, counter.data_ptr(), self._st()))
 
 
 class EPMoE:
@@ -230,14 +231,13 @@ class EPMoE:
         self.y_back, self.y_ptrs = sym(R, H, dtype=torch.bfloat16)              # outputs returned here
         self.flags, self.flag_ptrs = sym(n, dtype=torch.int64)                    # barrier epochs
         self.send_pos0 = torch.empty(self.E, dtype=torch.int32, device=dev)
+        self.epoch_ctr = torch.zeros(1, dtype=torch.int64, device=dev)
         self.flags.zero_()
         torch.cuda.synchronize(dev)
         dist.barrier(group=self.group)
-        self.epoch = 0
 
     def _barrier(self):
-        self.epoch += 1
-        self.ops.barrier(self.flag_ptrs, self.rank, self.world, self.epoch)
+        self.ops.barrier(self.flag_ptrs, self.rank, self.world, self.epoch_ctr)
 
     def close(self):
         """Release the symmetric buffers (before the process group is destroyed)."""

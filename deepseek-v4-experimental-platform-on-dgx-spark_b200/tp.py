@@ -8,9 +8,10 @@ of writing the slice to a local buffer and all-gathering it with NCCL
 epilogue straight into each rank's copy of C, mapped into this process
 through symmetric memory; the NVLink transfer overlaps the remaining math.
 A symmetric-memory barrier after the kernel makes every rank's slice
-visible everywhere.  The barrier is the library's own (bs_peer_barrier:
-epoch flags in symmetric memory, bounded waits that report a device-side
-timeout instead of trapping).
+visible everywhere.  The barrier is the library's own
+(bs_peer_barrier_counted: epoch flags in symmetric memory, the epoch counted
+on the device so calls can be captured in CUDA graphs, bounded waits that
+report a device-side timeout instead of trapping).
 
 Two symmetric output buffers alternate between calls: every rank passes the
 barrier of call i before any rank can start call i+1, so call i+1's stores
@@ -89,10 +90,10 @@ class TPGemm:
         self.handles.append(fh)
         self.flag_ptrs = (ctypes.c_void_p * self.world)(*[self._peer_ptr(self.flags, fh, q)
                                                           for q in range(self.world)])
+        self.epoch_ctr = torch.zeros(1, dtype=torch.int64, device=self.device)
         self.flags.zero_()
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
-        self.epoch = 0
         self.calls = 0
         self._fn = self.lib.bs_fp4_gemm_allgather if fp4 else self.lib.bs_fp8_gemm_allgather
 
@@ -134,8 +135,8 @@ class TPGemm:
             _lib.check(self._fn(a.data_ptr(), a_s.data_ptr(), as_dt, b_local.data_ptr(), b_s_local.data_ptr(), bs_dt,
                                 M, self.n_local, K, self.ptrs[i], self.world, self.N, self.col0, st.cuda_stream))
             # every rank's slice has landed in every rank's buffer i
-            self.epoch += 1
-            _lib.check(self.lib.bs_peer_barrier(self.flag_ptrs, self.world, self.rank, self.epoch, st.cuda_stream))
+            _lib.check(self.lib.bs_peer_barrier_counted(self.flag_ptrs, self.world, self.rank,
+                                                        self.epoch_ctr.data_ptr(), st.cuda_stream))
         return self.bufs[i]
 
     def close(self):

@@ -140,6 +140,11 @@ int bs_fp4_gemm_allgather(const void* a, const void* a_s, int as_dtype, const vo
  * BS_ERR_DEVICE_TIMEOUT (see bs_device_error_check) and return.
  */
 int bs_peer_barrier(void* const* flags_ranks, int n_ranks, int rank, int64_t epoch, void* stream);
+/* The same barrier with the epoch kept in device memory: *counter (a device
+ * int64, zero before the first barrier, the same count on every rank) is
+ * incremented by the kernel and used as the epoch, so the launch can be
+ * captured in a CUDA graph and replayed. */
+int bs_peer_barrier_counted(void* const* flags_ranks, int n_ranks, int rank, int64_t* counter, void* stream);
 
 /* ------------------------------------------------------------------------
  * Grouped per-expert MoE layer.

@@ -34,6 +34,15 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 PKG = "deepseek-v4-experimental-platform-on-dgx-spark_b200"
 
+# DRAM bytes (read + write) per launch of the dominant kernel, from one ncu
+# capture of the same workload (dram__bytes_read.sum + dram__bytes_write.sum;
+# the summaries and commands are in profiles/).  Output writes that are still
+# in L2 when the kernel ends are not counted by ncu for that launch.
+NCU_TRAFFIC = {
+    "fp8_gemm_4096x4096x4096": 34_120_960 + 2_532_864,      # profiles/fp8_gemm_4096_prefill.md
+    "fp4_decode_16x4096x4096": 9_039_872 + 0,               # profiles/fp4_gemm_decode_m16_n4096.md
+}
+
 PEAKS_FILE = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
@@ -258,11 +267,7 @@ def bench_fp8_prefill(args, torch, dist, ws, rank, dev):
         nvlink = {"bytes_per_gpu": gathered_bytes, "gbs_per_direction": 770.0,
                   "target_ms": round(max(t_math, t_link) * 1e3, 4),
                   "bound_by": "nvlink" if t_link > t_math else "tensor"}
-    traffic = None
-    tfile = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(tfile):
-        with open(tfile) as f:
-            traffic = json.load(f).get(f"fp8_gemm_{M}x{n_local}x{K}")
+    traffic = NCU_TRAFFIC.get(f"fp8_gemm_{M}x{n_local}x{K}")
     line = {
         "metric": "block-scaled FP8 GEMM TFLOP/s (dense fp8_gemm, 1x128 act + 128x128 weight fp32 scales)",
         "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
@@ -362,7 +367,8 @@ def bench_fp4_decode(args, torch, dist, ws, rank, dev):
             "data": "synthetic", "config": {"workload": f"fp4_gemm decode M={M} N={N} K={K}",
                                             "l2": f"{n_sets} rotating weight copies"},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": round(gbs / peaks["hbm_gbs"], 3), "traffic": None, "peak_source": src},
+                         "frac": round(gbs / peaks["hbm_gbs"], 3),
+                         "traffic": NCU_TRAFFIC.get(f"fp4_decode_{M}x{N}x{K}"), "peak_source": src},
             "gpu_launches": steps * reps, "clocks": clk,
             "eager_ms_per_call": round(ms_eager, 5)}
 

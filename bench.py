@@ -531,14 +531,158 @@ def cpu_fp8_prefill(steps: int, warmup: int, m_rows: int = 4096):
     return 2.0 * m_rows * 4096 * 4096 / s / 1e12, s
 
 
+def zipf_bias(torch, E, seed):
+    """Expert popularity skew of the long-prefill config: -1.2*ln(1 + rank of e)
+    under a seeded permutation of the experts (a Zipf(1.2)-like stand-in)."""
+    perm = torch.randperm(E, generator=torch.Generator().manual_seed(seed))
+    return -1.2 * torch.log1p(perm.float())
+
+
+def bench_moe_stack(args, torch, dist, ws, rank, dev):
+    """Config-5 long-prefill stack: T=8192 tokens, 4 layers, each an fp8_gemm
+    4096->4096 projection (1x128 activation, 128x128 weight scales) followed by
+    the config-4 MoE (256 experts, top-8) under Zipf-skewed expert popularity.
+
+    One GPU: the whole stack.  N GPUs: rank r owns tokens [r*T/N, (r+1)*T/N)
+    (its projections run on its own tokens with a full copy of the small dense
+    weights) and experts [r*E/N, (r+1)*E/N) of every layer; the MoE rows
+    travel over NVLink peer memory.  Metric: token-layers per second
+    (T x 4 / stack time), strong scaling.
+    """
+    import importlib
+    pkg = importlib.import_module(PKG)
+    moe = importlib.import_module(PKG + ".moe")
+    T, H, I, E, k, L = args.tokens, 4096, 2048, args.experts, 8, 4
+    if T % ws or E % ws:
+        raise SystemExit("tokens and experts must split evenly over the ranks")
+    El, tl = E // ws, T // ws
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    x_all = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    bias = zipf_bias(torch, E, 11).to(dev)
+    logits = [(torch.randn(T, E, generator=g, device=dev) + bias)[rank * tl:(rank + 1) * tl].contiguous()
+              for _ in range(L)]
+    proj = []
+    for _ in range(L):
+        w = torch.randn(H, H, generator=g, device=dev) * 0.02
+        wb = w.view(H // 128, 128, H // 128, 128)
+        sc = wb.abs().amax(dim=(1, 3)).clamp(min=1e-4) / 448.0
+        proj.append(((wb / sc[:, None, :, None]).clamp(-448, 448).to(torch.float8_e4m3fn).view(H, H), sc.contiguous()))
+    g.manual_seed(2000 + rank)
+    layers = []
+    for _ in range(L):
+        w13 = torch.randint(0, 256, (El, 2 * I, H // 2), generator=g, device=dev, dtype=torch.uint8)
+        w13_s = 127 - torch.randint(0, 7, (El, 2 * I, H // 32), generator=g, device=dev, dtype=torch.uint8)
+        w2 = torch.randint(0, 256, (El, H, I // 2), generator=g, device=dev, dtype=torch.uint8)
+        w2_s = 127 - torch.randint(0, 7, (El, H, I // 32), generator=g, device=dev, dtype=torch.uint8)
+        layers.append(moe.MoEWeights(w13, w13_s, w2, w2_s))
+        del w13, w13_s, w2, w2_s
+    x0 = x_all[rank * tl:(rank + 1) * tl].contiguous()
+    del x_all
+    if ws > 1:
+        ep = importlib.import_module(PKG + ".ep")
+        eps = [ep.EPMoE(W, E, k, max_tokens=tl, transport=args.ep_transport) for W in layers]
+    outs = [torch.empty(tl, H, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+
+    def stack(x):
+        for l in range(L):
+            a, a_s = pkg.act_quant(x, 128)
+            h = pkg.fp8_gemm(a, a_s, proj[l][0], proj[l][1])
+            out = outs[l & 1]
+            if ws > 1:
+                eps[l].forward(h, logits[l], out=out)
+            else:
+                moe.moe_forward(h, logits[l], layers[l], k, out=out)
+            x = out
+        return x
+
+    for _ in range(args.warmup):
+        stack(x0)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    clocks = Clocks(torch.cuda.current_device())
+    clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        stack(x0)
+    t1.record()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    clk = clocks.stop()
+    ms = max_over_ranks(torch, dist, t0.elapsed_time(t1) / args.steps)
+    # load balance: rows each rank's experts received per layer (max / mean over ranks)
+    recv = torch.zeros(L, dtype=torch.float64, device=dev)
+    for l in range(L):
+        if ws > 1:
+            recv[l] = float(eps[l].loc_off[El].item()) if args.ep_transport == "peer" else float(
+                eps[l].recv_counts.sum().item())
+        else:
+            recv[l] = float(tl * k)
+    if dist is not None:
+        mx, mean = recv.clone(), recv.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        dist.all_reduce(mean)
+        mean /= ws
+        imbalance = [round(float(a / b), 3) for a, b in zip(mx, mean)]
+    else:
+        imbalance = [1.0] * L
+    # end to end: pinned host tokens in, the last layer's output out
+    x_host = x0.cpu().pin_memory()
+    o_host = torch.empty(tl, H, dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty_like(x0)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        o_host.copy_(stack(x_dev), non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(torch, dist, e0.elapsed_time(e1) / args.steps)
+    if ws > 1:
+        pkg._lib.device_error_check()
+        for m in eps:
+            m.close()
+    peaks, src = load_peaks()
+    flops = L * (2.0 * T * H * H + T * k * (2.0 * H * 2 * I + 2.0 * I * H))
+    achieved = flops / ws / (ms * 1e-3) / 1e12
+    peak = 2.0 * peaks["bf16_tflops"]
+    return {"metric": "MoE stack token-layers/s (long prefill)", "value": round(T * L / (ms * 1e-3), 1),
+            "unit": "token-layers/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "e4m3 x e2m1 (MoE), e4m3 (projections)", "data": "synthetic (Zipf-skewed gate logits)",
+            "config": {"workload": f"{L} layers x (fp8_gemm {H}->{H} + MoE E={E} top-{k} I={I}), T={T}",
+                       "parallelism": f"ep{ws} (+ token-parallel projections)" if ws > 1 else "none",
+                       "exchange": ("NVLink peer memory" if args.ep_transport == "peer" else "NCCL all-to-all")
+                       if ws > 1 else None,
+                       "load_imbalance_max_over_mean": imbalance},
+            "e2e": {"value": round(T * L / (e2e_ms * 1e-3), 1), "unit": "token-layers/s",
+                    "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 2, "ms_per_step": round(e2e_ms, 3)},
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
+                         "frac": round(achieved / peak, 3), "traffic": None,
+                         "note": "per-GPU FLOP of the stack / stack time vs the dense e4m3 rate"},
+            "gpu_launches": args.steps * L * (2 + (14 if ws > 1 and args.ep_transport == "peer" else 9)),
+            "clocks": clk}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["fp8_prefill", "fp4_decode", "moe"], default="fp8_prefill")
-    ap.add_argument("--tokens", type=int, default=1024)
+    ap.add_argument("--workload", choices=["fp8_prefill", "fp4_decode", "moe", "moe_stack"], default="fp8_prefill")
+    ap.add_argument("--tokens", type=int, default=None, help="moe: 1024, moe_stack: 8192")
     ap.add_argument("--experts", type=int, default=256)
     ap.add_argument("--m", type=int, default=16)
     ap.add_argument("--n", type=int, default=4096)
@@ -549,6 +693,8 @@ def main():
                     help="fp8_prefill at N>1: all-gather fused into the GEMM epilogue, or NCCL after it")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.tokens is None:
+        args.tokens = 8192 if args.workload == "moe_stack" else 1024
     ws, rank, local = dist_env()
 
     if args.impl == "reference":
@@ -588,6 +734,8 @@ def main():
         line = bench_fp8_prefill(args, torch, dist, ws, rank, dev)
     elif args.workload == "moe":
         line = bench_moe(args, torch, dist, ws, rank, dev)
+    elif args.workload == "moe_stack":
+        line = bench_moe_stack(args, torch, dist, ws, rank, dev)
     else:
         line = bench_fp4_decode(args, torch, dist, ws, rank, dev)
 

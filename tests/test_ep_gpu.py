@@ -30,11 +30,14 @@ def _free_port():
     return p
 
 
-def _problem(dev, T, H, I, E, seed):
+def _problem(dev, T, H, I, E, seed, skew=False):
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
     x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
     logits = torch.randn(T, E, generator=g, device=dev)
+    if skew:
+        # every token's top-k lies in rank 0's experts: rank 1 receives nothing
+        logits[:, :E // 2] += 20.0
     w13 = torch.randint(0, 256, (E, 2 * I, H // 2), generator=g, device=dev, dtype=torch.uint8)
     w13_s = 127 - torch.randint(0, 7, (E, 2 * I, H // 32), generator=g, device=dev, dtype=torch.uint8)
     w2 = torch.randint(0, 256, (E, H, I // 2), generator=g, device=dev, dtype=torch.uint8)
@@ -42,7 +45,7 @@ def _problem(dev, T, H, I, E, seed):
     return x, logits, w13, w13_s, w2, w2_s
 
 
-def _worker(rank, world, port, q, T, H, I, E, topk, transport):
+def _worker(rank, world, port, q, T, H, I, E, topk, transport, skew):
     import datetime
     import torch.distributed as dist
     sys.path.insert(0, os.path.dirname(HERE))
@@ -57,7 +60,7 @@ def _worker(rank, world, port, q, T, H, I, E, topk, transport):
     try:
         ep = importlib.import_module(PKG + ".ep")
         moe = importlib.import_module(PKG + ".moe")
-        x, logits, w13, w13_s, w2, w2_s = _problem(dev, T, H, I, E, 5)
+        x, logits, w13, w13_s, w2, w2_s = _problem(dev, T, H, I, E, 5, skew)
         e0, e1 = ep.expert_range(E, world, rank)
         W = moe.MoEWeights(w13[e0:e1], w13_s[e0:e1], w2[e0:e1], w2_s[e0:e1])
         tl = T // world
@@ -81,13 +84,15 @@ def _worker(rank, world, port, q, T, H, I, E, topk, transport):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 @pytest.mark.parametrize("transport", ["peer", "nccl"])
-@pytest.mark.parametrize("T,H,I,E,topk", [(64, 512, 256, 16, 4), (256, 4096, 2048, 32, 8)])
-def test_ep_two_gpus_match_single_gpu(T, H, I, E, topk, transport):
+@pytest.mark.parametrize("T,H,I,E,topk,skew", [(64, 512, 256, 16, 4, False), (256, 4096, 2048, 32, 8, False),
+                                               (64, 512, 256, 16, 4, True)])
+def test_ep_two_gpus_match_single_gpu(T, H, I, E, topk, skew, transport):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, T, H, I, E, topk, transport)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, T, H, I, E, topk, transport, skew))
+             for r in range(2)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=240) for _ in range(2))

@@ -75,17 +75,29 @@ def test_moe_routing_matches_oracle():
     np.testing.assert_array_equal(counts.cpu().numpy(), np.bincount(ridx.ravel(), minlength=E))
 
 
-def test_moe_config4_consistency():
-    """Config-4 shape (T=1024, H=4096, I=2048, E=256, top-8): finite, deterministic,
-    and equal to the per-expert fp4_gemm composition on a sample of tokens."""
+def zipf_bias(E, seed):
+    """Expert popularity skew of the long-prefill config: -1.2*ln(1 + rank of e)
+    under a seeded permutation of the experts."""
+    perm = torch.randperm(E, generator=torch.Generator().manual_seed(seed))
+    return -1.2 * torch.log1p(perm.float())
+
+
+@pytest.mark.parametrize("T,skew", [(1024, False), (2048, True)])
+def test_moe_config4_consistency(T, skew):
+    """Config-4 shape (H=4096, I=2048, E=256, top-8; T=1024, and T=2048 with the
+    Zipf-like popularity skew of config 5, where a few experts receive over a
+    thousand rows): finite, deterministic, and equal to the per-expert fp4_gemm
+    composition on a sample of tokens."""
     mm = moe_mod()
     pkg = importlib.import_module(PKG_NAME)
     dev = torch.device("cuda")
     g = torch.Generator(device=dev)
     g.manual_seed(0)
-    T, H, I, E, k = 1024, 4096, 2048, 256, 8
+    H, I, E, k = 4096, 2048, 256, 8
     x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
     logits = torch.randn(T, E, generator=g, device=dev)
+    if skew:
+        logits += zipf_bias(E, 9).to(dev)
     w13 = torch.randint(0, 256, (E, 2 * I, H // 2), generator=g, device=dev, dtype=torch.uint8)
     w13_s = 127 - torch.randint(0, 7, (E, 2 * I, H // 32), generator=g, device=dev, dtype=torch.uint8)
     w2 = torch.randint(0, 256, (E, H, I // 2), generator=g, device=dev, dtype=torch.uint8)
@@ -97,7 +109,7 @@ def test_moe_config4_consistency():
     assert torch.isfinite(out.float()).all()
     assert torch.equal(out, out2)
     # per-token check through the dense drop-in ops for 4 tokens
-    tok = torch.tensor([0, 1, 511, 1023], device=dev)
+    tok = torch.tensor([0, 1, T // 2 - 1, T - 1], device=dev)
     idx, wts = ob.moe_route(logits[tok].cpu().numpy(), k)
     ref = torch.zeros(len(tok), H, device=dev)
     xq, xs = pkg.act_quant(x[tok], 128, "ue8m0")
@@ -111,7 +123,10 @@ def test_moe_config4_consistency():
             y = pkg.fp4_gemm(zq, zs, w2[e].view(torch.float4_e2m1fn_x2), w2_s[e].view(torch.float8_e8m0fnu)).float()
             ref[r] += float(wts[r, s]) * y[0]
     e = (torch.linalg.norm(out[tok].float() - ref) / torch.linalg.norm(ref)).item()
-    print(f"moe config4 sampled tokens: rel_fro={e:.3e}")
+    if skew:
+        top = torch.bincount(torch.topk(logits, k, dim=1).indices.flatten(), minlength=E).max().item()
+        print(f"most popular expert receives {top} rows")
+    print(f"moe T={T} skew={skew} sampled tokens: rel_fro={e:.3e}")
     assert e <= TOL
 
 

@@ -9,13 +9,20 @@
 //                      scope, after a system fence: the stores of the kernels
 //                      before it on this stream are ordered before it), then
 //                      acquire-spin until this rank's flags[q] >= e.
-// The spin is bounded; a peer that never arrives makes the kernel record
-// BS_ERR_DEVICE_TIMEOUT in bs_device_error and return, leaving the context
-// usable.
+// The spin is bounded in time (kPeerTimeoutNs of %globaltimer); a peer that
+// never arrives makes the kernel record BS_ERR_DEVICE_TIMEOUT in
+// bs_device_error and return, leaving the context usable.
 
 namespace peer {
 
 constexpr int kMaxRanks = 8;
+constexpr unsigned long long kPeerTimeoutNs = 2000000000ull;   // 2 s
+
+BS_DEVINL unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 struct Flags {
   unsigned long long* f[kMaxRanks];   // f[q]: rank q's flag array, mapped here
@@ -39,10 +46,12 @@ __global__ void barrier_kernel(Flags fl, int n_ranks, int rank, unsigned long lo
   __threadfence_system();
   asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(fl.f[q] + rank), "l"(epoch) : "memory");
   const unsigned long long* mine = fl.f[rank] + q;
-  for (uint32_t i = 0; i < BS_SPIN_LIMIT; ++i) {
+  const unsigned long long t0 = globaltimer_ns();
+  for (;;) {
     unsigned long long v;
     asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(mine) : "memory");
     if (v >= epoch) return;
+    if (globaltimer_ns() - t0 > kPeerTimeoutNs) break;
     __nanosleep(64);
   }
   bs_set_error(BS_ERR_DEVICE_TIMEOUT);

@@ -136,7 +136,7 @@ int bs_fp4_gemm_allgather(const void* a, const void* a_s, int as_dtype, const vo
  * one per barrier.  One small kernel on `stream` release-stores `epoch` into
  * every peer's flags[rank] (system scope, after the kernels before it on the
  * stream) and waits until each of this rank's flags holds >= epoch.  The wait
- * is bounded: a peer that never arrives makes the kernel record
+ * is bounded (2 s): a peer that never arrives makes the kernel record
  * BS_ERR_DEVICE_TIMEOUT (see bs_device_error_check) and return.
  */
 int bs_peer_barrier(void* const* flags_ranks, int n_ranks, int rank, int64_t epoch, void* stream);

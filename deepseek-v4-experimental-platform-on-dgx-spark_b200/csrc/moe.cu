@@ -297,7 +297,8 @@ struct GemmArgs {
   int K;                     // reduction size (hidden for W13, inter for W2)
   int n_tiles;               // 128-row output tiles per expert
   int w_rows;                // rows per expert in the weight tensor
-  int up_off;                // W13: row offset of W3 inside W13
+  int up_off;                // row offset of an item's second weight tile (W13: W3 inside W13)
+  int nt_stride;             // weight rows advanced per item tile index
   const int* offsets;        // [E+1] token-row offsets
   const int* chunk_prefix;   // [E+1] prefix of token chunks
   const uint8_t* w_sp;       // weights' scales, packed [E][w_rows/128][K/128][512]
@@ -314,13 +315,19 @@ struct GemmArgs {
   __nv_bfloat16* y_ranks[8];
 };
 
-template <bool PAIRED>
+// Grouped GEMM modes: W2 with one 128-row weight tile per item; W1/W3 with
+// the gate and up tiles of one 128-feature slice per item and the SwiGLU +
+// e4m3 quantisation epilogue; W2 with two adjacent 128-row tiles per item
+// sharing one token tile (twice the weight bytes in flight per stage).
+constexpr int kModeW2 = 0, kModeW13 = 1, kModeW2Pair = 2;
+
+template <int MODE>
 struct Cfg {
-  static constexpr int kXTiles = PAIRED ? 2 : 1;
+  static constexpr int kXTiles = MODE == kModeW2 ? 1 : 2;
   static constexpr int kXBytes = kXTiles * 128 * 128;   // unpacked e2m1 in smem
   static constexpr int kYBytes = 128 * 128;             // token tile: 32-row boxes, <= 128 rows
   static constexpr int kStageBytes = kXBytes + kYBytes;
-  static constexpr int kStages = PAIRED ? 4 : 6;
+  static constexpr int kStages = MODE == kModeW2 ? 6 : 4;
   static constexpr int kSfBytes = 512 * (kXTiles + 1);
   static constexpr int kAccBufs = 2;
   static constexpr int kAccCols = kXTiles * kTok;        // per accumulator buffer
@@ -339,10 +346,10 @@ BS_DEVINL void named_bar_epi() { asm volatile("bar.sync 1, 128;" ::: "memory"); 
 BS_DEVINL float silu(float g) { return g / (1.0f + expf(-g)); }
 BS_DEVINL float bf16_round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
-template <bool PAIRED>
+template <int MODE>
 __global__ void __launch_bounds__(192, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a, GemmArgs p) {
-  using C = Cfg<PAIRED>;
+  using C = Cfg<MODE>;
   extern __shared__ uint8_t smem_raw[];
   // 1 KB alignment by offsetting smem_raw itself, so that every buffer
   // carved from it stays in the shared address space for the compiler
@@ -431,7 +438,7 @@ __global__ void __launch_bounds__(192, 1)
           uint8_t* sf = sf_base + s * C::kSfBytes;
           mbar_arrive_expect_tx(&full[s], C::kXTiles * (8192 + 512) + nbox * 32 * 128 + 512);
           for (int t = 0; t < C::kXTiles; ++t) {
-            const int wr0 = (t == 0 ? 0 : p.up_off) + nt * 128;
+            const int wr0 = (t == 0 ? 0 : p.up_off) + nt * p.nt_stride;
             tma_load_3d(sx + t * 16384, &tm_w, &full[s], kb * 128, wr0, e);
             bulk_load(sf + t * 512, p.w_sp + (((int64_t)e * w_tiles + wr0 / 128) * nkb + kb) * 512, 512, &full[s]);
           }
@@ -510,7 +517,7 @@ __global__ void __launch_bounds__(192, 1)
       for (int c0 = 0; c0 < cnt; c0 += 16) {
         uint32_t g[16];
         BS_TMEM_LD16(tl + c0, g);
-        if constexpr (PAIRED) {
+        if constexpr (MODE == kModeW13) {
           uint32_t u[16];
           BS_TMEM_LD16(tl + kTok + c0, u);
           tmem_ld_wait();
@@ -547,6 +554,8 @@ __global__ void __launch_bounds__(192, 1)
             }
           }
         } else {
+          uint32_t g2[16];
+          if constexpr (MODE == kModeW2Pair) BS_TMEM_LD16(tl + kTok + c0, g2);
           tmem_ld_wait();
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
@@ -559,7 +568,9 @@ __global__ void __launch_bounds__(192, 1)
               } else {
                 yrow = p.y + (int64_t)(p.y_rowmap ? p.y_rowmap[row0 + tok] : row0 + tok) * p.H;
               }
-              yrow[nt * 128 + f] = __float2bfloat16_rn(__uint_as_float(g[j]));
+              yrow[nt * p.nt_stride + f] = __float2bfloat16_rn(__uint_as_float(g[j]));
+              if constexpr (MODE == kModeW2Pair)
+                yrow[nt * p.nt_stride + p.up_off + f] = __float2bfloat16_rn(__uint_as_float(g2[j]));
             }
           }
         }
@@ -634,10 +645,10 @@ int sm_count() {
   return n;
 }
 
-template <bool PAIRED>
+template <int MODE>
 cudaError_t launch_grouped(const CUtensorMap& mw, const CUtensorMap& ma, const GemmArgs& a, cudaStream_t st) {
-  using C = Cfg<PAIRED>;
-  auto kern = grouped_gemm_kernel<PAIRED>;
+  using C = Cfg<MODE>;
+  auto kern = grouped_gemm_kernel<MODE>;
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
@@ -716,18 +727,24 @@ int bs_launch_moe_experts(int E, int64_t rows, int H, int I, const uint8_t* ap, 
       !moe::make_weight_map(&mw2, w2, E, H, I) || !moe::make_act_map(&ma2, hq, rows, I))
     return BS_ERR_UNSUPPORTED;
   moe::GemmArgs a1 = {};
-  a1.E = E; a1.K = H; a1.n_tiles = I / 128; a1.w_rows = 2 * I; a1.up_off = I;
+  a1.E = E; a1.K = H; a1.n_tiles = I / 128; a1.w_rows = 2 * I; a1.up_off = I; a1.nt_stride = 128;
   a1.offsets = offsets; a1.chunk_prefix = chunk_prefix; a1.w_sp = w13_sp; a1.a_sp = asp;
   a1.hq = hq; a1.hs_p = hs_p; a1.I = I; a1.y = nullptr; a1.H = H;
-  *cerr = moe::launch_grouped<true>(mw1, ma1, a1, st);
+  *cerr = moe::launch_grouped<moe::kModeW13>(mw1, ma1, a1, st);
   if (*cerr != cudaSuccess) return BS_ERR_CUDA;
   moe::GemmArgs a2 = {};
-  a2.E = E; a2.K = I; a2.n_tiles = H / 128; a2.w_rows = H; a2.up_off = 0;
+  // two adjacent 128-row W2 tiles per item when H allows it
+  const bool w2_pair = (H / 128) % 2 == 0;
+  a2.E = E; a2.K = I; a2.w_rows = H;
+  a2.n_tiles = w2_pair ? H / 256 : H / 128;
+  a2.up_off = w2_pair ? 128 : 0;
+  a2.nt_stride = w2_pair ? 256 : 128;
   a2.offsets = offsets; a2.chunk_prefix = chunk_prefix; a2.w_sp = w2_sp; a2.a_sp = hs_p;
   a2.hq = nullptr; a2.hs_p = nullptr; a2.I = I; a2.y = y; a2.H = H; a2.y_rowmap = y_rowmap;
   a2.ret = ret;
   for (int q = 0; q < n_ranks && q < 8; ++q) a2.y_ranks[q] = reinterpret_cast<__nv_bfloat16*>(y_ranks[q]);
-  *cerr = moe::launch_grouped<false>(mw2, ma2, a2, st);
+  *cerr = w2_pair ? moe::launch_grouped<moe::kModeW2Pair>(mw2, ma2, a2, st)
+                  : moe::launch_grouped<moe::kModeW2>(mw2, ma2, a2, st);
   return *cerr == cudaSuccess ? 0 : BS_ERR_CUDA;
 }
 

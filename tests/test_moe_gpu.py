@@ -47,7 +47,8 @@ def test_moe_golden_small(golden):
     check(out, golden["moe/small/out"], "moe golden small")
 
 
-@pytest.mark.parametrize("T,H,inter,E,topk", [(64, 512, 256, 16, 4), (300, 256, 256, 4, 2), (200, 1024, 512, 32, 8), (500, 512, 256, 2, 1)])
+@pytest.mark.parametrize("T,H,inter,E,topk", [(64, 512, 256, 16, 4), (300, 256, 256, 4, 2), (200, 1024, 512, 32, 8),
+                                              (500, 512, 256, 2, 1), (100, 384, 256, 4, 2)])
 def test_moe_vs_oracle(T, H, inter, E, topk):
     m = cases.moe_case_small(T=T, H=H, inter=inter, E=E, topk=topk, seed=T + E)
     ref = ob.moe_layer(m["x"], m["idx"], m["w"], m["w13"], m["w13_s"], m["w2"], m["w2_s"])

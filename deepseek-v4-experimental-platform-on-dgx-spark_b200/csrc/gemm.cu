@@ -272,44 +272,74 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN>::kThreads, 1)
           tc_cp_32x128b_warpx4(tmem_base + sfa_col + 4 * b, sdesc_sf_chunk(smem_u32(sf_const) + 512 * b));
       __syncwarp();
     }
-    for (int it = 0; it < n_kb; ++it) {
-      const int st = it / C::kKps, sub = it % C::kKps;
-      const int s = st % C::kStages;
-      const uint32_t ph = (st / C::kStages) & 1;
-      const int buf = it % C::kPBufs;
-      const uint32_t pph = (it / C::kPBufs) & 1;
-      bool ok = sub != 0 || mbar_wait(&full[s], ph, abort_flag);
-      ok = ok && mbar_wait(&pempty[buf], pph ^ 1, abort_flag);
-      if (!__all_sync(0xffffffffu, ok)) break;
-      tc_fence_after();
-      if (elect_one()) {
-        const uint32_t sx = smem_u32(stage_base + s * C::kStageBytes) + sub * C::kXSub;
-        const uint32_t sy = smem_u32(stage_base + s * C::kStageBytes) + C::kXBytes + sub * C::kYSub;
-        const uint32_t d = tmem_base + buf * BN;
-        if constexpr (FP4) {
-          const uint32_t wslot = tmem_base + sfw_col0 + (it & 1) * C::kSfWCols;
-          const uint32_t sfs = smem_u32(sf_base + (s * C::kKps + sub) * C::kSfSub);
-          for (int b = 0; b < C::kWChunks; ++b) tc_cp_32x128b_warpx4(wslot + 4 * b, sdesc_sf_chunk(sfs + 512 * b));
-          // X is the weights in swap mode, the activations otherwise
-          const uint32_t sfa = SWAP ? wslot : tmem_base + sfa_col;
-          const uint32_t sfb = SWAP ? tmem_base + sfa_col : wslot;
+    // issue the MMAs of K block `it` (stage slot s, sub-block sub) into
+    // partial buffer `buf`; called by one elected thread
+    auto issue_kb = [&](int it, int s, int sub, int buf) {
+      const uint32_t sx = smem_u32(stage_base + s * C::kStageBytes) + sub * C::kXSub;
+      const uint32_t sy = smem_u32(stage_base + s * C::kStageBytes) + C::kXBytes + sub * C::kYSub;
+      const uint32_t d = tmem_base + buf * BN;
+      if constexpr (FP4) {
+        const uint32_t wslot = tmem_base + sfw_col0 + (it & 1) * C::kSfWCols;
+        const uint32_t sfs = smem_u32(sf_base + (s * C::kKps + sub) * C::kSfSub);
+        for (int b = 0; b < C::kWChunks; ++b) tc_cp_32x128b_warpx4(wslot + 4 * b, sdesc_sf_chunk(sfs + 512 * b));
+        // X is the weights in swap mode, the activations otherwise
+        const uint32_t sfa = SWAP ? wslot : tmem_base + sfa_col;
+        const uint32_t sfb = SWAP ? tmem_base + sfa_col : wslot;
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const uint32_t idesc =
-                idesc_mxf8f6f4(C::kXFp4 ? 5 : 0, C::kYFp4 ? 5 : 0, 128, BN, k, k);
-            tc_mma_mxf8f6f4(d, sdesc_k128_sw128(sx + k * 32), sdesc_k128_sw128(sy + k * 32), idesc,
-                            sfa | ((uint32_t)k << 30), sfb | ((uint32_t)k << 30), k > 0 ? 1u : 0u);
-          }
-        } else {
-          constexpr uint32_t idesc = idesc_f8f6f4(0, 0, 128, BN);
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            tc_mma_f8f6f4(d, sdesc_k128_sw128(sx + k * 32), sdesc_k128_sw128(sy + k * 32), idesc, k > 0 ? 1u : 0u);
+        for (int k = 0; k < 4; ++k) {
+          const uint32_t idesc = idesc_mxf8f6f4(C::kXFp4 ? 5 : 0, C::kYFp4 ? 5 : 0, 128, BN, k, k);
+          tc_mma_mxf8f6f4(d, sdesc_k128_sw128(sx + k * 32), sdesc_k128_sw128(sy + k * 32), idesc,
+                          sfa | ((uint32_t)k << 30), sfb | ((uint32_t)k << 30), k > 0 ? 1u : 0u);
         }
-        if (sub == C::kKps - 1 || it == n_kb - 1) tc_commit(&empty[s]);
-        tc_commit(&pfull[buf]);
+      } else {
+        constexpr uint32_t idesc = idesc_f8f6f4(0, 0, 128, BN);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          tc_mma_f8f6f4(d, sdesc_k128_sw128(sx + k * 32), sdesc_k128_sw128(sy + k * 32), idesc, k > 0 ? 1u : 0u);
       }
-      __syncwarp();
+      tc_commit(&pfull[buf]);
+    };
+    if constexpr (SWAP) {
+      // decode: one full wait and one issue block per stage (both K blocks);
+      // partial buffers not yet used in this launch need no wait
+      const int n_st = (n_kb + C::kKps - 1) / C::kKps;
+      for (int st = 0; st < n_st; ++st) {
+        const int s = st % C::kStages;
+        const uint32_t ph = (st / C::kStages) & 1;
+        bool ok = mbar_wait(&full[s], ph, abort_flag);
+        for (int sub = 0; sub < C::kKps; ++sub) {
+          const int it = st * C::kKps + sub;
+          if (it < n_kb && it >= C::kPBufs)
+            ok = ok && mbar_wait(&pempty[it % C::kPBufs], ((it / C::kPBufs) & 1) ^ 1, abort_flag);
+        }
+        if (!__all_sync(0xffffffffu, ok)) break;
+        tc_fence_after();
+        if (elect_one()) {
+          for (int sub = 0; sub < C::kKps; ++sub) {
+            const int it = st * C::kKps + sub;
+            if (it < n_kb) issue_kb(it, s, sub, it % C::kPBufs);
+          }
+          tc_commit(&empty[s]);
+        }
+        __syncwarp();
+      }
+    } else {
+      for (int it = 0; it < n_kb; ++it) {
+        const int st = it / C::kKps, sub = it % C::kKps;
+        const int s = st % C::kStages;
+        const uint32_t ph = (st / C::kStages) & 1;
+        const int buf = it % C::kPBufs;
+        const uint32_t pph = (it / C::kPBufs) & 1;
+        bool ok = sub != 0 || mbar_wait(&full[s], ph, abort_flag);
+        ok = ok && mbar_wait(&pempty[buf], pph ^ 1, abort_flag);
+        if (!__all_sync(0xffffffffu, ok)) break;
+        tc_fence_after();
+        if (elect_one()) {
+          issue_kb(it, s, sub, buf);
+          if (sub == C::kKps - 1 || it == n_kb - 1) tc_commit(&empty[s]);
+        }
+        __syncwarp();
+      }
     }
   } else {
     // ------------------------------------------------------------ epilogue

@@ -64,14 +64,19 @@ BS_DEVINL float load_scale(const void* p, int dtype, int64_t idx) {
   return bs_e8m0_to_f32(__ldg(reinterpret_cast<const uint8_t*>(p) + idx));
 }
 
-template <bool SWAP, bool FP4, int BN>
+// TWO (decode only): two CTAs per SM with a 2-stage ring, for launches whose
+// CTAs outnumber half the SMs -- at one CTA per SM the next call's CTAs could
+// not become resident early to stream their weights (programmatic dependent
+// launch) while this call runs.
+template <bool SWAP, bool FP4, int BN, bool TWO = false>
 struct Cfg {
   static constexpr int kBM = 128;                       // MMA M (rows of X)
   // Each pipeline stage carries two 128-wide K blocks, fetched by one 3-D TMA
   // box per operand: measured L2->SM throughput is ~100 B/clk/SM with two K
   // blocks per box against ~50-75 with one (per-copy cost dominates).
   static constexpr int kKps = 2;                        // K blocks per stage
-  static constexpr int kStages = SWAP ? 4 : (BN == 256 ? 2 : 3);
+  static constexpr int kStages = SWAP ? (TWO ? 2 : 4) : (BN == 256 ? 2 : 3);
+  static constexpr int kMinBlocks = TWO ? 2 : 1;
   static constexpr int kXSub = kBM * 128;               // one K block of X in smem (e2m1 unpacked to 1 B/elem)
   static constexpr int kYSub = BN * 128;
   static constexpr int kXBytes = kXSub * kKps;
@@ -102,11 +107,15 @@ struct Cfg {
   // TMEM partial buffers: normal mode double-buffers its wide tile; the
   // narrow decode tile keeps 4-8 so the MMA runs through a whole split-K
   // range without waiting for the per-K-block promotion.
-  static constexpr int kPBufs = SWAP ? (BN <= 32 ? 8 : 4) : 2;
+  // (TWO: the two CTAs of an SM share its 512 TMEM columns, so each keeps to
+  // 256 -- a CTA whose allocation waited on its SM neighbour while both sit
+  // in one cluster would wait forever at the cluster barrier)
+  static constexpr int kPBufs = SWAP ? (TWO ? (BN == 16 ? 8 : BN == 32 ? 7 : 3) : (BN <= 32 ? 8 : 4)) : 2;
   static constexpr int kTmemNeed = kPBufs * BN + 2 * kSfWCols + kSfACols;
   static constexpr int kTmemCols = kTmemNeed <= 32 ? 32 : kTmemNeed <= 64 ? 64 : kTmemNeed <= 128 ? 128
                                    : kTmemNeed <= 256 ? 256 : 512;
   static_assert(kTmemNeed <= 512, "TMEM budget");
+  static_assert(!TWO || (SWAP && kTmemCols <= 256), "two CTAs per SM must share TMEM");
   static_assert(SWAP || kStages * (kXBytes + kYBytes) >= kBM * (BN + 8) * 2, "output staging fits the ring");
   // Shared memory: [align slack | operand ring | SF ring | constant SF |
   // column scales | receive buffer | barriers].  The last two variable parts
@@ -121,10 +130,10 @@ struct Cfg {
   }
 };
 
-template <bool SWAP, bool FP4, int BN>
-__global__ void __launch_bounds__(Cfg<SWAP, FP4, BN>::kThreads, 1)
+template <bool SWAP, bool FP4, int BN, bool TWO>
+__global__ void __launch_bounds__(Cfg<SWAP, FP4, BN, TWO>::kThreads, Cfg<SWAP, FP4, BN, TWO>::kMinBlocks)
     bsg_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_y, GemmArgs p) {
-  using C = Cfg<SWAP, FP4, BN>;
+  using C = Cfg<SWAP, FP4, BN, TWO>;
   extern __shared__ uint8_t smem_raw[];
   // 1 KB alignment by offsetting smem_raw itself, so that every buffer
   // carved from it stays in the shared address space for the compiler
@@ -605,12 +614,17 @@ int max_dyn_smem() {
   return v;
 }
 
-template <bool SWAP, bool FP4, int BN>
+template <bool SWAP, bool FP4, int BN, bool TWO>
 cudaError_t prepare_kernel() {
   static bool done = false;
   if (!done) {
-    auto kern = bsg_kernel<SWAP, FP4, BN>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, max_dyn_smem());
+    auto kern = bsg_kernel<SWAP, FP4, BN, TWO>;
+    // the opt-in limit covers static plus dynamic shared memory
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, kern);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             max_dyn_smem() - (int)fa.sharedSizeBytes);
     if (e != cudaSuccess) return e;
     if (SWAP) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     done = true;
@@ -618,12 +632,12 @@ cudaError_t prepare_kernel() {
   return cudaSuccess;
 }
 
-template <bool SWAP, bool FP4, int BN>
+template <bool SWAP, bool FP4, int BN, bool TWO = false>
 cudaError_t launch(const CUtensorMap& mx, const CUtensorMap& my, const GemmArgs& a, dim3 grid, int split,
                    cudaStream_t st) {
-  using C = Cfg<SWAP, FP4, BN>;
-  auto kern = bsg_kernel<SWAP, FP4, BN>;
-  cudaError_t e = prepare_kernel<SWAP, FP4, BN>();
+  using C = Cfg<SWAP, FP4, BN, TWO>;
+  auto kern = bsg_kernel<SWAP, FP4, BN, TWO>;
+  cudaError_t e = prepare_kernel<SWAP, FP4, BN, TWO>();
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
@@ -646,13 +660,13 @@ cudaError_t launch(const CUtensorMap& mx, const CUtensorMap& my, const GemmArgs&
 }
 
 // Co-resident clusters of `split` swap-mode CTAs (cached per configuration).
-template <bool FP4, int BN>
+template <bool FP4, int BN, bool TWO>
 int max_clusters_t(int split) {
   static int cache[9] = {0};
   if (cache[split]) return cache[split];
-  using C = Cfg<true, FP4, BN>;
-  auto kern = bsg_kernel<true, FP4, BN>;
-  prepare_kernel<true, FP4, BN>();
+  using C = Cfg<true, FP4, BN, TWO>;
+  auto kern = bsg_kernel<true, FP4, BN, TWO>;
+  prepare_kernel<true, FP4, BN, TWO>();
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(1, 1, split);
   cfg.blockDim = dim3(C::kThreads, 1, 1);
@@ -673,23 +687,45 @@ int max_clusters_t(int split) {
   return n;
 }
 
-// Does a swap-mode launch with this split fit in shared memory?
-bool decode_smem_fits(bool fp4, int bn, int split, int kb_per_split) {
-  int need;
-  if (fp4) need = bn == 16 ? Cfg<true, true, 16>::smem_bytes(split, kb_per_split)
-                : bn == 32 ? Cfg<true, true, 32>::smem_bytes(split, kb_per_split)
-                           : Cfg<true, true, 64>::smem_bytes(split, kb_per_split);
-  else need = bn == 16 ? Cfg<true, false, 16>::smem_bytes(split, kb_per_split)
-              : bn == 32 ? Cfg<true, false, 32>::smem_bytes(split, kb_per_split)
-                         : Cfg<true, false, 64>::smem_bytes(split, kb_per_split);
-  return need <= max_dyn_smem();
+// Dynamic shared memory one CTA may use when two must share an SM.
+int two_cta_smem_limit() {
+  static int v = 0;
+  if (!v) {
+    int dev = 0, per_sm = 0, reserved = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+    cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+    v = per_sm / 2 - reserved;
+  }
+  return v;
 }
 
-int max_clusters(bool fp4, int bn, int split) {
-  if (fp4) return bn == 16 ? max_clusters_t<true, 16>(split) : bn == 32 ? max_clusters_t<true, 32>(split)
-                                                                        : max_clusters_t<true, 64>(split);
-  return bn == 16 ? max_clusters_t<false, 16>(split) : bn == 32 ? max_clusters_t<false, 32>(split)
-                                                               : max_clusters_t<false, 64>(split);
+template <bool FP4, bool TWO>
+int decode_smem_need(int bn, int split, int kb_per_split) {
+  return bn == 16 ? Cfg<true, FP4, 16, TWO>::smem_bytes(split, kb_per_split)
+         : bn == 32 ? Cfg<true, FP4, 32, TWO>::smem_bytes(split, kb_per_split)
+                    : Cfg<true, FP4, 64, TWO>::smem_bytes(split, kb_per_split);
+}
+
+// Does a swap-mode launch with this split fit in shared memory?
+bool decode_smem_fits(bool fp4, int bn, int split, int kb_per_split, bool two) {
+  int need;
+  if (two) need = fp4 ? decode_smem_need<true, true>(bn, split, kb_per_split)
+                      : decode_smem_need<false, true>(bn, split, kb_per_split);
+  else need = fp4 ? decode_smem_need<true, false>(bn, split, kb_per_split)
+                  : decode_smem_need<false, false>(bn, split, kb_per_split);
+  return need <= (two ? two_cta_smem_limit() : max_dyn_smem());
+}
+
+template <bool FP4, bool TWO>
+int max_clusters_b(int bn, int split) {
+  return bn == 16 ? max_clusters_t<FP4, 16, TWO>(split) : bn == 32 ? max_clusters_t<FP4, 32, TWO>(split)
+                                                                   : max_clusters_t<FP4, 64, TWO>(split);
+}
+
+int max_clusters(bool fp4, int bn, int split, bool two) {
+  if (two) return fp4 ? max_clusters_b<true, true>(bn, split) : max_clusters_b<false, true>(bn, split);
+  return fp4 ? max_clusters_b<true, false>(bn, split) : max_clusters_b<false, false>(bn, split);
 }
 
 }  // namespace
@@ -744,22 +780,41 @@ int bs_launch_gemm(bool fp4, const void* a, const void* a_s, int as_dtype, const
     const int y_tiles = (int)((M + bn - 1) / bn);
     // Largest split-K (2..8, a thread-block cluster along K) whose clusters
     // all fit on the GPU at once, so the grid runs in one wave; at least two
-    // K blocks per CTA.
-    int split = 1;
-    for (int sp = 8; sp >= 2; sp /= 2) {
-      if (nkb % sp || nkb / sp < 2) continue;
-      if (x_tiles * y_tiles <= max_clusters(fp4, bn, sp)) { split = sp; break; }
-    }
+    // K blocks per CTA.  When the CTAs outnumber half the SMs, two calls in a
+    // row could not be resident together at one CTA per SM, so the next
+    // call could not stream its weights early: for up to 16 tokens use the
+    // two-CTAs-per-SM form with a 4-way split (2-stage ring; measured 7.2 ->
+    // 6.6 us at N=4096 and 8.9 -> 7.9 us at N=7168; slower than one CTA per
+    // SM at N=2048, and with the fewer TMEM partial buffers that 32 and 64
+    // tokens leave it is slower there too).  The cluster co-residency check
+    // only aims at one wave; a cluster's own CTAs are always co-resident.
+    auto pick = [&](bool two) {
+      for (int sp = two ? 4 : 8; sp >= 2; sp /= 2) {
+        if (nkb % sp || nkb / sp < 2) continue;
+        if (x_tiles * y_tiles <= max_clusters(fp4, bn, sp, two)) return sp;
+      }
+      return 1;
+    };
+    int split = pick(false);
+    bool two = bn == 16 && x_tiles * y_tiles * split > num_sms() / 2;
+    if (two) split = (nkb % 4 == 0 && nkb / 4 >= 2) ? 4 : pick(true);
     // shared memory holds the column scales of a split's K range and the
     // receive buffer of the split-K reduction: the first shrinks with the
     // split, the second grows with it
-    auto fits = [&](int sp) { return decode_smem_fits(fp4, bn, sp, (nkb + sp - 1) / sp); };
+    auto fits = [&](int sp) { return decode_smem_fits(fp4, bn, sp, (nkb + sp - 1) / sp, two); };
     while (split > 1 && !fits(split)) split /= 2;
     while (!fits(split) && split < 8 && nkb % (2 * split) == 0) split *= 2;
+    if (two && !fits(split)) {
+      two = false;
+      split = pick(false);
+      while (split > 1 && !fits(split)) split /= 2;
+      while (!fits(split) && split < 8 && nkb % (2 * split) == 0) split *= 2;
+    }
     if (!fits(split)) return BS_ERR_UNSUPPORTED;
     args.kb_per_split = (nkb + split - 1) / split;
     dim3 grid(x_tiles, y_tiles, split);
-#define BS_DEC(F, B) *cerr = launch<true, F, B>(mx, my, args, grid, split, st)
+#define BS_DEC(F, B) *cerr = two ? launch<true, F, B, true>(mx, my, args, grid, split, st) \
+                                : launch<true, F, B, false>(mx, my, args, grid, split, st)
     if (fp4) {
       if (bn == 16) BS_DEC(true, 16); else if (bn == 32) BS_DEC(true, 32); else BS_DEC(true, 64);
     } else {

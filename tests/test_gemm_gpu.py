@@ -70,7 +70,8 @@ def test_fp4_decode_sweep(pkg, M, N):
     np.testing.assert_array_equal(bits(run_fp4(pkg, c)), bits(out))  # deterministic
 
 
-@pytest.mark.parametrize("shape", [(1, 256, 512), (16, 384, 1024), (64, 1024, 4096), (33, 200, 384)])
+@pytest.mark.parametrize("shape", [(1, 256, 512), (16, 384, 1024), (64, 1024, 4096), (33, 200, 384),
+                                   (16, 4096, 2048), (64, 4096, 1024), (32, 7168, 4096)])
 def test_fp8_decode_vs_oracle(pkg, shape):
     M, N, K = shape
     rng = np.random.default_rng(M * 7 + N)

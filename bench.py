@@ -595,6 +595,27 @@ def cpu_fp8_prefill(steps: int, warmup: int, m_rows: int = 4096):
     return 2.0 * m_rows * 4096 * 4096 / s / 1e12, s
 
 
+def cpu_fp4_decode(M: int, N: int, K: int = 4096, steps: int = 3):
+    """The oracle's fp4_gemm (the reference CPU path: LUT dequant of all of B ->
+    bf16 -> matmul) on the decode shape; GB/s of the same bytes the GPU line
+    counts."""
+    from oracle import blockscaled as ob
+    rng = np.random.default_rng(77)
+    x = ob.f32_to_bf16(rng.standard_normal((M, K)).astype(np.float32))
+    a, a_s = ob.act_quant(x, ob.DT_BF16, 128, None, ob.DT_F32)
+    b = rng.integers(0, 256, size=(N, K // 2), dtype=np.uint8)
+    b_s = (127 - rng.integers(0, 7, size=(N, K // 32))).astype(np.uint8)
+    ob.fp4_gemm(a, a_s, b, b_s, ob.DT_F32, ob.DT_E8M0)
+    times = []
+    for _ in range(steps):
+        t = time.perf_counter()
+        ob.fp4_gemm(a, a_s, b, b_s, ob.DT_F32, ob.DT_E8M0)
+        times.append(time.perf_counter() - t)
+    s = min(times)
+    byts = N * K // 2 + N * K // 32 + M * K + 4 * M * K // 128 + 2 * M * N
+    return byts / s / 1e9, s
+
+
 def zipf_bias(torch, E, seed):
     """Expert popularity skew of the long-prefill config: -1.2*ln(1 + rank of e)
     under a seeded permutation of the experts (a Zipf(1.2)-like stand-in)."""
@@ -803,6 +824,12 @@ def main():
     else:
         line = bench_fp4_decode(args, torch, dist, ws, rank, dev)
 
+    if rank == 0 and ws == 1 and args.workload == "fp4_decode" and not args.no_cpu_baseline:
+        torch.set_num_threads(cpu_threads())
+        v, s = cpu_fp4_decode(args.m, args.n)
+        line["cpu_baseline"] = {"value": round(v, 3), "unit": "GB/s", "cores": cpu_threads(), "kind": "port",
+                                "sample": f"fp4_gemm M={args.m} N={args.n} K=4096 on the host ({s * 1e3:.1f} ms per "
+                                          "call): LUT dequant of all of B -> bf16 -> fp32 matmul (numpy), best of 3"}
     if rank == 0 and ws == 1 and args.workload == "fp8_prefill" and not args.no_cpu_baseline:
         torch.set_num_threads(cpu_threads())
         v, s = cpu_fp8_prefill(1, 0, m_rows=4096)

@@ -137,15 +137,15 @@ def make_fp8_prefill(torch, dev, M, N, K, seed, n_sets):
 
 
 class pipelined_e2e:
-    """e2e steps of the single-GPU prefill on three streams with two buffers:
-    step i copies the pinned host activations in (stream in), quantises and
-    multiplies through the public act_quant / fp8_gemm (stream compute) and
-    copies C out to pinned host memory (stream out).  Step i+2 reuses step
-    i's buffers only after step i's compute and copy-out are done, so steps
-    overlap without sharing data."""
+    """Single-GPU e2e steps on three streams with two buffers: step i copies
+    the pinned host activations in (stream in), runs `compute(i, x_dev)`
+    through the public API (stream compute) and copies the result out to
+    pinned host memory (stream out).  Step i+2 reuses step i's buffers only
+    after step i's compute and copy-out are done, so steps overlap without
+    sharing data."""
 
-    def __init__(self, torch, pkg, x_host, out_shape, b, b_s):
-        self.torch, self.pkg, self.x_host, self.b, self.b_s = torch, pkg, x_host, b, b_s
+    def __init__(self, torch, x_host, out_shape, compute):
+        self.torch, self.x_host, self.compute = torch, x_host, compute
         dev = torch.device("cuda", torch.cuda.current_device())
         self.x_dev = [torch.empty(x_host.shape, dtype=x_host.dtype, device=dev) for _ in range(2)]
         self.o_host = [torch.empty(out_shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
@@ -167,8 +167,7 @@ class pipelined_e2e:
             self.in_done[b].record()
         with torch.cuda.stream(self.s_comp):
             self.s_comp.wait_event(self.in_done[b])
-            a, a_s = self.pkg.act_quant(self.x_dev[b], 128)
-            c = self.pkg.fp8_gemm(a, a_s, self.b, self.b_s)
+            c = self.compute(i, self.x_dev[b])
             c.record_stream(self.s_out)
             self.comp_done[b].record()
         with torch.cuda.stream(self.s_out):
@@ -291,7 +290,8 @@ def bench_fp8_prefill(args, torch, dist, ws, rank, dev):
         # one GPU: consecutive steps overlap on three streams (inputs in,
         # compute, result out; two buffers each), as a serving loop would run
         # them; every step still copies its own input in and its result out
-        e2e_step = pipelined_e2e(torch, pkg, x_host, o_host.shape, b_loc, s_loc)
+        e2e_step = pipelined_e2e(torch, x_host, o_host.shape,
+                                 lambda i, xd: pkg.fp8_gemm(*pkg.act_quant(xd, 128), b_loc, s_loc))
     for i in range(2):
         e2e_step(i)
     torch.cuda.synchronize()
@@ -422,6 +422,37 @@ def bench_fp4_decode(args, torch, dist, ws, rank, dev):
     e1.record()
     torch.cuda.synchronize()
     ms_eager = e0.elapsed_time(e1) / steps
+    # end to end through the public API, as a decode loop runs it: each call
+    # copies its bf16 activations in from pinned host memory, runs act_quant
+    # and fp4_gemm (rotating resident weights) and copies its output back to
+    # pinned host memory; the calls are captured once in a CUDA graph
+    wv = [(b.view(torch.float4_e2m1fn_x2), bs.view(torch.float8_e8m0fnu)) for b, bs in ws_]
+    x_host = x.cpu().pin_memory()
+    o_host = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty_like(x)
+
+    def e2e_call(i):
+        x_dev.copy_(x_host, non_blocking=True)
+        o_host.copy_(pkg.fp4_gemm(*pkg.act_quant(x_dev, 128), *wv[i % n_sets]), non_blocking=True)
+
+    for i in range(2):
+        e2e_call(i)
+    torch.cuda.synchronize()
+    g_e2e = torch.cuda.CUDAGraph()
+    cap.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(cap):
+        with torch.cuda.graph(g_e2e, stream=cap):
+            for i in range(steps):
+                e2e_call(i)
+    torch.cuda.current_stream().wait_stream(cap)
+    g_e2e.replay()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        g_e2e.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / (reps * steps)
     nbytes = N * K // 2 + N * K // 32 + M * K + 4 * M * K // 128 + 2 * M * N
     gbs = nbytes / (ms * 1e-3) / 1e9
     peaks, src = load_peaks()
@@ -433,6 +464,11 @@ def bench_fp4_decode(args, torch, dist, ws, rank, dev):
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(gbs / peaks["hbm_gbs"], 3),
                          "traffic": NCU_TRAFFIC.get(f"fp4_decode_{M}x{N}x{K}"), "peak_source": src},
+            "e2e": {"value": round(nbytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                    "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2,
+                    "ms_per_step": round(e2e_ms, 5),
+                    "path": "act_quant + fp4_gemm public API per call with pinned host copies in and out, "
+                            "calls replayed from one CUDA graph"},
             "gpu_launches": steps * reps, "clocks": clk,
             "eager_ms_per_call": round(ms_eager, 5)}
 

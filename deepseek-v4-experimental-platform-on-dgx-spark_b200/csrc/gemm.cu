@@ -99,8 +99,10 @@ struct Cfg {
   // normal mode: one epilogue warp per (TMEM lane quadrant, 64-column group),
   // so BN=256 has 16 epilogue warps, 4 per SM sub-partition, to keep the
   // per-K-block promotion (TMEM load + FMA of the partial) ahead of the MMA
-  static constexpr int kEpiWarps = SWAP ? 4 : 4 * (BN / 64);
-  static constexpr int kCols = SWAP ? BN : 64;          // columns per epilogue warp
+  // decode: one warp per TMEM lane quadrant and group of up to 32 token
+  // columns (64 tokens: 8 warps), so the per-K-block promotion stays short
+  static constexpr int kEpiWarps = SWAP ? 4 * (BN > 32 ? BN / 32 : 1) : 4 * (BN / 64);
+  static constexpr int kCols = SWAP ? (BN > 32 ? 32 : BN) : 64;   // columns per epilogue warp
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
   static constexpr int kSfWCols = FP4 ? 4 * kWChunks : 0;   // TMEM columns per weights' SF slot (2 slots)
   static constexpr int kSfACols = FP4 ? 4 * kAChunks : 0;   // TMEM columns of the constant activation SF
@@ -437,7 +439,7 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN, TWO>::kThreads, Cfg<SWAP, F
         tmem_ld_wait();
         const int nj = (c + 1 < C::kCols / 16) ? 32 : 16;
         if constexpr (SWAP) {
-          const float* cs = col_scale + it * BN + c * 16;
+          const float* cs = col_scale + it * BN + col0 + c * 16;
 #pragma unroll
           for (int j = 0; j < 32; ++j)
             if (j < nj) acc[c * 16 + j] = fmaf(__uint_as_float(r[j]), rs * cs[j], acc[c * 16 + j]);
@@ -495,7 +497,7 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN, TWO>::kThreads, Cfg<SWAP, F
         // 16-byte row chunks
         __nv_bfloat16* tile = reinterpret_cast<__nv_bfloat16*>(stage_base);
 #pragma unroll
-        for (int j = 0; j < BN; ++j) tile[j * C::kBM + row] = __float2bfloat16_rn(acc[j]);
+        for (int j = 0; j < C::kCols; ++j) tile[(col0 + j) * C::kBM + row] = __float2bfloat16_rn(acc[j]);
         asm volatile("bar.sync 1, %0;" ::"r"(32 * C::kEpiWarps) : "memory");
         write_tile(tile, C::kBM, x0);
       }
@@ -518,18 +520,19 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN, TWO>::kThreads, Cfg<SWAP, F
       cluster_wait();
       if (owner != me) {
         const int slot = me < owner ? me : me - 1;
-        const uint32_t dst = mapa_shared(smem_u32(recv + (slot * rows_per + rl) * BN), (uint32_t)owner);
+        const uint32_t dst = mapa_shared(smem_u32(recv + (slot * rows_per + rl) * BN + col0), (uint32_t)owner);
         const uint32_t bar = mapa_shared(smem_u32(recv_bar), (uint32_t)owner);
 #pragma unroll
-        for (int j = 0; j < BN; j += 4) st_async_f4(dst + j * 4, acc[j], acc[j + 1], acc[j + 2], acc[j + 3], bar);
+        for (int j = 0; j < C::kCols; j += 4)
+          st_async_f4(dst + j * 4, acc[j], acc[j + 1], acc[j + 2], acc[j + 3], bar);
       } else {
         // every peer always pushes (also after an abort), so this wait does
         // not take the abort flag: the CTA must not exit while peers write
         // into its shared memory
         mbar_spin(recv_bar, 0);
-        const uint32_t rbase = smem_u32(recv) + (uint32_t)(rl * BN) * 4u;
+        const uint32_t rbase = smem_u32(recv) + (uint32_t)(rl * BN + col0) * 4u;
 #pragma unroll
-        for (int j = 0; j < BN; j += 4) {
+        for (int j = 0; j < C::kCols; j += 4) {
           float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
           for (int q = 0; q < S; ++q) {
             const int slot = q < me ? q : q - 1;
@@ -537,10 +540,10 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN, TWO>::kThreads, Cfg<SWAP, F
                                      : ld_shared_f4(rbase + (uint32_t)(slot * rows_per * BN + j) * 4u);
             t.x += v.x; t.y += v.y; t.z += v.z; t.w += v.w;
           }
-          tile[(j + 0) * rows_per + rl] = __float2bfloat16_rn(t.x);
-          tile[(j + 1) * rows_per + rl] = __float2bfloat16_rn(t.y);
-          tile[(j + 2) * rows_per + rl] = __float2bfloat16_rn(t.z);
-          tile[(j + 3) * rows_per + rl] = __float2bfloat16_rn(t.w);
+          tile[(col0 + j + 0) * rows_per + rl] = __float2bfloat16_rn(t.x);
+          tile[(col0 + j + 1) * rows_per + rl] = __float2bfloat16_rn(t.y);
+          tile[(col0 + j + 2) * rows_per + rl] = __float2bfloat16_rn(t.z);
+          tile[(col0 + j + 3) * rows_per + rl] = __float2bfloat16_rn(t.w);
         }
       }
       asm volatile("bar.sync 1, %0;" ::"r"(32 * C::kEpiWarps) : "memory");

@@ -15,6 +15,50 @@
 
 #include "../../include/bsgemm.h"
 
+#include <mutex>
+
+// ---------------------------------------------------------------------------
+// Host-side caches (kernel attributes set, occupancy, device limits): one
+// slot per device, all behind one mutex.  A value is computed outside the
+// lock (two racing threads compute the same value) and stored as value + 1
+// so that 0 means "not yet known".
+// ---------------------------------------------------------------------------
+
+namespace hostcache {
+constexpr int kMaxDevices = 64;
+inline std::mutex& mu() {
+  static std::mutex m;
+  return m;
+}
+inline int device() {
+  int d = -1;
+  if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= kMaxDevices) return -1;
+  return d;
+}
+template <class F>
+int get(int* slots, F&& compute) {
+  const int d = device();
+  if (d >= 0) {
+    std::lock_guard<std::mutex> g(mu());
+    if (slots[d]) return slots[d] - 1;
+  }
+  const int v = compute();
+  if (d >= 0) {
+    std::lock_guard<std::mutex> g(mu());
+    slots[d] = v + 1;
+  }
+  return v;
+}
+inline int device_attr(int* slots, cudaDeviceAttr attr) {
+  return get(slots, [&] {
+    int dev = 0, v = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&v, attr, dev);
+    return v;
+  });
+}
+}  // namespace hostcache
+
 #define BS_DEVINL __device__ __forceinline__
 
 #ifndef BS_SPIN_LIMIT

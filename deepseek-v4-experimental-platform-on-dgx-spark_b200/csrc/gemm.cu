@@ -570,14 +570,14 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 EncodeTiledFn get_encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  if (!fn) {
+  static const EncodeTiledFn fn = [] {   // initialised once, thread-safe
     void* ptr = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(ptr);
-  }
+      return reinterpret_cast<EncodeTiledFn>(ptr);
+    return EncodeTiledFn(nullptr);
+  }();
   return fn;
 }
 
@@ -597,42 +597,31 @@ bool make_map(CUtensorMap* m, const void* base, bool fp4, int64_t K, int64_t row
   return r == CUDA_SUCCESS;
 }
 
-int g_num_sms = 0;
 int num_sms() {
-  if (!g_num_sms) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-  }
-  return g_num_sms;
+  static int slots[hostcache::kMaxDevices];
+  return hostcache::device_attr(slots, cudaDevAttrMultiProcessorCount);
 }
 
 int max_dyn_smem() {
-  static int v = 0;
-  if (!v) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-  }
-  return v;
+  static int slots[hostcache::kMaxDevices];
+  return hostcache::device_attr(slots, cudaDevAttrMaxSharedMemoryPerBlockOptin);
 }
 
 template <bool SWAP, bool FP4, int BN, bool TWO>
 cudaError_t prepare_kernel() {
-  static bool done = false;
-  if (!done) {
+  static int slots[hostcache::kMaxDevices];
+  return (cudaError_t)hostcache::get(slots, [] {
     auto kern = bsg_kernel<SWAP, FP4, BN, TWO>;
     // the opt-in limit covers static plus dynamic shared memory
     cudaFuncAttributes fa;
     cudaError_t e = cudaFuncGetAttributes(&fa, kern);
-    if (e != cudaSuccess) return e;
+    if (e != cudaSuccess) return (int)e;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              max_dyn_smem() - (int)fa.sharedSizeBytes);
-    if (e != cudaSuccess) return e;
+    if (e != cudaSuccess) return (int)e;
     if (SWAP) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    done = true;
-  }
-  return cudaSuccess;
+    return 0;
+  });
 }
 
 template <bool SWAP, bool FP4, int BN, bool TWO = false>
@@ -662,18 +651,16 @@ cudaError_t launch(const CUtensorMap& mx, const CUtensorMap& my, const GemmArgs&
   return cudaLaunchKernelEx(&cfg, kern, mx, my, a);
 }
 
-// Co-resident clusters of `split` swap-mode CTAs (cached per configuration).
+// Co-resident clusters of `split` swap-mode CTAs.
 template <bool FP4, int BN, bool TWO>
-int max_clusters_t(int split) {
-  static int cache[9] = {0};
-  if (cache[split]) return cache[split];
+int max_clusters_query(int split) {
   using C = Cfg<true, FP4, BN, TWO>;
   auto kern = bsg_kernel<true, FP4, BN, TWO>;
   prepare_kernel<true, FP4, BN, TWO>();
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(1, 1, split);
   cfg.blockDim = dim3(C::kThreads, 1, 1);
-  cfg.dynamicSmemBytes = C::smem_bytes(split, 1);   // one CTA per SM at any split
+  cfg.dynamicSmemBytes = C::smem_bytes(split, 1);
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
@@ -686,21 +673,21 @@ int max_clusters_t(int split) {
     cudaGetLastError();
     n = num_sms() / split;
   }
-  cache[split] = n;
   return n;
+}
+
+// ... cached per device and configuration.
+template <bool FP4, int BN, bool TWO>
+int max_clusters_t(int split) {
+  static int slots[9][hostcache::kMaxDevices];
+  return hostcache::get(slots[split], [split] { return max_clusters_query<FP4, BN, TWO>(split); });
 }
 
 // Dynamic shared memory one CTA may use when two must share an SM.
 int two_cta_smem_limit() {
-  static int v = 0;
-  if (!v) {
-    int dev = 0, per_sm = 0, reserved = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
-    cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev);
-    v = per_sm / 2 - reserved;
-  }
-  return v;
+  static int per_sm[hostcache::kMaxDevices], reserved[hostcache::kMaxDevices];
+  return hostcache::device_attr(per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor) / 2 -
+         hostcache::device_attr(reserved, cudaDevAttrReservedSharedMemoryPerBlock);
 }
 
 template <bool FP4, bool TWO>
@@ -742,12 +729,11 @@ int bs_launch_fp8_gemm_pair(const void* a, const void* a_s, int as_dtype, const 
 // peer's epilogue every K block; measured at 0.64 PFLOP/s on 4096^3 against
 // 1.25 for the single-SM kernel, so it is opt-in (BS_FP8_GEMM_PAIR=1).
 static bool fp8_pair_enabled() {
-  static int v = -1;
-  if (v < 0) {
+  static const bool v = [] {   // read once, thread-safe
     const char* e = getenv("BS_FP8_GEMM_PAIR");
-    v = (e && e[0] == '1') ? 1 : 0;
-  }
-  return v == 1;
+    return e && e[0] == '1';
+  }();
+  return v;
 }
 
 // Returns 0 on success, BS_ERR_UNSUPPORTED if a tensor map could not be

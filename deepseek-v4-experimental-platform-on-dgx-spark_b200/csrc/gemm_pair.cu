@@ -215,13 +215,12 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
 
 cudaError_t launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a, int m_tiles, int n_tiles,
                         cudaStream_t st) {
-  static bool attr_done = false;
-  if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(bsg_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         PairCfg::kSmemBytes);
-    if (e != cudaSuccess) return e;
-    attr_done = true;
-  }
+  static int slots[hostcache::kMaxDevices];
+  cudaError_t e = (cudaError_t)hostcache::get(slots, [] {
+    return (int)cudaFuncSetAttribute(bsg_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     PairCfg::kSmemBytes);
+  });
+  if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)((m_tiles + 1) / 2 * 2), (unsigned)n_tiles, 1);
   cfg.blockDim = dim3(PairCfg::kThreads, 1, 1);

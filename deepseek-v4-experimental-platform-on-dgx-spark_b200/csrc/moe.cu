@@ -598,14 +598,14 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  if (!fn) {
+  static const EncodeTiledFn fn = [] {   // initialised once, thread-safe
     void* ptr = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(ptr);
-  }
+      return reinterpret_cast<EncodeTiledFn>(ptr);
+    return EncodeTiledFn(nullptr);
+  }();
   return fn;
 }
 
@@ -636,25 +636,19 @@ bool make_act_map(CUtensorMap* m, const void* a, int64_t rows, int64_t K) {
 }
 
 int sm_count() {
-  static int n = 0;
-  if (!n) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  }
-  return n;
+  static int slots[hostcache::kMaxDevices];
+  return hostcache::device_attr(slots, cudaDevAttrMultiProcessorCount);
 }
 
 template <int MODE>
 cudaError_t launch_grouped(const CUtensorMap& mw, const CUtensorMap& ma, const GemmArgs& a, cudaStream_t st) {
   using C = Cfg<MODE>;
   auto kern = grouped_gemm_kernel<MODE>;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  static int slots[hostcache::kMaxDevices];
+  const cudaError_t e = (cudaError_t)hostcache::get(slots, [&] {
+    return (int)cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  });
+  if (e != cudaSuccess) return e;
   kern<<<sm_count(), C::kThreads, C::kSmemBytes, st>>>(mw, ma, a);
   return cudaGetLastError();
 }

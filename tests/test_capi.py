@@ -93,3 +93,40 @@ def test_cpu_tensors_rejected():
         pkg.act_quant(torch.zeros(4, 100, dtype=torch.bfloat16))
     with pytest.raises(NotImplementedError):
         pkg.fp4_act_quant(torch.zeros(4, 32, dtype=torch.bfloat16), 32, False)
+
+
+def test_multi_gpu_entry_points_validate_arguments(lib):
+    """Tensor-parallel, barrier and expert-parallel entry points reject bad
+    arguments before any CUDA call."""
+    pkg = import_pkg()
+    L = pkg._lib
+    vp = ctypes.c_void_p
+    nine = (vp * 9)(*([None] * 9))
+    two = (vp * 2)(None, None)
+    # fused all-gather GEMM: 1..8 output buffers, columns must fit the rows
+    assert lib.bs_fp8_gemm_allgather(None, None, L.DT_F32, None, None, L.DT_F32, 16, 256, 128, nine, 9, 512, 0,
+                                     None) == L.BS_ERR_UNSUPPORTED
+    assert lib.bs_fp8_gemm_allgather(None, None, L.DT_F32, None, None, L.DT_F32, 16, 256, 128, None, 2, 512, 0,
+                                     None) == L.BS_ERR_INVALID_ARG
+    assert lib.bs_fp8_gemm_allgather(None, None, L.DT_F32, None, None, L.DT_F32, 16, 256, 128, two, 2, 512, 384,
+                                     None) == L.BS_ERR_INVALID_ARG
+    assert b"do not fit" in lib.bs_last_error()
+    assert lib.bs_fp4_gemm_allgather(None, None, L.DT_F32, None, None, L.DT_E8M0, 0, 256, 128, two, 2, 512, 256,
+                                     None) == L.BS_OK
+    # barriers: rank range, positive epoch, a counter
+    assert lib.bs_peer_barrier(two, 0, 0, 1, None) == L.BS_ERR_INVALID_ARG
+    assert lib.bs_peer_barrier(two, 2, 2, 1, None) == L.BS_ERR_INVALID_ARG
+    assert lib.bs_peer_barrier(two, 2, 0, 0, None) == L.BS_ERR_INVALID_ARG
+    assert lib.bs_peer_barrier(two, 2, 0, 1, None) == L.BS_ERR_INVALID_ARG   # null flag arrays
+    assert lib.bs_peer_barrier_counted(two, 2, 0, None, None) == L.BS_ERR_INVALID_ARG
+    # expert parallel: experts split evenly, H a multiple of 128
+    assert lib.bs_ep_counts_push(None, 255, 0, 2, two, None) == L.BS_ERR_UNSUPPORTED
+    assert lib.bs_ep_plan(None, 2, 256, 2, None, None, None, None) == L.BS_ERR_UNSUPPORTED
+    assert lib.bs_ep_plan(None, 2, 256, 0, None, None, None, None) == L.BS_ERR_INVALID_ARG
+    assert lib.bs_ep_rows_push(None, None, None, None, 256, 100, 0, 2, 16, two, two, two, None) == \
+        L.BS_ERR_UNSUPPORTED
+    assert lib.bs_ep_rows_push(None, None, None, None, 256, 128, 0, 2, 16, two, two, two, None) == \
+        L.BS_ERR_INVALID_ARG
+    assert lib.bs_ep_pack_scales(None, None, None, 0, 128, 16, None, None) == L.BS_ERR_UNSUPPORTED
+    assert lib.bs_ep_experts_return(16, 0, 4096, 2048, None, None, None, None, None, None, None, None, None, two, 2,
+                                    None, None, None) == L.BS_OK

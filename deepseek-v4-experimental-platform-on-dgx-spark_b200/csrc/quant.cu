@@ -123,6 +123,117 @@ __global__ void __launch_bounds__(kThreads) act_quant_kernel(const T* __restrict
   }
 }
 
+// Correctly rounded a/b for a finite b > 0, given y = RN(1/b) (Markstein,
+// IBM J. Res. Dev. 34(1), 1990): q0 = RN(a*y) lies within about 2 ulp of
+// a/b; one remainder correction q1 = RN(q0 + RN(a - b*q0)*y) brings it within
+// 1 ulp, and with q1 within 1 ulp and y within 1/2 ulp of 1/b the remainder
+// a - b*q1 is exact and RN(q1 + (a - b*q1)*y) = RN(a/b).  This holds while
+// nothing underflows; quotients that small (|a/b| < 2^-100 here) become an
+// e4m3 zero whose sign copysign keeps.
+BS_DEVINL float div_markstein(float a, float b, float y) {
+  const float q0 = __fmul_rn(a, y);
+  const float q1 = __fmaf_rn(__fmaf_rn(-b, q0, a), y, q0);
+  const float q2 = __fmaf_rn(__fmaf_rn(-b, q1, a), y, q1);
+  return copysignf(q2, a);
+}
+
+BS_DEVINL uint32_t max_u16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// bf16 input, 1 x 128 blocks, e4m3 out (the shape every GEMM path feeds).
+// Half a warp owns one block (16 lanes x 8 elements); each thread first
+// issues the loads of U blocks (kept as packed bf16), then quantises them, so
+// that enough bytes are in flight per SM to run at HBM rate.  Same results as
+// act_quant_kernel, with fewer instructions per element:
+//   amax   an integer max over the bits with the sign cleared: for
+//          non-negative floats integer order is float order and every NaN
+//          sorts above inf, so NaN propagates as in torch.amax;
+//   x/s    for a power-of-two scale, x * (1/s), which is exact (1/s is a
+//          power of two in the normal range); otherwise div_markstein; a
+//          non-finite scale (a block holding inf or NaN) takes __fdiv_rn;
+//   clamp  left to cvt.rn.satfinite, which maps everything beyond +-448
+//          (inf included) to +-448 and NaN to NaN, as clamp-then-convert does.
+template <int SDT, int U, bool POW2>
+__global__ void __launch_bounds__(kThreads) act_quant_bf16_128_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                      uint8_t* __restrict__ y, void* __restrict__ s,
+                                                                      int64_t n_groups) {
+  const int lane16 = threadIdx.x & 15;
+  const int half = (threadIdx.x >> 4) & 1;
+  const int64_t warp_global = ((int64_t)blockIdx.x * kThreads + threadIdx.x) >> 5;
+  const int64_t n_warps = ((int64_t)gridDim.x * kThreads) >> 5;
+  for (int64_t base = warp_global * 2 * U; base < n_groups; base += n_warps * 2 * U) {
+    uint4 raw[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t g = base + 2 * u + half;
+      raw[u] = g < n_groups ? __ldg(reinterpret_cast<const uint4*>(x + g * 128) + lane16) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t g = base + 2 * u + half;
+      const uint32_t w[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
+      const uint32_t m2 = max_u16x2(max_u16x2(w[0] & 0x7FFF7FFFu, w[1] & 0x7FFF7FFFu),
+                                    max_u16x2(w[2] & 0x7FFF7FFFu, w[3] & 0x7FFF7FFFu));
+      uint32_t mb = max(m2 << 16, m2 & 0xFFFF0000u);
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+      float amax = __uint_as_float(mb);
+      amax = amax < 1e-4f ? 1e-4f : amax;  // torch.clamp(min=1e-4); NaN passes through
+      float scale = __fdiv_rn(amax, 448.0f);
+      if (POW2) scale = bs_round_pow2(scale);
+      if (g >= n_groups) continue;
+      float f[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        f[2 * i] = __uint_as_float(w[i] << 16);
+        f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+      }
+      float q[8];
+      if ((__float_as_uint(scale) & 0x7F800000u) != 0x7F800000u) {
+        if (POW2) {
+          const float r = bs_inv_pow2(scale);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) q[i] = __fmul_rn(f[i], r);
+        } else {
+          const float r = __frcp_rn(scale);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) q[i] = div_markstein(f[i], scale, r);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) q[i] = __fdiv_rn(f[i], scale);
+      }
+      uint2 c;
+      c.x = bs_cvt_e4m3x2(q[0], q[1]) | ((uint32_t)bs_cvt_e4m3x2(q[2], q[3]) << 16);
+      c.y = bs_cvt_e4m3x2(q[4], q[5]) | ((uint32_t)bs_cvt_e4m3x2(q[6], q[7]) << 16);
+      *reinterpret_cast<uint2*>(y + g * 128 + lane16 * 8) = c;
+      if (lane16 == 0) {
+        if (SDT == BS_DT_F32) reinterpret_cast<float*>(s)[g] = scale;
+        else if (SDT == BS_DT_BF16) reinterpret_cast<__nv_bfloat16*>(s)[g] = __float2bfloat16_rn(scale);
+        else if (SDT == BS_DT_F16) reinterpret_cast<__half*>(s)[g] = __float2half_rn(scale);
+        else reinterpret_cast<uint8_t*>(s)[g] = bs_f32_to_e8m0(scale);
+      }
+    }
+  }
+}
+
+int grid_for(int64_t n_groups, int tpb);
+
+template <int U, bool POW2>
+void launch_aq128(const void* x, void* y, void* s, int s_dtype, int64_t n_groups, cudaStream_t st) {
+  // two blocks per warp and U per thread in each pass
+  const int grid = grid_for((n_groups + U - 1) / U, 16);
+  const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
+  uint8_t* yb = static_cast<uint8_t*>(y);
+  if (s_dtype == BS_DT_F32) act_quant_bf16_128_kernel<BS_DT_F32, U, POW2><<<grid, kThreads, 0, st>>>(xb, yb, s, n_groups);
+  else if (s_dtype == BS_DT_BF16) act_quant_bf16_128_kernel<BS_DT_BF16, U, POW2><<<grid, kThreads, 0, st>>>(xb, yb, s, n_groups);
+  else if (s_dtype == BS_DT_F16) act_quant_bf16_128_kernel<BS_DT_F16, U, POW2><<<grid, kThreads, 0, st>>>(xb, yb, s, n_groups);
+  else act_quant_bf16_128_kernel<BS_DT_E8M0, U, POW2><<<grid, kThreads, 0, st>>>(xb, yb, s, n_groups);
+}
+
 // e2m1 magnitudes {0,.5,1,1.5,2,3,4,6}: index = number of midpoints
 // {.25,.75,1.25,1.75,2.5,3.5,5} strictly below |v| (a tie keeps the smaller
 // magnitude, as argmin's first index does).  Differences to the two
@@ -194,9 +305,8 @@ __global__ void __launch_bounds__(kThreads) fp4_act_quant_kernel(T* __restrict__
 }
 
 int grid_for(int64_t n_groups, int tpb) {
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  static int slots[hostcache::kMaxDevices];
+  const int sms = hostcache::device_attr(slots, cudaDevAttrMultiProcessorCount);
   const int64_t threads = n_groups * tpb;
   int64_t blocks = (threads + kThreads - 1) / kThreads;
   const int64_t cap = (int64_t)sms * 8;
@@ -225,6 +335,14 @@ cudaError_t bs_launch_act_quant(const void* x, int x_dtype, int64_t rows, int64_
   const int nv = lanes / tpb;
   const int64_t n_groups = rows * (K / bs);
   if (n_groups == 0) return cudaSuccess;
+  if (x_dtype == BS_DT_BF16 && bs == 128 && !inplace) {
+    // U = 4 once there is enough work for every warp slot of the GPU
+    static int slots[hostcache::kMaxDevices];
+    const bool big = n_groups >= (int64_t)hostcache::device_attr(slots, cudaDevAttrMultiProcessorCount) * 256;
+    if (big) pow2 ? launch_aq128<4, true>(x, y, s, s_dtype, n_groups, st) : launch_aq128<4, false>(x, y, s, s_dtype, n_groups, st);
+    else pow2 ? launch_aq128<1, true>(x, y, s, s_dtype, n_groups, st) : launch_aq128<1, false>(x, y, s, s_dtype, n_groups, st);
+    return cudaGetLastError();
+  }
   const int grid = grid_for(n_groups, tpb);
   const int tl = ilog2(tpb);
 #define BS_AQ(T)                                                                                                  \

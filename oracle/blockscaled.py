@@ -147,12 +147,14 @@ def ceil_log2_f32(x: np.ndarray) -> np.ndarray:
 
 
 def round_scale_pow2(scale: np.ndarray) -> np.ndarray:
-    """``exp2(ceil(log2(scale)))`` in fp32 (kernel_sm121.py:51-52)."""
+    """``exp2(ceil(log2(scale)))`` in fp32 (kernel_sm121.py:51-52); NaN stays
+    NaN and +inf stays +inf (exp2(ceil(log2(inf))) = inf), as in torch."""
     scale = np.asarray(scale, dtype=np.float32)
-    e = ceil_log2_f32(scale)
+    finite = np.isfinite(scale)
+    e = ceil_log2_f32(np.where(finite, scale, np.float32(1.0)))
     with np.errstate(over="ignore", invalid="ignore"):
         out = np.ldexp(np.float32(1.0), np.clip(e, -200, 200)).astype(np.float32)
-    return np.where(np.isnan(scale), np.float32(np.nan), out).astype(np.float32)
+    return np.where(finite, out, scale).astype(np.float32)
 
 
 def to_f32(x: np.ndarray, dtype: int) -> np.ndarray:

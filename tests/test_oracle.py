@@ -92,6 +92,11 @@ def test_known_answers():
                                   np.array([0.0, 1.0, 2.0, np.inf], np.float32))
     # a scale one ulp above a power of two does not round up (fp32 log2)
     assert ob.round_scale_pow2(np.float32(2.0 ** -10) * np.float32(1 + 2.0 ** -23)) == np.float32(2.0 ** -10)
+    # special scales follow torch.exp2(torch.ceil(torch.log2(s))): inf -> inf, NaN -> NaN
+    import torch
+    sp = np.array([np.inf, np.nan, 2.0 ** -130, 1e30, 3.0], np.float32)
+    np.testing.assert_array_equal(ob.round_scale_pow2(sp),
+                                  torch.exp2(torch.ceil(torch.log2(torch.from_numpy(sp)))).numpy())
     # e4m3 RNE ties go to even; 448 is the largest finite value
     np.testing.assert_array_equal(ob.f32_to_e4m3(np.array([1.0625, 1.1875, 448.0, -448.0], np.float32)),
                                   np.array([0x38, 0x3A, 0x7E, 0xFE], np.uint8))

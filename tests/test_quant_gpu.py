@@ -63,6 +63,71 @@ def test_act_quant_sweep_vs_oracle(pkg, block, xdt):
     np.testing.assert_array_equal(bits(t), np_bits(ob.fp4_act_quant_inplace(x, DT[xdt], 32)))
 
 
+@pytest.mark.parametrize("sdt", [ob.DT_F32, ob.DT_BF16, ob.DT_F16, ob.DT_E8M0])
+@pytest.mark.parametrize("pow2", [0, 1])
+def test_act_quant_bf16_128_ragged_all_scale_dtypes(pkg, sdt, pow2):
+    """bf16 input with 1x128 blocks through the C ABI: a block count that no
+    grid pass divides evenly (plus zero, NaN, inf and tiny blocks), every
+    scale dtype, both scale modes."""
+    L = pkg._lib
+    rng = np.random.default_rng(7 + sdt + 10 * pow2)
+    rows, K = 3001, 896  # 21007 blocks
+    f = (rng.standard_normal((rows, K)) * 2.0 ** rng.integers(-30, 30, size=(rows, 1))).astype(np.float32)
+    f[5, :128] = 0.0
+    f[6, 3] = np.nan
+    f[7, 200] = np.inf
+    f[8, 256:384] = 1e-7
+    x = ob.f32_to_bf16(f)
+    xt = cuda_x(x, "bf16")
+    y = torch.empty(rows, K, device="cuda", dtype=torch.uint8)
+    nb = K // 128
+    s = torch.empty(rows * nb * (4 if sdt == ob.DT_F32 else 2 if sdt in (ob.DT_BF16, ob.DT_F16) else 1),
+                    device="cuda", dtype=torch.uint8)
+    L.check(L.load().bs_act_quant(xt.data_ptr(), ob.DT_BF16, rows, K, 128, pow2, y.data_ptr(), s.data_ptr(), sdt,
+                                  torch.cuda.current_stream().cuda_stream))
+    ry, rs = ob.act_quant(x, ob.DT_BF16, 128, "ue8m0" if pow2 else None, sdt)
+    # NaN encodings are the platform's: inf/inf (the inf element over its own
+    # inf scale) is +NaN on the GPU (e4m3 0x7F, as the reference's GPU kernel
+    # gives) but -NaN from numpy on x86 (0xFF); the NaN block's scale is the
+    # canonical NaN on the GPU but keeps the input payload in numpy.  NaNs are
+    # therefore compared as NaN, everything else bit for bit.
+    def nan_canon(c):
+        c = np.array(c, copy=True)
+        c[(c & 0x7F) == 0x7F] = 0x7F
+        return c
+    np.testing.assert_array_equal(nan_canon(bits(y)), nan_canon(ry))
+    assert np.count_nonzero(bits(y) != ry) <= 1
+    raw = s.cpu().numpy().view(np.asarray(rs).dtype).reshape(rs.shape)
+    got, want = ob.to_f32(raw, sdt), ob.to_f32(rs, sdt)
+    np.testing.assert_array_equal(np.isnan(got), np.isnan(want))
+    fin = ~np.isnan(want)
+    np.testing.assert_array_equal(raw[fin], np.asarray(rs)[fin])
+
+
+@pytest.mark.parametrize("fmt", [None, "ue8m0"])
+def test_act_quant_bf16_every_value_under_many_scales(pkg, fmt):
+    """Every finite bf16 magnitude (both signs) quantised under 24 block
+    maxima, so x/s meets every e4m3 rounding boundary a bf16 input can reach
+    with many non-power-of-two scales.  Each row is [amax, 127 values <= amax]."""
+    rng = np.random.default_rng(11)
+    codes = np.arange(0, 0x7F80, dtype=np.uint16)  # +0 .. largest finite
+    mags = ob.bf16_to_f32(codes)
+    amaxes = np.concatenate([[1.0, 3.0, 448.0, 1e-3, 7.5e-5, 1e30],
+                             2.0 ** rng.uniform(-20, 40, 18)]).astype(np.float32)
+    rows = []
+    for A in ob.bf16_to_f32(ob.f32_to_bf16(amaxes)):
+        v = codes[mags <= A]
+        v = np.where(rng.random(v.shape) < 0.5, v | 0x8000, v).astype(np.uint16)
+        n = (len(v) + 126) // 127 * 127
+        v = np.concatenate([v, np.zeros(n - len(v), np.uint16)]).reshape(-1, 127)
+        rows.append(np.concatenate([np.full((v.shape[0], 1), ob.f32_to_bf16(np.float32(A)), np.uint16), v], axis=1))
+    x = np.concatenate(rows)
+    y, s = pkg.act_quant(cuda_x(x, "bf16"), 128, fmt, torch.float32)
+    ry, rs = ob.act_quant(x, ob.DT_BF16, 128, fmt, ob.DT_F32)
+    np.testing.assert_array_equal(bits(y), ry)
+    np.testing.assert_array_equal(bits(s), np_bits(rs))
+
+
 def test_act_quant_e4m3_rounding_exhaustive(pkg):
     """Every e4m3 midpoint and its neighbours (ties to even, subnormals)."""
     codes = np.arange(0, 0x7E, dtype=np.uint8)

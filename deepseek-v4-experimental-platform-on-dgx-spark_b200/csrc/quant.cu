@@ -304,6 +304,92 @@ __global__ void __launch_bounds__(kThreads) fp4_act_quant_kernel(T* __restrict__
   }
 }
 
+// fp4_act_quant's per-element rule for a block whose scale is finite (a
+// power of two in [2^-126, 2^126], so c = x * (1/s) equals x/s exactly):
+// clamp |c| to 6, then the nearest e2m1 magnitude with ties to the smaller,
+// which on each binade of the e2m1 grid (spacing d = 0.5 below 2, 1 below 4,
+// 2 up to 6) is d * ceil(|c|/d - 0.5); the same values as e2m1_nearest.
+// The sign is torch.sign's (+0 for a zero c), the product with s is exact.
+BS_DEVINL float fp4_fake_quant(float x, float inv, float scale) {
+  const float c = __fmul_rn(x, inv);
+  const float a = fminf(fabsf(c), 6.0f);
+  const bool lo = a < 2.0f, mid = a < 4.0f;
+  const float d = lo ? 0.5f : (mid ? 1.0f : 2.0f);
+  const float id = lo ? 2.0f : (mid ? 1.0f : 0.5f);
+  const float m = __fmul_rn(d, ceilf(__fmaf_rn(a, id, -0.5f)));
+  const float q = c == 0.0f ? 0.0f : copysignf(m, c);
+  return __fmul_rn(q, scale);
+}
+
+// bf16, in place, blocks of 8*TPB elements (TPB lanes of 16 bytes each); U
+// blocks per lane group and pass, their loads issued first.  A block with a
+// non-finite scale (it holds inf or NaN) takes fp4_act_quant_kernel's
+// arithmetic.
+template <int TPB, int U>
+__global__ void __launch_bounds__(kThreads) fp4_act_quant_bf16_kernel(__nv_bfloat16* __restrict__ x,
+                                                                      int64_t n_groups) {
+  constexpr int kGpw = 32 / TPB;
+  const int lane_g = threadIdx.x & (TPB - 1);
+  const int sub = (threadIdx.x & 31) / TPB;
+  const int64_t warp_global = ((int64_t)blockIdx.x * kThreads + threadIdx.x) >> 5;
+  const int64_t n_warps = ((int64_t)gridDim.x * kThreads) >> 5;
+  for (int64_t base = warp_global * kGpw * U; base < n_groups; base += n_warps * kGpw * U) {
+    uint4 raw[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t g = base + u * kGpw + sub;
+      raw[u] = g < n_groups ? *(reinterpret_cast<const uint4*>(x + g * (8 * TPB)) + lane_g) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t g = base + u * kGpw + sub;
+      const uint32_t w[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
+      const uint32_t m2 = max_u16x2(max_u16x2(w[0] & 0x7FFF7FFFu, w[1] & 0x7FFF7FFFu),
+                                    max_u16x2(w[2] & 0x7FFF7FFFu, w[3] & 0x7FFF7FFFu));
+      uint32_t mb = max(m2 << 16, m2 & 0xFFFF0000u);
+#pragma unroll
+      for (int o = TPB / 2; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+      float amax = __uint_as_float(mb);
+      const float floor_v = 6.0f * 1.1754943508222875e-38f;  // 6 * 2^-126
+      amax = amax < floor_v ? floor_v : amax;
+      const float scale = bs_round_pow2(__fdiv_rn(amax, 6.0f));
+      if (g >= n_groups) continue;
+      float r[8];
+      if ((__float_as_uint(scale) & 0x7F800000u) != 0x7F800000u) {
+        const float inv = bs_inv_pow2(scale);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          r[2 * i] = fp4_fake_quant(__uint_as_float(w[i] << 16), inv, scale);
+          r[2 * i + 1] = fp4_fake_quant(__uint_as_float(w[i] & 0xFFFF0000u), inv, scale);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float f2[2] = {__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xFFFF0000u)};
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const float c = bs_clamp(__fdiv_rn(f2[j], scale), -6.0f, 6.0f);
+            const float sgn = c > 0.0f ? 1.0f : (c < 0.0f ? -1.0f : 0.0f);
+            r[2 * i + j] = sgn * e2m1_nearest(fabsf(c)) * scale;
+          }
+        }
+      }
+      *(reinterpret_cast<uint4*>(x + g * (8 * TPB)) + lane_g) = pack<__nv_bfloat16>(r);
+    }
+  }
+}
+
+template <int TPB>
+void launch_fp4_bf16(__nv_bfloat16* x, int64_t n_groups, cudaStream_t st) {
+  static int slots[hostcache::kMaxDevices];
+  const int sms = hostcache::device_attr(slots, cudaDevAttrMultiProcessorCount);
+  // U = 4 once there is enough work for every warp slot of the GPU
+  if (n_groups * TPB >= (int64_t)sms * 2048)
+    fp4_act_quant_bf16_kernel<TPB, 4><<<grid_for((n_groups + 3) / 4, TPB), kThreads, 0, st>>>(x, n_groups);
+  else
+    fp4_act_quant_bf16_kernel<TPB, 1><<<grid_for(n_groups, TPB), kThreads, 0, st>>>(x, n_groups);
+}
+
 int grid_for(int64_t n_groups, int tpb) {
   static int slots[hostcache::kMaxDevices];
   const int sms = hostcache::device_attr(slots, cudaDevAttrMultiProcessorCount);
@@ -366,6 +452,14 @@ cudaError_t bs_launch_fp4_act_quant(void* x, int x_dtype, int64_t rows, int64_t 
   const int nv = lanes / tpb;
   const int64_t n_groups = rows * (K / bs);
   if (n_groups == 0) return cudaSuccess;
+  if (x_dtype == BS_DT_BF16 && bs >= 16 && bs <= 128) {
+    __nv_bfloat16* xb = static_cast<__nv_bfloat16*>(x);
+    if (bs == 16) launch_fp4_bf16<2>(xb, n_groups, st);
+    else if (bs == 32) launch_fp4_bf16<4>(xb, n_groups, st);
+    else if (bs == 64) launch_fp4_bf16<8>(xb, n_groups, st);
+    else launch_fp4_bf16<16>(xb, n_groups, st);
+    return cudaGetLastError();
+  }
   const int grid = grid_for(n_groups, tpb);
   const int tl = ilog2(tpb);
   if (x_dtype == BS_DT_BF16)

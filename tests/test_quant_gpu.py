@@ -128,6 +128,43 @@ def test_act_quant_bf16_every_value_under_many_scales(pkg, fmt):
     np.testing.assert_array_equal(bits(s), np_bits(rs))
 
 
+@pytest.mark.parametrize("block", [16, 32, 64, 128])
+def test_fp4_act_quant_bf16_every_value(pkg, block):
+    """In-place e2m1 fake quantisation of every finite bf16 value (both
+    signs) under 24 block maxima, each row [amax, block-1 values <= amax],
+    plus blocks holding NaN, inf, zeros and subnormals; the row count leaves
+    a ragged last pass."""
+    rng = np.random.default_rng(13 + block)
+    codes = np.arange(0, 0x7F80, dtype=np.uint16)
+    mags = ob.bf16_to_f32(codes)
+    amaxes = np.concatenate([[6.0, 1.0, 3e38, 1e-38, 7.0, 0.3],
+                             2.0 ** rng.uniform(-120, 120, 18)]).astype(np.float32)
+    rows = []
+    for A in ob.bf16_to_f32(ob.f32_to_bf16(amaxes)):
+        v = codes[mags <= A]
+        v = np.where(rng.random(v.shape) < 0.5, v | 0x8000, v).astype(np.uint16)
+        n = (len(v) + block - 2) // (block - 1) * (block - 1)
+        v = np.concatenate([v, np.zeros(n - len(v), np.uint16)]).reshape(-1, block - 1)
+        rows.append(np.concatenate([np.full((v.shape[0], 1), ob.f32_to_bf16(np.float32(A)), np.uint16), v], axis=1))
+    x = np.concatenate(rows).reshape(-1)
+    special = np.zeros((4, block), np.uint16)
+    special[0, 3] = 0x7FC0      # NaN
+    special[1, 5] = 0x7F80      # inf
+    special[1, 6] = 0x3F80
+    special[2, :] = 0x8000      # -0
+    special[3, :] = rng.integers(1, 0x80, block) | (rng.integers(0, 2, block) << 15)  # subnormals
+    x = np.concatenate([x, special.reshape(-1)])
+    K = 4 * block
+    x = np.concatenate([x, np.zeros((-len(x)) % K, np.uint16)]).reshape(-1, K)
+    t = cuda_x(x, "bf16")
+    pkg.fp4_act_quant(t, block, True)
+    want = ob.fp4_act_quant_inplace(x, ob.DT_BF16, block)
+    got = bits(t)
+    nan_g, nan_w = (got & 0x7FFF) > 0x7F80, (want & 0x7FFF) > 0x7F80
+    np.testing.assert_array_equal(nan_g, nan_w)  # NaN encodings are the platform's
+    np.testing.assert_array_equal(got[~nan_w], want[~nan_w])
+
+
 def test_act_quant_e4m3_rounding_exhaustive(pkg):
     """Every e4m3 midpoint and its neighbours (ties to even, subnormals)."""
     codes = np.arange(0, 0x7E, dtype=np.uint8)

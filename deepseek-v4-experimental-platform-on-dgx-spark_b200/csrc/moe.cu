@@ -43,14 +43,16 @@ constexpr int kTok = 112;
 // ---------------------------------------------------------------------------
 
 // One warp per token.  Ties keep the lower expert index (a stable sort of
-// -logits).  Weights: softmax over the k selected logits.
+// -logits).  Weights: softmax over the k selected logits.  kMaxPer logits per
+// lane (E <= 32 * kMaxPer), chosen per launch so that no round scans empty
+// slots.
+template <int kMaxPer>
 __global__ void route_kernel(const float* __restrict__ logits, int T, int E, int topk, int* __restrict__ idx,
                              float* __restrict__ w, int* __restrict__ counts) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= T) return;
   const float* row = logits + (int64_t)warp * E;
-  constexpr int kMaxPer = 32;  // E <= 1024
   float v[kMaxPer];
   const int per = (E + 31) / 32;
 #pragma unroll
@@ -666,7 +668,13 @@ cudaError_t bs_launch_moe_route(const float* logits, int T, int E, int topk, int
   if (T == 0) return cudaSuccess;
   const int threads = 256;
   const int blocks = (int)(((int64_t)T * 32 + threads - 1) / threads);
-  moe::route_kernel<<<blocks, threads, 0, st>>>(logits, T, E, topk, idx, w, counts);
+  const int per = (E + 31) / 32;  // E <= 1024
+  if (per <= 1) moe::route_kernel<1><<<blocks, threads, 0, st>>>(logits, T, E, topk, idx, w, counts);
+  else if (per <= 2) moe::route_kernel<2><<<blocks, threads, 0, st>>>(logits, T, E, topk, idx, w, counts);
+  else if (per <= 4) moe::route_kernel<4><<<blocks, threads, 0, st>>>(logits, T, E, topk, idx, w, counts);
+  else if (per <= 8) moe::route_kernel<8><<<blocks, threads, 0, st>>>(logits, T, E, topk, idx, w, counts);
+  else if (per <= 16) moe::route_kernel<16><<<blocks, threads, 0, st>>>(logits, T, E, topk, idx, w, counts);
+  else moe::route_kernel<32><<<blocks, threads, 0, st>>>(logits, T, E, topk, idx, w, counts);
   return cudaGetLastError();
 }
 

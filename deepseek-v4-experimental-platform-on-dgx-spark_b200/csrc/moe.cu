@@ -337,19 +337,21 @@ struct Cfg {
   static constexpr int kSfCol0 = kAccBufs * kAccCols;
   static_assert(kSfCol0 + 2 * kSfSlot <= 512, "TMEM budget");
   static constexpr int kTmemCols = 512;
-  static constexpr int kThreads = 192;
+  static constexpr int kEpiWarps = 8;                   // two sets of four (one per TMEM lane quadrant)
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;
   static constexpr int kMaxE = 1024;
   static constexpr int kSmemBytes = 1024 + kStages * (kStageBytes + kSfBytes) + 2 * (kMaxE + 1) * 4 + 2 * 80 * 4 + 256;
   static_assert(kStageBytes % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
 };
 
-BS_DEVINL void named_bar_epi() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// the four warps of one epilogue set (barrier 1 + set)
+BS_DEVINL void named_bar_epi(int set) { asm volatile("bar.sync %0, 128;" ::"r"(1 + set) : "memory"); }
 
 BS_DEVINL float silu(float g) { return g / (1.0f + expf(-g)); }
 BS_DEVINL float bf16_round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
 template <int MODE>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(64 + 32 * 8, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a, GemmArgs p) {
   using C = Cfg<MODE>;
   extern __shared__ uint8_t smem_raw[];
@@ -360,7 +362,7 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* sf_base = smem + C::kStages * C::kStageBytes;
   int* s_off = reinterpret_cast<int*>(sf_base + C::kStages * C::kSfBytes);
   int* s_chunk = s_off + C::kMaxE + 1;
-  // per 16-token epilogue chunk, double-buffered by chunk parity:
+  // per 16-token epilogue chunk, one buffer per epilogue set:
   // [4 warps][16] amax bits, then [16] scales
   uint32_t* s_red = reinterpret_cast<uint32_t*>(s_chunk + C::kMaxE + 1);
   uint64_t* full = reinterpret_cast<uint64_t*>(s_red + 2 * 80);
@@ -383,7 +385,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);
+      mbar_init(&acc_empty[b], C::kEpiWarps);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -505,7 +507,11 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    // Two sets of four warps (warps 2-5 and 6-9), each covering the four TMEM
+    // lane quadrants, take alternate 16-token groups of an item: SiLU's exp and
+    // divide leave one warp per sub-partition latency-bound.
     const int quad = warp & 3;
+    const int set = (warp - 2) >> 2;
     const int f = quad * 32 + lane;      // output feature within the 128-row tile
     int acc_it = 0;
     for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++acc_it) {
@@ -516,14 +522,14 @@ __global__ void __launch_bounds__(192, 1)
       if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[buf], aph, abort_flag))) break;
       tc_fence_after();
       const uint32_t tl = tmem_base + ((uint32_t)(quad * 32) << 16) + buf * C::kAccCols;
-      for (int c0 = 0; c0 < cnt; c0 += 16) {
+      for (int c0 = set * 16; c0 < cnt; c0 += 32) {
         uint32_t g[16];
         BS_TMEM_LD16(tl + c0, g);
         if constexpr (MODE == kModeW13) {
           uint32_t u[16];
           BS_TMEM_LD16(tl + kTok + c0, u);
           tmem_ld_wait();
-          uint32_t* red = s_red + ((c0 >> 4) & 1) * 80;
+          uint32_t* red = s_red + set * 80;
           float z[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
@@ -533,7 +539,7 @@ __global__ void __launch_bounds__(192, 1)
             const uint32_t m = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(z[j])));
             if (lane == 0) red[quad * 16 + j] = m;
           }
-          named_bar_epi();
+          named_bar_epi(set);
           if (quad == 0 && lane < 16) {
             const uint32_t m = max(max(red[lane], red[16 + lane]), max(red[32 + lane], red[48 + lane]));
             float amax = __uint_as_float(m);
@@ -545,7 +551,7 @@ __global__ void __launch_bounds__(192, 1)
               *reinterpret_cast<uint32_t*>(p.hs_p + ((int64_t)cg * (p.I / 128) + nt) * 512 + sf_word_off(r)) =
                   0x01010101u * bs_f32_to_e8m0(scale);
           }
-          named_bar_epi();
+          named_bar_epi(set);
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int tok = c0 + j;

@@ -68,7 +68,7 @@ BS_DEVINL float load_scale(const void* p, int dtype, int64_t idx) {
 // CTAs outnumber half the SMs -- at one CTA per SM the next call's CTAs could
 // not become resident early to stream their weights (programmatic dependent
 // launch) while this call runs.
-template <bool SWAP, bool FP4, int BN, bool TWO = false>
+template <bool SWAP, bool FP4, int BN, bool TWO = false, bool MX = false>
 struct Cfg {
   static constexpr int kBM = 128;                       // MMA M (rows of X)
   // Each pipeline stage carries two 128-wide K blocks, fetched by one 3-D TMA
@@ -93,9 +93,13 @@ struct Cfg {
   static constexpr int kSfYBlocks = (BN + 127) / 128;
   static constexpr int kWChunks = SWAP ? 1 : kSfYBlocks;          // weights' chunks per K block
   static constexpr int kAChunks = SWAP ? kSfYBlocks : 1;          // constant activation chunks
-  static constexpr int kSfSub = FP4 ? 512 * kWChunks : 0;         // per K block
+  // MX (normal-mode fp8 with ue8m0 scales on both operands): the
+  // activations' scale chunk of each K block follows the weights' chunks and
+  // the MMA applies both, so the whole K range accumulates in one TMEM buffer
+  // with no per-K-block promotion.
+  static constexpr int kSfSub = (FP4 || MX) ? 512 * (kWChunks + (MX ? 1 : 0)) : 0;   // per K block
   static constexpr int kSfBytes = kSfSub * kKps;                  // per stage
-  static constexpr int kSfConst = FP4 ? 512 * kAChunks : 0;
+  static constexpr int kSfConst = (FP4 && !MX) ? 512 * kAChunks : 0;
   // normal mode: one epilogue warp per (TMEM lane quadrant, 64-column group),
   // so BN=256 has 16 epilogue warps, 4 per SM sub-partition, to keep the
   // per-K-block promotion (TMEM load + FMA of the partial) ahead of the MMA
@@ -104,15 +108,17 @@ struct Cfg {
   static constexpr int kEpiWarps = SWAP ? 4 * (BN > 32 ? BN / 32 : 1) : 4 * (BN / 64);
   static constexpr int kCols = SWAP ? (BN > 32 ? 32 : BN) : 64;   // columns per epilogue warp
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
-  static constexpr int kSfWCols = FP4 ? 4 * kWChunks : 0;   // TMEM columns per weights' SF slot (2 slots)
-  static constexpr int kSfACols = FP4 ? 4 * kAChunks : 0;   // TMEM columns of the constant activation SF
+  static constexpr int kSfWCols = (FP4 || MX) ? 4 * kWChunks : 0;   // TMEM columns per weights' SF slot (2 slots)
+  // TMEM columns of the activation SF: constant (fp4), or two slots of one chunk (MX)
+  static constexpr int kSfACols = MX ? 8 : (FP4 ? 4 * kAChunks : 0);
   // TMEM partial buffers: normal mode double-buffers its wide tile; the
   // narrow decode tile keeps 4-8 so the MMA runs through a whole split-K
   // range without waiting for the per-K-block promotion.
   // (TWO: the two CTAs of an SM share its 512 TMEM columns, so each keeps to
   // 256 -- a CTA whose allocation waited on its SM neighbour while both sit
   // in one cluster would wait forever at the cluster barrier)
-  static constexpr int kPBufs = SWAP ? (TWO ? (BN == 16 ? 8 : BN == 32 ? 7 : 3) : (BN <= 32 ? 8 : 4)) : 2;
+  static constexpr int kPBufs = MX ? 1 : SWAP ? (TWO ? (BN == 16 ? 8 : BN == 32 ? 7 : 3) : (BN <= 32 ? 8 : 4)) : 2;
+  static_assert(!MX || (!SWAP && !TWO), "MX is a normal-mode form");
   static constexpr int kTmemNeed = kPBufs * BN + 2 * kSfWCols + kSfACols;
   static constexpr int kTmemCols = kTmemNeed <= 32 ? 32 : kTmemNeed <= 64 ? 64 : kTmemNeed <= 128 ? 128
                                    : kTmemNeed <= 256 ? 256 : 512;
@@ -132,10 +138,10 @@ struct Cfg {
   }
 };
 
-template <bool SWAP, bool FP4, int BN, bool TWO>
-__global__ void __launch_bounds__(Cfg<SWAP, FP4, BN, TWO>::kThreads, Cfg<SWAP, FP4, BN, TWO>::kMinBlocks)
+template <bool SWAP, bool FP4, int BN, bool TWO, bool MX>
+__global__ void __launch_bounds__(Cfg<SWAP, FP4, BN, TWO, MX>::kThreads, Cfg<SWAP, FP4, BN, TWO, MX>::kMinBlocks)
     bsg_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_y, GemmArgs p) {
-  using C = Cfg<SWAP, FP4, BN, TWO>;
+  using C = Cfg<SWAP, FP4, BN, TWO, MX>;
   extern __shared__ uint8_t smem_raw[];
   // 1 KB alignment by offsetting smem_raw itself, so that every buffer
   // carved from it stays in the shared address space for the compiler
@@ -171,7 +177,7 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN, TWO>::kThreads, Cfg<SWAP, F
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(&full[s], 1 + (FP4 ? 32 : 0));
+      mbar_init(&full[s], 1 + ((FP4 || MX) ? 32 : 0));
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < C::kPBufs; ++b) {
@@ -185,7 +191,7 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN, TWO>::kThreads, Cfg<SWAP, F
     if (gridDim.z > 1)
       mbar_arrive_expect_tx(recv_bar, (uint32_t)((gridDim.z - 1) * (C::kBM / gridDim.z) * BN * 4));
   }
-  if (FP4) {
+  if (FP4 && !MX) {
     // the constant activation block scales (ue8m0 1.0)
     for (int i = threadIdx.x; i < C::kSfConst / 4; i += blockDim.x)
       reinterpret_cast<uint32_t*>(sf_const)[i] = 0x7F7F7F7Fu;
@@ -224,7 +230,7 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN, TWO>::kThreads, Cfg<SWAP, F
     // fences before its arrive on full[s], so the MMA issuer needs no proxy
     // fence.  The prefetched stages share one wait.
     auto sf_publish = [&](int s0, int n) {
-      if (FP4) {
+      if (FP4 || MX) {
         cp_async_wait_all();
         fence_proxy_async_smem();
         for (int i = 0; i < n; ++i) mbar_arrive(&full[s0 + i]);
@@ -253,16 +259,47 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN, TWO>::kThreads, Cfg<SWAP, F
         mbar_arrive_expect_tx(&full[s], C::kXTx + C::kYTx);
         tma_load_3d(stage_base + s * C::kStageBytes + kWOff, tm_w, &full[s], 0, w_row, kb0);
       }
+      if (MX && !FP4) {
+        // the ue8m0 scale of each 128 x 128 weight block, repeated over its
+        // four 32-K sub-blocks (gathered while the tiles are in flight)
+        const uint8_t* bs = reinterpret_cast<const uint8_t*>(p.b_s);
+        for (int sub = 0; sub < C::kKps; ++sub) {
+          const int kb = kb0 + sub < kb_end ? kb0 + sub : kb_end - 1;
+          uint8_t* chunk = sf_base + (s * C::kKps + sub) * C::kSfSub;
+          for (int r = lane; r < BN; r += 32) {
+            const int n = n0 + r < p.N ? n0 + r : p.N - 1;
+            *reinterpret_cast<uint32_t*>(chunk + (r % 32) * 16 + ((r / 32) % 4) * 4 + (r / 128) * 512) =
+                0x01010101u * bs[(int64_t)(n / 128) * num_kb_total + kb];
+          }
+        }
+      }
     };
     auto issue_act = [&](int st, int s) {
       if (elect_one())
         tma_load_3d(stage_base + s * C::kStageBytes + kActOff, tm_act, &full[s], 0, act_row, kb_begin + st * C::kKps);
+      if (MX) {
+        // the activations' ue8m0 scale of each 1 x 128 block, repeated over
+        // its four 32-K sub-blocks (after the weights' chunks; gathered while
+        // the tile is in flight)
+        const uint8_t* as = reinterpret_cast<const uint8_t*>(p.a_s);
+        for (int sub = 0; sub < C::kKps; ++sub) {
+          const int kb = kb_begin + st * C::kKps + sub < kb_end ? kb_begin + st * C::kKps + sub : kb_end - 1;
+          uint8_t* chunk = sf_base + (s * C::kKps + sub) * C::kSfSub + C::kWChunks * 512;
+          for (int r = lane; r < C::kBM; r += 32) {
+            const int m = x0 + r < p.M ? x0 + r : p.M - 1;
+            *reinterpret_cast<uint32_t*>(chunk + (r % 32) * 16 + ((r / 32) % 4) * 4) =
+                0x01010101u * as[(int64_t)m * num_kb_total + kb];
+          }
+        }
+        __syncwarp();
+      }
     };
     for (int st = 0; st < n_pre; ++st) issue_weights(st, st);   // the ring starts empty
-    sf_publish(0, n_pre);
+    if (!MX) sf_publish(0, n_pre);
     if (lane == 0) pdl_wait();
     __syncwarp();
     for (int st = 0; st < n_pre; ++st) issue_act(st, st);
+    if (MX) sf_publish(0, n_pre);                              // after the activations' scales
     __syncwarp();
     for (int st = n_pre; st < n_st; ++st) {
       const int s = st % C::kStages;
@@ -289,18 +326,25 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN, TWO>::kThreads, Cfg<SWAP, F
       const uint32_t sx = smem_u32(stage_base + s * C::kStageBytes) + sub * C::kXSub;
       const uint32_t sy = smem_u32(stage_base + s * C::kStageBytes) + C::kXBytes + sub * C::kYSub;
       const uint32_t d = tmem_base + buf * BN;
-      if constexpr (FP4) {
+      if constexpr (FP4 || MX) {
         const uint32_t wslot = tmem_base + sfw_col0 + (it & 1) * C::kSfWCols;
         const uint32_t sfs = smem_u32(sf_base + (s * C::kKps + sub) * C::kSfSub);
         for (int b = 0; b < C::kWChunks; ++b) tc_cp_32x128b_warpx4(wslot + 4 * b, sdesc_sf_chunk(sfs + 512 * b));
+        uint32_t aslot = tmem_base + sfa_col;
+        if (MX) {
+          aslot += (it & 1) * 4;
+          tc_cp_32x128b_warpx4(aslot, sdesc_sf_chunk(sfs + 512 * C::kWChunks));
+        }
         // X is the weights in swap mode, the activations otherwise
-        const uint32_t sfa = SWAP ? wslot : tmem_base + sfa_col;
-        const uint32_t sfb = SWAP ? tmem_base + sfa_col : wslot;
+        const uint32_t sfa = SWAP ? wslot : aslot;
+        const uint32_t sfb = SWAP ? aslot : wslot;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const uint32_t idesc = idesc_mxf8f6f4(C::kXFp4 ? 5 : 0, C::kYFp4 ? 5 : 0, 128, BN, k, k);
+          // MX: one accumulator over the whole K range
+          const uint32_t acc = (k > 0 || (MX && it > 0)) ? 1u : 0u;
           tc_mma_mxf8f6f4(d, sdesc_k128_sw128(sx + k * 32), sdesc_k128_sw128(sy + k * 32), idesc,
-                          sfa | ((uint32_t)k << 30), sfb | ((uint32_t)k << 30), k > 0 ? 1u : 0u);
+                          sfa | ((uint32_t)k << 30), sfb | ((uint32_t)k << 30), acc);
         }
       } else {
         constexpr uint32_t idesc = idesc_f8f6f4(0, 0, 128, BN);
@@ -308,7 +352,7 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN, TWO>::kThreads, Cfg<SWAP, F
         for (int k = 0; k < 4; ++k)
           tc_mma_f8f6f4(d, sdesc_k128_sw128(sx + k * 32), sdesc_k128_sw128(sy + k * 32), idesc, k > 0 ? 1u : 0u);
       }
-      tc_commit(&pfull[buf]);
+      if (!MX || it == n_kb - 1) tc_commit(&pfull[buf]);
     };
     if constexpr (SWAP) {
       // decode: one full wait and one issue block per stage (both K blocks);
@@ -342,7 +386,7 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN, TWO>::kThreads, Cfg<SWAP, F
         const int buf = it % C::kPBufs;
         const uint32_t pph = (it / C::kPBufs) & 1;
         bool ok = sub != 0 || mbar_wait(&full[s], ph, abort_flag);
-        ok = ok && mbar_wait(&pempty[buf], pph ^ 1, abort_flag);
+        if (!MX) ok = ok && mbar_wait(&pempty[buf], pph ^ 1, abort_flag);
         if (!__all_sync(0xffffffffu, ok)) break;
         tc_fence_after();
         if (elect_one()) {
@@ -421,8 +465,24 @@ __global__ void __launch_bounds__(Cfg<SWAP, FP4, BN, TWO>::kThreads, Cfg<SWAP, F
       }
       asm volatile("bar.sync 1, %0;" ::"r"(32 * C::kEpiWarps) : "memory");
     }
-    float rs_next = n_kb > 0 ? row_scale(kb_begin) * blk_scale(kb_begin) : 0.0f;
-    for (int it = 0; it < n_kb; ++it) {
+    if constexpr (MX) {
+      // the MMAs applied every scale: read the finished accumulator once
+      if (n_kb > 0 && __all_sync(0xffffffffu, mbar_wait(&pfull[0], 0, abort_flag))) {
+        tc_fence_after();
+        const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + col0;
+#pragma unroll
+        for (int c = 0; c < C::kCols / 16; c += 2) {
+          uint32_t r[32];
+          BS_TMEM_LD16(taddr + c * 16, r);
+          BS_TMEM_LD16(taddr + (c + 1) * 16, (r + 16));
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[c * 16 + j] = __uint_as_float(r[j]);
+        }
+      }
+    }
+    float rs_next = (!MX && n_kb > 0) ? row_scale(kb_begin) * blk_scale(kb_begin) : 0.0f;
+    for (int it = 0; it < (MX ? 0 : n_kb); ++it) {
       const int buf = it % C::kPBufs;
       const uint32_t pph = (it / C::kPBufs) & 1;
       const float rs = rs_next;
@@ -607,11 +667,11 @@ int max_dyn_smem() {
   return hostcache::device_attr(slots, cudaDevAttrMaxSharedMemoryPerBlockOptin);
 }
 
-template <bool SWAP, bool FP4, int BN, bool TWO>
+template <bool SWAP, bool FP4, int BN, bool TWO, bool MX = false>
 cudaError_t prepare_kernel() {
   static int slots[hostcache::kMaxDevices];
   return (cudaError_t)hostcache::get(slots, [] {
-    auto kern = bsg_kernel<SWAP, FP4, BN, TWO>;
+    auto kern = bsg_kernel<SWAP, FP4, BN, TWO, MX>;
     // the opt-in limit covers static plus dynamic shared memory
     cudaFuncAttributes fa;
     cudaError_t e = cudaFuncGetAttributes(&fa, kern);
@@ -624,12 +684,12 @@ cudaError_t prepare_kernel() {
   });
 }
 
-template <bool SWAP, bool FP4, int BN, bool TWO = false>
+template <bool SWAP, bool FP4, int BN, bool TWO = false, bool MX = false>
 cudaError_t launch(const CUtensorMap& mx, const CUtensorMap& my, const GemmArgs& a, dim3 grid, int split,
                    cudaStream_t st) {
-  using C = Cfg<SWAP, FP4, BN, TWO>;
-  auto kern = bsg_kernel<SWAP, FP4, BN, TWO>;
-  cudaError_t e = prepare_kernel<SWAP, FP4, BN, TWO>();
+  using C = Cfg<SWAP, FP4, BN, TWO, MX>;
+  auto kern = bsg_kernel<SWAP, FP4, BN, TWO, MX>;
+  cudaError_t e = prepare_kernel<SWAP, FP4, BN, TWO, MX>();
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
@@ -655,7 +715,7 @@ cudaError_t launch(const CUtensorMap& mx, const CUtensorMap& my, const GemmArgs&
 template <bool FP4, int BN, bool TWO>
 int max_clusters_query(int split) {
   using C = Cfg<true, FP4, BN, TWO>;
-  auto kern = bsg_kernel<true, FP4, BN, TWO>;
+  auto kern = bsg_kernel<true, FP4, BN, TWO, false>;
   prepare_kernel<true, FP4, BN, TWO>();
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(1, 1, split);
@@ -817,8 +877,15 @@ int bs_launch_gemm(bool fp4, const void* a, const void* a_s, int as_dtype, const
     if (!make_map(&mx, a, false, K, M, 128) || !make_map(&my, b, fp4, K, N, bn)) return BS_ERR_UNSUPPORTED;
     args.kb_per_split = nkb;
     dim3 grid((unsigned)((M + 127) / 128), (unsigned)((N + bn - 1) / bn), 1);
+    // fp8 with ue8m0 scales on both operands: the block-scaled MMA applies
+    // them and the whole K range accumulates in TMEM (no per-K-block
+    // promotion; 1420 -> 1461 TFLOP/s at 4096^3).  The fp4 form with ue8m0
+    // activation scales measured slower (1065 -> 903): its narrower stage
+    // leaves the producer's scale gathers on the critical path.
+    const bool scaled_mma = !fp4 && as_dtype == BS_DT_E8M0 && bs_dtype == BS_DT_E8M0;
     if (fp4) *cerr = launch<false, true, 128>(mx, my, args, grid, 1, st);
-    else *cerr = launch<false, false, 256>(mx, my, args, grid, 1, st);
+    else *cerr = scaled_mma ? launch<false, false, 256, false, true>(mx, my, args, grid, 1, st)
+                            : launch<false, false, 256>(mx, my, args, grid, 1, st);
   }
   return *cerr == cudaSuccess ? 0 : BS_ERR_CUDA;
 }

@@ -102,6 +102,50 @@ def test_fp4_prefill_vs_oracle(pkg, shape, fmt):
     check(bits(run_fp4(pkg, c)), ref, f"fp4 M={M} N={N} K={K} fmt={fmt}")
 
 
+def _e8m0_weight_case(rng, N, K):
+    """Weights quantised per 128x128 block with power-of-two (ue8m0) scales."""
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    nb, kb = (N + 127) // 128, K // 128
+    pad = np.zeros((nb * 128, K), np.float32)
+    pad[:N] = w
+    blk = pad.reshape(nb, 128, kb, 128)
+    amax = np.maximum(np.abs(blk).max(axis=(1, 3)), np.float32(1e-4))
+    s = ob.round_scale_pow2((amax / np.float32(448)).astype(np.float32))
+    b = ob.f32_to_e4m3(np.clip(blk / s[:, None, :, None], -448, 448).astype(np.float32)).reshape(nb * 128, K)[:N]
+    return b, ob.from_f32(s, ob.DT_E8M0)
+
+
+@pytest.mark.parametrize("shape", [(256, 512, 1024), (130, 200, 384), (512, 768, 2048), (200, 300, 4096)])
+def test_fp8_prefill_ue8m0_scales_vs_oracle(pkg, shape):
+    """Both scale tensors ue8m0 (the DeepSeek checkpoints' format): the MMA
+    applies the scales and accumulates the whole K range in TMEM."""
+    M, N, K = shape
+    rng = np.random.default_rng(5 * M + N + K)
+    x = ob.f32_to_bf16(rng.standard_normal((M, K)).astype(np.float32))
+    a, a_s = ob.act_quant(x, ob.DT_BF16, 128, "ue8m0", ob.DT_E8M0)
+    b, b_s = _e8m0_weight_case(rng, N, K)
+    c = dict(a=a, a_s=a_s, b=b, b_s=b_s, as_dt="e8m0", bs_dt="e8m0")
+    out = run_fp8(pkg, c)
+    check(bits(out), ob.fp8_gemm(a, a_s, b, b_s, ob.DT_E8M0, ob.DT_E8M0), f"fp8 ue8m0 M={M} N={N} K={K}")
+    np.testing.assert_array_equal(bits(run_fp8(pkg, c)), bits(out))  # deterministic
+
+
+@pytest.mark.parametrize("shape", [(256, 512, 1024), (130, 200, 384), (300, 1024, 4096)])
+def test_fp4_prefill_ue8m0_act_scales_vs_oracle(pkg, shape):
+    """ue8m0 activation scales (act_quant with scale_fmt='ue8m0' and an e8m0
+    scale dtype) against the oracle, and against the same scales given as
+    fp32."""
+    M, N, K = shape
+    c = cases.cfg1_fp4(M=M, N=N, K=K, scale_fmt="ue8m0", seed=M + N + 1)
+    c = dict(c, a_s=ob.from_f32(c["a_s"], ob.DT_E8M0), as_dt="e8m0")
+    ref = ob.fp4_gemm(c["a"], c["a_s"], c["b"], c["b_s"], ob.DT_E8M0, ob.DT_E8M0)
+    out = run_fp4(pkg, c)
+    check(bits(out), ref, f"fp4 ue8m0 act M={M} N={N} K={K}")
+    # the same values as fp32 scales take the promotion path: the two agree closely
+    c32 = dict(c, a_s=ob.to_f32(c["a_s"], ob.DT_E8M0), as_dt="f32")
+    check(bits(out), bits(run_fp4(pkg, c32)), f"fp4 ue8m0 act vs fp32 scales M={M}")
+
+
 def test_gemm_leading_dims(pkg):
     c = cases.cfg1_fp4(M=12, N=256, K=512, seed=3)
     a = cuda_u8(c["a"], torch.float8_e4m3fn).view(3, 4, 512)

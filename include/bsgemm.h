@@ -91,7 +91,9 @@ int bs_fp4_act_quant_inplace(void* x, int x_dtype, int64_t rows, int64_t K, int 
  * A scales a_s [M, K/128] and per-(128x128) B scales b_s [ceil(N/128), K/128],
  * each BS_DT_F32 or BS_DT_E8M0 (e8m0 decoded as the reference does).
  * Replaces kernel_sm121.py:190-255 fp8_gemm(a, a_s, b, b_s, scale_dtype).
- * K must be a multiple of 128.
+ * K must be a multiple of 128.  With both scales BS_DT_E8M0 and M > 64 the
+ * MMA applies the scales (bytes 1..254 exact; byte 0 scales by 2^-127
+ * rather than 0, byte 255 gives NaN rather than inf).
  */
 int bs_fp8_gemm(const void* a, const void* a_s, int as_dtype, const void* b, const void* b_s, int bs_dtype,
                 int64_t M, int64_t N, int64_t K, void* c, void* stream);

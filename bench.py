@@ -2,7 +2,7 @@
 """Benchmark of the block-scaled GEMM path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload fp8_prefill|fp4_decode|fp4_cfg1|moe]
+                    [--workload fp8_prefill|fp4_decode|moe|moe_stack|act_quant|fp4_act_quant]
 
 Default workload (one "step"): the dense prefill fp8_gemm, M=N=K=4096, A
 quantised per 1x128 (fp32 scales), W e4m3 with fp32 128x128 block scales,
@@ -41,6 +41,9 @@ PKG = "deepseek-v4-experimental-platform-on-dgx-spark_b200"
 NCU_TRAFFIC = {
     "fp8_gemm_4096x4096x4096": 34_120_960 + 2_532_864,      # profiles/fp8_gemm_4096_prefill.md
     "fp4_decode_16x4096x4096": 9_046_784 + 0,               # profiles/fp4_gemm_decode_m16_n4096.md
+    # dram__bytes.sum.per_second x duration (profiles/quantisers_bf16_16384x7168.md)
+    "act_quant_16384x7168": 325_000_000,
+    "fp4_act_quant_16384x7168": 410_000_000,
 }
 
 PEAKS_FILE = os.path.join(ROOT, "MEASURED_PEAKS.json")
@@ -599,6 +602,120 @@ def bench_moe(args, torch, dist, ws, rank, dev):
             "gpu_launches": args.steps * launches, "clocks": clk}
 
 
+def bench_quant(args, torch, dist, ws, rank, dev):
+    """The quantisers that feed the GEMMs, on bf16 [rows, 7168] (rows = --tokens, default 16384):
+    act_quant (1x128 blocks, e4m3 + fp32 scales; 3 B per element + 4 B per block) or the
+    in-place fp4_act_quant (blocks of 32; 4 B per element).  One step = one call; the calls run
+    from one CUDA graph over three rotating inputs, each larger than L2.  N GPUs: independent
+    replicas (weak scaling), value = all ranks' bytes / the slowest rank's time."""
+    pkg = __import__("importlib").import_module(PKG)
+    lib = pkg._lib.load()
+    fp4 = args.workload == "fp4_act_quant"
+    R, K = args.tokens, 7168
+    n_sets = 3
+    g = torch.Generator(device=dev)
+    g.manual_seed(5 + rank)
+    xs = [torch.randn(R, K, generator=g, device=dev).to(torch.bfloat16) for _ in range(n_sets)]
+    y = torch.empty(R, K, dtype=torch.uint8, device=dev)
+    s_ = torch.empty(R, K // 128, dtype=torch.float32, device=dev)
+
+    def call(i, st):
+        x = xs[i % n_sets]
+        if fp4:
+            pkg._lib.check(lib.bs_fp4_act_quant_inplace(x.data_ptr(), pkg._lib.DT_BF16, R, K, 32, st))
+        else:
+            pkg._lib.check(lib.bs_act_quant(x.data_ptr(), pkg._lib.DT_BF16, R, K, 128, 0, y.data_ptr(),
+                                            s_.data_ptr(), pkg._lib.DT_F32, st))
+
+    cur = torch.cuda.current_stream().cuda_stream
+    for i in range(max(args.warmup, n_sets)):
+        call(i, cur)
+    torch.cuda.synchronize()
+    steps = max(args.steps, 2 * n_sets)
+    graph = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream()
+    cap.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(cap):
+        with torch.cuda.graph(graph, stream=cap):
+            for i in range(steps):
+                call(i, cap.cuda_stream)
+    torch.cuda.current_stream().wait_stream(cap)
+    graph.replay()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    reps = 3
+    clocks = Clocks(torch.cuda.current_device())
+    clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(reps):
+        graph.replay()
+    t1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = max_over_ranks(torch, dist, t0.elapsed_time(t1) / (reps * steps))
+    nbytes = R * K * 4 if fp4 else R * K * 3 + R * (K // 128) * 4
+    gbs = ws * nbytes / (ms * 1e-3) / 1e9
+    # end to end through the public API: bf16 rows in from pinned host memory, the result back
+    x_host = xs[0].cpu().pin_memory()
+    x_dev = torch.empty_like(xs[0])
+    y_host = torch.empty(R, K, dtype=torch.bfloat16 if fp4 else torch.uint8).pin_memory()
+    s_host = torch.empty(R, K // 128, dtype=torch.float32).pin_memory()
+
+    def e2e_call():
+        x_dev.copy_(x_host, non_blocking=True)
+        if fp4:
+            y_host.copy_(pkg.fp4_act_quant(x_dev, 32, True), non_blocking=True)
+        else:
+            yq, sq = pkg.act_quant(x_dev, 128)
+            y_host.copy_(yq.view(torch.uint8), non_blocking=True)
+            s_host.copy_(sq, non_blocking=True)
+
+    e2e_call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = 3
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_call()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(torch, dist, e0.elapsed_time(e1) / e2e_steps)
+    d2h = R * K * (2 if fp4 else 1) + (0 if fp4 else R * (K // 128) * 4)
+    peaks, src = load_peaks()
+    name = "fp4_act_quant bf16 block 32 (in place)" if fp4 else "act_quant bf16 1x128 -> e4m3 + fp32 scales"
+    key = f"{args.workload}_{R}x{K}"
+    line = {"metric": f"{args.workload} HBM GB/s", "value": round(gbs, 1), "unit": "GB/s", "n_gpus": ws,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16 -> e2m1 grid" if fp4 else "bf16 -> e4m3",
+            "data": "synthetic (seeded N(0,1))",
+            "config": {"workload": f"{name}, [{R}, {K}]", "l2": f"{n_sets} rotating inputs of {R * K * 2 >> 20} MiB",
+                       "parallelism": f"replicas x{ws}" if ws > 1 else "none"},
+            "roofline": {"bound": "hbm", "achieved": round(nbytes / (ms * 1e-3) / 1e9, 1), "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": round(nbytes / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 3),
+                         "traffic": NCU_TRAFFIC.get(key), "peak_source": src},
+            "e2e": {"value": round(ws * nbytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                    "h2d_bytes_per_step": R * K * 2, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
+                    "path": ("fp4_act_quant" if fp4 else "act_quant") +
+                            " public API with the rows copied in from and the result out to pinned host memory"},
+            "gpu_launches": steps * reps, "clocks": clk}
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        from oracle import blockscaled as ob
+        rows = 512
+        xh = xs[0][:rows].view(torch.int16).cpu().numpy().view(np.uint16)
+        t = time.perf_counter()
+        if fp4:
+            ob.fp4_act_quant_inplace(xh, ob.DT_BF16, 32)
+        else:
+            ob.act_quant(xh, ob.DT_BF16, 128, None, ob.DT_F32)
+        dt = time.perf_counter() - t
+        line["cpu_baseline"] = {"value": round(rows * nbytes / R / dt / 1e9, 3), "unit": "GB/s", "cores": 1,
+                                "kind": "port", "sample": f"{rows} of the {R} rows through the numpy port of the "
+                                                          f"reference's quantiser ({dt * 1e3:.0f} ms)"}
+    return line
+
+
 def max_over_ranks(torch, dist, v):
     if dist is None:
         return v
@@ -802,8 +919,10 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["fp8_prefill", "fp4_decode", "moe", "moe_stack"], default="fp8_prefill")
-    ap.add_argument("--tokens", type=int, default=None, help="moe: 1024, moe_stack: 8192")
+    ap.add_argument("--workload", choices=["fp8_prefill", "fp4_decode", "moe", "moe_stack", "act_quant",
+                                           "fp4_act_quant"], default="fp8_prefill")
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="moe: 1024, moe_stack: 8192, act_quant / fp4_act_quant: 16384 rows")
     ap.add_argument("--experts", type=int, default=256)
     ap.add_argument("--m", type=int, default=16)
     ap.add_argument("--n", type=int, default=4096)
@@ -815,7 +934,7 @@ def main():
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.tokens is None:
-        args.tokens = 8192 if args.workload == "moe_stack" else 1024
+        args.tokens = {"moe_stack": 8192, "act_quant": 16384, "fp4_act_quant": 16384}.get(args.workload, 1024)
     ws, rank, local = dist_env()
 
     if args.impl == "reference":
@@ -857,6 +976,8 @@ def main():
         line = bench_moe(args, torch, dist, ws, rank, dev)
     elif args.workload == "moe_stack":
         line = bench_moe_stack(args, torch, dist, ws, rank, dev)
+    elif args.workload in ("act_quant", "fp4_act_quant"):
+        line = bench_quant(args, torch, dist, ws, rank, dev)
     else:
         line = bench_fp4_decode(args, torch, dist, ws, rank, dev)
 

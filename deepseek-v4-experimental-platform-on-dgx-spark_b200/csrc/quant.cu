@@ -304,21 +304,25 @@ __global__ void __launch_bounds__(kThreads) fp4_act_quant_kernel(T* __restrict__
   }
 }
 
-// fp4_act_quant's per-element rule for a block whose scale is finite (a
-// power of two in [2^-126, 2^126], so c = x * (1/s) equals x/s exactly):
-// clamp |c| to 6, then the nearest e2m1 magnitude with ties to the smaller,
-// which on each binade of the e2m1 grid (spacing d = 0.5 below 2, 1 below 4,
-// 2 up to 6) is d * ceil(|c|/d - 0.5); the same values as e2m1_nearest.
-// The sign is torch.sign's (+0 for a zero c), the product with s is exact.
-BS_DEVINL float fp4_fake_quant(float x, float inv, float scale) {
+// fp4_act_quant's per-element rule for a block whose scale s is finite (a
+// power of two in [2^-126, 2^126], so c = x * (1/s) equals x/s exactly): the
+// nearest e2m1 magnitude of min(|c|, 6) with ties to the smaller, which on
+// each binade of the e2m1 grid (spacing d = 0.5 below 2, 1 below 4, 2 up to
+// 6) is d * ceil(|c|/d - 0.5) -- the same values as e2m1_nearest -- times s.
+//   * ds[] = {0.5 s, s, 2 s} folds the final product with s into d (exact:
+//     powers of two times a small integer; overflow to inf as the reference).
+//   * No clamp: |c| exceeds 6 only by the scale's rounding (a few ulps), and
+//     the formula already sends all of (5, 7] to 6.
+//   * torch.sign's zero rule (+0 for c = -0): copysign from c + 0, which is
+//     +0 for -0 and c otherwise.
+BS_DEVINL float fp4_fake_quant(float x, float inv, const float (&ds)[3]) {
   const float c = __fmul_rn(x, inv);
-  const float a = fminf(fabsf(c), 6.0f);
+  const float a = fabsf(c);
   const bool lo = a < 2.0f, mid = a < 4.0f;
-  const float d = lo ? 0.5f : (mid ? 1.0f : 2.0f);
+  const float d = lo ? ds[0] : (mid ? ds[1] : ds[2]);
   const float id = lo ? 2.0f : (mid ? 1.0f : 0.5f);
   const float m = __fmul_rn(d, ceilf(__fmaf_rn(a, id, -0.5f)));
-  const float q = c == 0.0f ? 0.0f : copysignf(m, c);
-  return __fmul_rn(q, scale);
+  return copysignf(m, __fadd_rn(c, 0.0f));
 }
 
 // bf16, in place, blocks of 8*TPB elements (TPB lanes of 16 bytes each); U
@@ -357,10 +361,11 @@ __global__ void __launch_bounds__(kThreads) fp4_act_quant_bf16_kernel(__nv_bfloa
       float r[8];
       if ((__float_as_uint(scale) & 0x7F800000u) != 0x7F800000u) {
         const float inv = bs_inv_pow2(scale);
+        const float ds[3] = {__fmul_rn(0.5f, scale), scale, __fmul_rn(2.0f, scale)};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          r[2 * i] = fp4_fake_quant(__uint_as_float(w[i] << 16), inv, scale);
-          r[2 * i + 1] = fp4_fake_quant(__uint_as_float(w[i] & 0xFFFF0000u), inv, scale);
+          r[2 * i] = fp4_fake_quant(__uint_as_float(w[i] << 16), inv, ds);
+          r[2 * i + 1] = fp4_fake_quant(__uint_as_float(w[i] & 0xFFFF0000u), inv, ds);
         }
       } else {
 #pragma unroll

@@ -161,6 +161,7 @@ __global__ void dispatch_kernel(const int* __restrict__ idx, int T, int topk, co
   if (lane == 0) pos_of[warp] = pos;
   const uint4* src = reinterpret_cast<const uint4*>(xq + (int64_t)t * H);
   uint4* dst = reinterpret_cast<uint4*>(ap + (int64_t)pos * H);
+#pragma unroll 8
   for (int i = lane; i < H / 16; i += 32) dst[i] = src[i];
   const int nb = H / 128;
   const int cin = pos - offsets[e];
@@ -193,21 +194,35 @@ __global__ void pack_scales_kernel(const uint8_t* __restrict__ ws, int64_t E, in
 
 // out[t] = bf16( sum_k w[t,k] * y[pos_of[t,k]] ), fp32 accumulation in slot
 // order.  One block per token, 8 bf16 per thread.
+// One block per token; the row indices and weights of all its k experts,
+// then all k row segments, are loaded before any is summed (two memory round
+// trips instead of 2k); the sum runs in k order as before.
 __global__ void combine_kernel(const __nv_bfloat16* __restrict__ y, const int* __restrict__ pos_of,
                                const float* __restrict__ w, int topk, int H, __nv_bfloat16* __restrict__ out) {
+  constexpr int kMaxTopk = 8;
   const int t = blockIdx.x;
+  int p[kMaxTopk];
+  float wk[kMaxTopk];
+#pragma unroll
+  for (int k = 0; k < kMaxTopk; ++k) {
+    p[k] = k < topk ? pos_of[(int64_t)t * topk + k] : 0;
+    wk[k] = k < topk ? w[(int64_t)t * topk + k] : 0.0f;
+  }
   for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
+    uint4 raw[kMaxTopk];
+#pragma unroll
+    for (int k = 0; k < kMaxTopk; ++k)
+      if (k < topk) raw[k] = *reinterpret_cast<const uint4*>(y + (int64_t)p[k] * H + c);
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int k = 0; k < topk; ++k) {
-      const int p = pos_of[(int64_t)t * topk + k];
-      const float wk = w[(int64_t)t * topk + k];
-      const uint4 raw = *reinterpret_cast<const uint4*>(y + (int64_t)p * H + c);
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int k = 0; k < kMaxTopk; ++k) {
+      if (k >= topk) break;
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[k]);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float2 f = __bfloat1622float2(h[j]);
-        acc[2 * j] = fmaf(wk, f.x, acc[2 * j]);
-        acc[2 * j + 1] = fmaf(wk, f.y, acc[2 * j + 1]);
+        acc[2 * j] = fmaf(wk[k], f.x, acc[2 * j]);
+        acc[2 * j + 1] = fmaf(wk[k], f.y, acc[2 * j + 1]);
       }
     }
     uint4 o;

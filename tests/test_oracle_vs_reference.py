@@ -144,3 +144,30 @@ def test_fp4_gemm_random_vs_reference(ks):
                       torch.from_numpy(b).view(torch.float4_e2m1fn_x2), torch.from_numpy(b_s).view(torch.float8_e8m0fnu))
     ref = ob.fp4_gemm(a, a_s, b, b_s, ob.DT_F32, ob.DT_E8M0)
     assert rel_fro(bits(out), ref) <= 1e-4
+
+
+@pytest.mark.parametrize("seed,T,E,topk", [(11, 40, 8, 2), (12, 24, 16, 4)])
+def test_moe_layer_random_vs_reference(ks, seed, T, E, topk):
+    """The MoE oracle against the same composition of the reference's own ops
+    (act_quant with ue8m0 scales, fp4_gemm, SiLU in fp32, the top-k weighted
+    sum), on fresh seeded cases."""
+    import cases
+    m = cases.moe_case_small(T=T, H=256, inter=256, E=E, topk=topk, seed=seed)
+    x = t_bf16(m["x"])
+    idx, w = m["idx"], m["w"]
+    inter = m["w13"].shape[1] // 2
+    acc = torch.zeros(x.shape, dtype=torch.float32)
+    for e in range(E):
+        tok, slot = np.nonzero(idx == e)
+        if tok.size == 0:
+            continue
+        h, hs = ks.act_quant(x[torch.from_numpy(tok)], 128, "ue8m0", torch.float32)
+        gu = ks.fp4_gemm(h, hs, torch.from_numpy(m["w13"][e]).view(torch.float4_e2m1fn_x2),
+                         torch.from_numpy(m["w13_s"][e]).view(torch.float8_e8m0fnu)).float()
+        z = torch.nn.functional.silu(gu[:, :inter]) * gu[:, inter:]
+        q, qs = ks.act_quant(z, 128, "ue8m0", torch.float32)
+        y = ks.fp4_gemm(q, qs, torch.from_numpy(m["w2"][e]).view(torch.float4_e2m1fn_x2),
+                        torch.from_numpy(m["w2_s"][e]).view(torch.float8_e8m0fnu)).float()
+        acc.index_add_(0, torch.from_numpy(tok), torch.from_numpy(w[tok, slot])[:, None] * y)
+    got = ob.moe_layer(m["x"], idx, w, m["w13"], m["w13_s"], m["w2"], m["w2_s"])
+    assert rel_fro(got, bits(acc.to(torch.bfloat16))) <= 1e-4

@@ -171,3 +171,25 @@ def test_moe_layer_random_vs_reference(ks, seed, T, E, topk):
         acc.index_add_(0, torch.from_numpy(tok), torch.from_numpy(w[tok, slot])[:, None] * y)
     got = ob.moe_layer(m["x"], idx, w, m["w13"], m["w13_s"], m["w2"], m["w2_s"])
     assert rel_fro(got, bits(acc.to(torch.bfloat16))) <= 1e-4
+
+
+@pytest.mark.parametrize("xdt", ["f32", "f16"])
+@pytest.mark.parametrize("fmt", [None, "ue8m0"])
+def test_quantisers_f32_f16_inputs_vs_reference(ks, xdt, fmt):
+    """fp32 and fp16 inputs (the generic kernels' dtypes) through both quantisers."""
+    rng = np.random.default_rng(5000 + len(xdt) + (1 if fmt else 0))
+    f = ob.bf16_to_f32(random_rows(rng, 48, 256, 128)).astype(np.float32)
+    f = f * np.float32(1 + 2.0 ** -9)               # bits below bf16 precision
+    if xdt == "f16":
+        f = np.clip(f, -60000, 60000)
+        x, tag, tt = ob.f32_to_f16(f), ob.DT_F16, torch.from_numpy(ob.f32_to_f16(f).view(np.float16).copy())
+    else:
+        x, tag, tt = f, ob.DT_F32, torch.from_numpy(f.copy())
+    y, s = ks.act_quant(tt.clone(), 128, fmt, torch.float32, False)
+    ry, rs = ob.act_quant(x, tag, 128, fmt, ob.DT_F32)
+    np.testing.assert_array_equal(e4m3_nan_canon(bits(y)), e4m3_nan_canon(ry))
+    same_bits_nan_aware(bits(s).view(np.float32), rs, ob.DT_F32)
+    r = ks.fp4_act_quant(tt.clone(), 32, True)
+    want = ob.fp4_act_quant_inplace(x, tag, 32)
+    got = r.numpy().view(np.uint16) if xdt == "f16" else r.numpy()
+    same_bits_nan_aware(got, want, tag)

@@ -52,7 +52,9 @@ def f16_to_f32(u16: np.ndarray) -> np.ndarray:
 
 
 def f32_to_f16(f: np.ndarray) -> np.ndarray:
-    return np.asarray(f, dtype=np.float32).astype(np.float16).view(np.uint16)
+    """Round to nearest even; beyond the fp16 range gives inf, as torch's cast does."""
+    with np.errstate(over="ignore"):
+        return np.asarray(f, dtype=np.float32).astype(np.float16).view(np.uint16)
 
 
 def _e4m3_table() -> np.ndarray:
@@ -232,7 +234,8 @@ def act_quant_inplace(x: np.ndarray, x_dtype: int = DT_BF16, block_size: int = 1
     """Quantise-dequantise back to x's dtype, kernel_sm121.py:75-81."""
     shape = np.shape(x)
     _, _, scale, clamped = _act_quant_core(x, x_dtype, block_size, scale_fmt is not None)
-    q = (e4m3_to_f32(f32_to_e4m3(clamped)) * scale[..., None]).astype(np.float32)
+    with np.errstate(invalid="ignore", over="ignore"):   # NaN / inf blocks stay NaN / inf
+        q = (e4m3_to_f32(f32_to_e4m3(clamped)) * scale[..., None]).astype(np.float32)
     return from_f32(q.reshape(shape), x_dtype)
 
 

@@ -21,6 +21,10 @@
 //                (the reference's per-128-K "promotion"; it keeps arbitrary,
 //                non power-of-two fp32 scales exact).  Two partial buffers
 //                let the MMA run one K block ahead of the epilogue.
+//                fp8 with ue8m0 scales on both operands (MX form): the
+//                producer gathers both operands' scales, the MMA applies
+//                them (kind::mxf8f6f4.block_scale), one TMEM accumulator
+//                spans the whole K range and the epilogue reads it once.
 // Split-K (swap mode): a thread-block cluster of S CTAs along K reduces its
 // fp32 tiles through distributed shared memory; no workspace, one launch.
 //

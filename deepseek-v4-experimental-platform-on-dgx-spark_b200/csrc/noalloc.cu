@@ -23,7 +23,12 @@
 //     fits up to about 500 tokens per call);
 //   * the first call on each device looks up the array's device address
 //     (cudaGetSymbolAddress) with that device current; make that first call
-//     before any stream capture.
+//     before any stream capture;
+//   * that address is kept for the life of the process: cudaDeviceReset (or
+//     anything else that tears down the device's primary context) reloads
+//     the library's device image, may move the array, and leaves the kept
+//     address stale -- do not call this entry point on a device after
+//     resetting it.
 //
 // This file is part of the single translation unit lib.cu (it uses fail()
 // from capi.cu and calls bs_moe_forward).

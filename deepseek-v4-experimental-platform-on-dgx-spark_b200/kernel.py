@@ -17,7 +17,6 @@ CPU tensors are an error: there is no CPU fallback here.
 from __future__ import annotations
 
 import time as _time
-from collections import defaultdict
 from typing import Optional
 
 import torch
@@ -26,22 +25,32 @@ from . import _lib
 
 __all__ = ["act_quant", "fp4_act_quant", "fp8_gemm", "fp4_gemm", "profile_report"]
 
-# Same shape as the reference's profiler (kernel_sm121.py:31-44): call count
-# and host seconds per op.  Host time without a device sync measures launch
-# cost for asynchronous kernels, exactly as in the reference.
-_PROFILE = defaultdict(lambda: [0, 0.0])
+# Per-op call counter and host-side seconds, reported by profile_report() in
+# the same columns as the reference module's report (kernel_sm121.py:31-44).
+# The host clock brackets the launch only (no device sync), so for these
+# asynchronous kernels it measures launch cost, as the reference's does.
+_PROFILE: dict = {}
+
+
+def _tally(op: str, t0: float) -> None:
+    rec = _PROFILE.setdefault(op, [0, 0.0])
+    rec[0] += 1
+    rec[1] += _time.perf_counter() - t0
 
 
 def profile_report():
-    """Print accumulated per-op call counts / host seconds and reset."""
+    """Print each op's call count and host seconds (largest first), then clear them."""
     if not _PROFILE:
         return
-    print("[bsgemm] === Profile Report ===", flush=True)
-    total = sum(v[1] for v in _PROFILE.values())
-    for name, (cnt, sec) in sorted(_PROFILE.items(), key=lambda kv: -kv[1][1]):
-        pct = sec / total * 100 if total > 0 else 0
-        print(f"  {name:25s}: {cnt:6d} calls, {sec:7.3f}s ({pct:5.1f}%)", flush=True)
-    print(f"  {'TOTAL':25s}: {sum(v[0] for v in _PROFILE.values()):6d} calls, {total:7.3f}s", flush=True)
+    rows = sorted(_PROFILE.items(), key=lambda item: item[1][1], reverse=True)
+    secs = sum(rec[1] for _, rec in rows)
+    calls = sum(rec[0] for _, rec in rows)
+    lines = ["[bsgemm] per-op host time"]
+    for op, (n, t) in rows:
+        share = 100.0 * t / secs if secs > 0 else 0.0
+        lines.append(f"  {op:25s}: {n:6d} calls, {t:7.3f}s ({share:5.1f}%)")
+    lines.append(f"  {'TOTAL':25s}: {calls:6d} calls, {secs:7.3f}s")
+    print("\n".join(lines), flush=True)
     _PROFILE.clear()
 
 
@@ -82,8 +91,7 @@ def act_quant(x: torch.Tensor, block_size: int = 128, scale_fmt: Optional[str] =
         _lib.check(lib.bs_act_quant_inplace(xc.data_ptr(), _X_DT[xc.dtype], rows, N, block_size, pow2, _stream(x)))
         if xc.data_ptr() != x.data_ptr() or xc.dtype != x.dtype:
             x.copy_(xc)
-        _PROFILE["act_quant_inplace"][0] += 1
-        _PROFILE["act_quant_inplace"][1] += _time.perf_counter() - t0
+        _tally("act_quant_inplace", t0)
         return x
     if scale_dtype not in _S_DT:
         raise NotImplementedError(f"act_quant: scale_dtype {scale_dtype} not supported")
@@ -91,8 +99,7 @@ def act_quant(x: torch.Tensor, block_size: int = 128, scale_fmt: Optional[str] =
     s = torch.empty(*x.shape[:-1], N // block_size, dtype=scale_dtype, device=x.device)
     _lib.check(lib.bs_act_quant(xc.data_ptr(), _X_DT[xc.dtype], rows, N, block_size, pow2, y.data_ptr(),
                                 s.data_ptr(), _S_DT[scale_dtype], _stream(x)))
-    _PROFILE["act_quant"][0] += 1
-    _PROFILE["act_quant"][1] += _time.perf_counter() - t0
+    _tally("act_quant", t0)
     return y, s
 
 
@@ -101,7 +108,7 @@ def fp4_act_quant(x: torch.Tensor, block_size: int = 32, inplace: bool = False) 
     N = x.size(-1)
     assert N % block_size == 0
     if not inplace:
-        raise NotImplementedError("fp4_act_quant non-inplace not needed for sm_121 fallback")
+        raise NotImplementedError("fp4_act_quant: only inplace=True is supported (the model calls it in place)")
     _require_cuda(x)
     xc = x.contiguous()
     if xc.dtype not in _X_DT:
@@ -144,8 +151,7 @@ def fp8_gemm(a: torch.Tensor, a_s: torch.Tensor, b: torch.Tensor, b_s: torch.Ten
     out = torch.empty(M, N, device=a.device, dtype=torch.bfloat16)
     _lib.check(_lib.load().bs_fp8_gemm(a_flat.data_ptr(), a_sf.data_ptr(), as_dt, b_flat.data_ptr(),
                                        b_sf.data_ptr(), bs_dt, M, N, K, out.data_ptr(), _stream(a)))
-    _PROFILE["fp8_gemm"][0] += 1
-    _PROFILE["fp8_gemm"][1] += _time.perf_counter() - t0
+    _tally("fp8_gemm", t0)
     return out.view(out_shape)
 
 
@@ -187,6 +193,5 @@ def fp4_gemm(a: torch.Tensor, a_s: torch.Tensor, b: torch.Tensor, b_s: torch.Ten
     out = torch.empty(M, N, device=a.device, dtype=torch.bfloat16)
     _lib.check(_lib.load().bs_fp4_gemm(a_flat.data_ptr(), a_sf.data_ptr(), as_dt, b_u8.data_ptr(),
                                        b_sf.data_ptr(), _lib.DT_E8M0, M, N, K, out.data_ptr(), _stream(a)))
-    _PROFILE["fp4_gemm"][0] += 1
-    _PROFILE["fp4_gemm"][1] += _time.perf_counter() - t0
+    _tally("fp4_gemm", t0)
     return out.view(out_shape)

@@ -41,10 +41,17 @@ def bf16_to_f32(u16: np.ndarray) -> np.ndarray:
 def f32_to_bf16(f: np.ndarray) -> np.ndarray:
     """float32 -> bf16 bits, round-to-nearest-even; NaN -> 0x7FC0 (c10 rule)."""
     f = np.asarray(f, dtype=np.float32)
-    bits = f.view(np.uint32).astype(np.uint64)
-    bias = ((bits >> 16) & 1) + 0x7FFF
-    out = ((bits + bias) >> 16).astype(np.uint16)
-    return np.where(np.isnan(f), np.uint16(0x7FC0), out).astype(np.uint16)
+    bits = f.view(np.uint32)
+    # bits + 0x7FFF + lsb stays below 2^32 for every non-NaN pattern (the
+    # largest, -inf 0xFF800000, gains at most 0x8000), and NaNs are replaced
+    acc = (bits >> 16) & np.uint32(1)
+    acc += np.uint32(0x7FFF)
+    with np.errstate(over="ignore"):
+        acc += bits
+    acc >>= 16
+    out = acc.astype(np.uint16)
+    out[np.isnan(f)] = 0x7FC0
+    return out
 
 
 def f16_to_f32(u16: np.ndarray) -> np.ndarray:
@@ -278,15 +285,17 @@ FP4_TABLE = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0,
                       0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0], dtype=np.float32)
 
 
+# every byte's two decoded values: [byte] -> (low nibble, high nibble)
+_FP4_PAIRS = np.stack([FP4_TABLE[np.arange(256) & 0x0F], FP4_TABLE[np.arange(256) >> 4]], axis=-1)
+
+
 def dequant_fp4(b: np.ndarray) -> np.ndarray:
     """Packed e2m1 [N, K/2] -> fp32 [N, K] (kernel_sm121.py:263-266, 334-340).
 
     Low nibble holds the even k, high nibble the odd k.
     """
     b = np.asarray(b, dtype=np.uint8)
-    lo = FP4_TABLE[b & 0x0F]
-    hi = FP4_TABLE[(b >> 4) & 0x0F]
-    return np.stack([lo, hi], axis=-1).reshape(*b.shape[:-1], b.shape[-1] * 2)
+    return _FP4_PAIRS[b].reshape(*b.shape[:-1], b.shape[-1] * 2)
 
 
 def _scales_f32(s: np.ndarray, dtype: int) -> np.ndarray:
@@ -377,7 +386,7 @@ def moe_route(logits: np.ndarray, topk: int):
 
 def moe_layer(x_bf16: np.ndarray, idx: np.ndarray, w: np.ndarray,
               w13: np.ndarray, w13_s: np.ndarray, w2: np.ndarray, w2_s: np.ndarray,
-              experts=None) -> np.ndarray:
+              experts=None, workers: int = 1) -> np.ndarray:
     """MoE layer composed from the reference ops, expert by expert.
 
     Per expert e and its routed tokens: h = act_quant(x, 128, "ue8m0");
@@ -386,21 +395,36 @@ def moe_layer(x_bf16: np.ndarray, idx: np.ndarray, w: np.ndarray,
     q = act_quant(z, 128, "ue8m0"); y = fp4_gemm(q, W2_e); the token output
     is sum_k w[t,k] * y_k accumulated in fp32, rounded to bf16.
     ``experts`` restricts the computation to a subset (contributions from
-    other experts are left out), for sampled checks at large sizes.
+    other experts are left out), for sampled checks at large sizes.  The
+    weight arguments only need ``.shape`` and ``[e]`` (so a caller can fetch
+    one expert at a time); ``workers`` > 1 computes the experts' outputs on
+    that many threads and still sums them in expert order (same result).
     """
     T, H = x_bf16.shape
     E, twoI, _ = w13.shape
     inter = twoI // 2
     out = np.zeros((T, H), dtype=np.float32)
     ex_list = range(E) if experts is None else experts
-    for e in ex_list:
+
+    def expert(e):
         tok, slot = np.nonzero(idx == e)
         if tok.size == 0:
-            continue
+            return None
         h, hs = act_quant(x_bf16[tok], DT_BF16, 128, "ue8m0", DT_F32)
         gu = bf16_to_f32(fp4_gemm(h, hs, w13[e], w13_s[e], DT_F32, DT_E8M0))
         z = (silu_f32(gu[:, :inter]) * gu[:, inter:]).astype(np.float32)
         q, qs = act_quant(z, DT_F32, 128, "ue8m0", DT_F32)
         y = bf16_to_f32(fp4_gemm(q, qs, w2[e], w2_s[e], DT_F32, DT_E8M0))
-        np.add.at(out, tok, w[tok, slot][:, None] * y)
+        return tok, slot, y
+
+    if workers > 1:
+        from concurrent.futures import ThreadPoolExecutor
+        with ThreadPoolExecutor(workers) as pool:
+            parts = list(pool.map(expert, ex_list))
+    else:
+        parts = [expert(e) for e in ex_list]
+    for part in parts:
+        if part is not None:
+            tok, slot, y = part
+            np.add.at(out, tok, w[tok, slot][:, None] * y)
     return f32_to_bf16(out)

@@ -2,7 +2,9 @@
 
 Run once in a container where the reference project is mounted:
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <reference project directory>
+
+(or with the directory in ``BS_REFERENCE_DIR``).
 
 It imports the reference module ``kernel_sm121`` and calls ``act_quant``,
 ``fp4_act_quant``, ``fp8_gemm`` and ``fp4_gemm`` on CPU tensors (the branch
@@ -132,4 +134,7 @@ def main(ref_dir: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("BS_REFERENCE_DIR", "")
+    if not ref:
+        sys.exit("usage: make_golden.py <reference project directory> (or set BS_REFERENCE_DIR)")
+    main(ref)

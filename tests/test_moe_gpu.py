@@ -11,6 +11,7 @@ activation can land one step apart).
 from __future__ import annotations
 
 import importlib
+import os
 
 import numpy as np
 import pytest
@@ -129,6 +130,50 @@ def test_moe_config4_consistency(T, skew):
         print(f"most popular expert receives {top} rows")
     print(f"moe T={T} skew={skew} sampled tokens: rel_fro={e:.3e}")
     assert e <= TOL
+
+
+class _ExpertFetch:
+    """One expert's tensor at a time, copied to the host on demand, so the
+    oracle can read the experts it needs without a host copy of all of them."""
+
+    def __init__(self, t: torch.Tensor):
+        self.t, self.shape = t, tuple(t.shape)
+
+    def __getitem__(self, e):
+        return self.t[e].cpu().numpy()
+
+
+@pytest.mark.parametrize("T,skew", [(1024, False), (2048, True)])
+def test_moe_config_shapes_vs_oracle(T, skew):
+    """MoE layer at the config-4 shape (H=4096, I=2048, E=256, top-8, T=1024)
+    and at T=2048 with the Zipf-like popularity skew of the long-prefill
+    config, against the oracle's composition of the reference ops
+    (kernel_sm121.py:55-87 act_quant, :343-421 fp4_gemm) on 32 sampled tokens
+    and every expert they route to.  Tolerance: relative Frobenius <= 1e-2,
+    max-abs printed."""
+    mm = moe_mod()
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev)
+    g.manual_seed(100 + T)
+    H, I, E, k = 4096, 2048, 256, 8
+    x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    logits = torch.randn(T, E, generator=g, device=dev)
+    if skew:
+        logits += zipf_bias(E, 9).to(dev)
+    w13 = torch.randint(0, 256, (E, 2 * I, H // 2), generator=g, device=dev, dtype=torch.uint8)
+    w13_s = 127 - torch.randint(0, 7, (E, 2 * I, H // 32), generator=g, device=dev, dtype=torch.uint8)
+    w2 = torch.randint(0, 256, (E, H, I // 2), generator=g, device=dev, dtype=torch.uint8)
+    w2_s = 127 - torch.randint(0, 7, (E, H, I // 32), generator=g, device=dev, dtype=torch.uint8)
+    out = mm.moe_forward(x, logits, mm.MoEWeights(w13, w13_s, w2, w2_s), k)
+    torch.cuda.synchronize()
+    tok = np.sort(np.random.default_rng(T).choice(T, size=32, replace=False))
+    sel = torch.from_numpy(tok).to(dev)
+    idx, wts = ob.moe_route(logits[sel].cpu().numpy(), k)
+    experts = np.unique(idx)
+    ref = ob.moe_layer(bits(x[sel]), idx, wts, _ExpertFetch(w13), _ExpertFetch(w13_s), _ExpertFetch(w2),
+                       _ExpertFetch(w2_s), experts=experts, workers=min(16, len(os.sched_getaffinity(0))))
+    print(f"moe T={T} skew={skew}: {len(tok)} sampled tokens over {len(experts)} experts")
+    check(bits(out[sel]), ref, f"moe config shape T={T} skew={skew}")
 
 
 def test_pack_scales_layout():

@@ -5,8 +5,8 @@ seeded inputs each time (wide exponent ranges, inf / NaN / zero / subnormal
 blocks, values a few ulps around rounding ties) and runs them through both
 ``kernel_sm121`` (its CPU branches, as ``tests/golden/make_golden.py`` does)
 and ``oracle.blockscaled``.  It needs the reference project on disk: the
-directory comes from ``BS_REFERENCE_DIR`` (default: the checkout the golden
-script reads) and the test skips where it is absent.
+directory comes from the ``BS_REFERENCE_DIR`` environment variable, and the
+test skips when it is unset or does not hold ``kernel_sm121.py``.
 
 Quantisers are compared bit for bit, NaNs as NaNs (their sign and payload
 are the platform's); GEMMs to 1e-4 relative Frobenius (accumulation order).
@@ -24,13 +24,13 @@ import torch
 from conftest import rel_fro
 from oracle import blockscaled as ob
 
-REF_DIR = os.environ.get("BS_REFERENCE_DIR", "/root/reference")
+REF_DIR = os.environ.get("BS_REFERENCE_DIR", "")
 
 
 @pytest.fixture(scope="module")
 def ks():
-    if not os.path.exists(os.path.join(REF_DIR, "kernel_sm121.py")):
-        pytest.skip("reference project not present")
+    if not REF_DIR or not os.path.exists(os.path.join(REF_DIR, "kernel_sm121.py")):
+        pytest.skip("BS_REFERENCE_DIR does not point at the reference project")
     sys.path.insert(0, REF_DIR)
     try:
         import kernel_sm121

@@ -258,9 +258,70 @@ MoeLayout moe_layout(int64_t T, int H, int I, int E, int topk) {
 }
 }  // namespace
 
+namespace {
+// Sizes the three-kernel layer supports: two 128-row W2 tiles per work item
+// (H a multiple of 256) and return addresses of 24 bits.
+bool fused_ok(int64_t T, int H, int topk) { return H % 256 == 0 && T * topk < (int64_t(1) << 24); }
+
+// Workspace of the three-kernel layer.  `local_only`: the expert-parallel
+// form, whose receive buffers, count matrix, return buffer and sync words
+// live in peer-mapped memory the caller passes separately.
+struct FusedLayout {
+  size_t sync, counts, cursor, zero_end, cnt_all, xq, xs, idx, w, offsets, chunks, hq, hsp, hdone, rows, rows_sp, ret,
+      y_back, total;
+  int64_t cap, chunk_cap;
+};
+FusedLayout fused_layout(int64_t T_max, int H, int I, int E, int topk, int n_ranks, bool local_only) {
+  FusedLayout L = {};
+  const int El = E / n_ranks;
+  L.cap = (int64_t)n_ranks * T_max * topk;
+  L.chunk_cap = bs_moe_max_chunks(L.cap, El);
+  size_t o = 0;
+  auto take = [&](size_t bytes) { size_t at = o; o += up256(bytes); return at; };
+  // cleared before every single-GPU call (one memset): sync words, counters
+  L.sync = local_only ? 0 : take(8 * (size_t)mf::kSyncWords);
+  L.counts = take(4 * 2 * (size_t)E);
+  L.cursor = take(4 * 2 * (size_t)E);
+  L.zero_end = o;
+  L.cnt_all = local_only ? 0 : take(4 * (size_t)E);
+  L.xq = take((size_t)T_max * H);
+  L.xs = take((size_t)T_max * (H / 128));
+  L.idx = take(4 * (size_t)T_max * topk);
+  L.w = take(4 * (size_t)T_max * topk);
+  L.offsets = take(4 * (size_t)(El + 1));
+  L.chunks = take(4 * (size_t)(El + 1));
+  L.hq = take((size_t)L.cap * I);
+  L.hsp = take((size_t)L.chunk_cap * (I / 128) * 512);
+  L.hdone = take(4 * (size_t)L.chunk_cap);
+  if (!local_only) {
+    L.rows = take((size_t)L.cap * H);
+    L.rows_sp = take((size_t)L.chunk_cap * (H / 128) * 512);
+    L.ret = take(4 * (size_t)L.cap);
+    L.y_back = take((size_t)T_max * topk * H * 2);
+  }
+  L.total = o;
+  return L;
+}
+
+int moe_forward_staged(const void* x, const float* logits, int64_t T, int H, int I, int E, int topk, const void* w13,
+                       const void* w13_sp, const void* w2, const void* w2_sp, void* out, void* workspace,
+                       size_t workspace_bytes, void* stream);
+}  // namespace
+
 size_t bs_moe_workspace_size(int64_t T, int H, int I, int E, int topk) {
   if (check_moe_dims(T, H, I, E, topk)) return 0;
+  if (fused_ok(T, H, topk)) return fused_layout(T, H, I, E, topk, 1, false).total;
   return moe_layout(T, H, I, E, topk).total;
+}
+
+size_t bs_moe_staged_workspace_size(int64_t T, int H, int I, int E, int topk) {
+  if (check_moe_dims(T, H, I, E, topk)) return 0;
+  return moe_layout(T, H, I, E, topk).total;
+}
+
+void bs_moe_time_experts(void* ev_begin, void* ev_end) {
+  mf::t_ev_begin = (cudaEvent_t)ev_begin;
+  mf::t_ev_end = (cudaEvent_t)ev_end;
 }
 
 int bs_moe_pack_scales(const void* w_s, int64_t E, int rows, int K, void* out, void* stream) {
@@ -273,17 +334,82 @@ int bs_moe_pack_scales(const void* w_s, int64_t E, int rows, int K, void* out, v
 
 int64_t bs_moe_chunk_capacity(int64_t rows, int E) { return rows < 0 || E <= 0 ? 0 : bs_moe_max_chunks(rows, E); }
 
+static int moe_forward_fused(const void* x, const float* logits, int64_t T, int H, int I, int E, int topk,
+                             const void* w13, const void* w13_sp, const void* w2, const void* w2_sp, void* out,
+                             void* workspace, size_t workspace_bytes, void* stream) {
+  const FusedLayout L = fused_layout(T, H, I, E, topk, 1, false);
+  if (workspace_bytes < L.total)
+    return fail(BS_ERR_INVALID_ARG, "moe: workspace of %zu bytes, %zu needed", workspace_bytes, L.total);
+  cudaStream_t s = (cudaStream_t)stream;
+  uint8_t* ws = (uint8_t*)workspace;
+  cudaError_t e = cudaMemsetAsync(ws, 0, L.zero_end, s);   // epoch and counters: every call is epoch 1
+  if (e != cudaSuccess) return cuda_status(e, "moe: clearing the sync words");
+  mf::Layer ly = {};
+  mf::FrontArgs& f = ly.f;
+  f.x = (const __nv_bfloat16*)x; f.logits = logits;
+  f.T = (int)T; f.H = H; f.E = E; f.topk = topk; f.El = E; f.n = 1; f.me = 0;
+  f.cap = L.cap; f.chunk_cap = L.chunk_cap;
+  f.xq = ws + L.xq; f.xs = ws + L.xs; f.idx = (int*)(ws + L.idx); f.w = (float*)(ws + L.w);
+  f.counts = (int*)(ws + L.counts); f.cursor = (int*)(ws + L.cursor);
+  f.offsets = (int*)(ws + L.offsets); f.chunk_prefix = (int*)(ws + L.chunks); f.h_done = (int*)(ws + L.hdone);
+  mf::ExpArgs& xa = ly.x;
+  xa.E = E; xa.H = H; xa.I = I; xa.n = 1; xa.me = 0; xa.cap = L.cap;
+  xa.offsets = f.offsets; xa.chunk_prefix = f.chunk_prefix; xa.a_sp = ws + L.rows_sp; xa.ret = (const int*)(ws + L.ret);
+  xa.w13_sp = (const uint8_t*)w13_sp; xa.w2_sp = (const uint8_t*)w2_sp;
+  xa.hq = ws + L.hq; xa.hs_p = ws + L.hsp; xa.h_done = f.h_done;
+  ly.pr.cnt_all[0] = (int*)(ws + L.cnt_all); ly.pr.rows[0] = ws + L.rows; ly.pr.rows_sp[0] = ws + L.rows_sp;
+  ly.pr.ret[0] = (int*)(ws + L.ret); ly.pr.y_back[0] = (__nv_bfloat16*)(ws + L.y_back);
+  ly.pr.sync[0] = (unsigned long long*)(ws + L.sync);
+  ly.w13 = w13; ly.w2 = w2; ly.out = (__nv_bfloat16*)out; ly.wts = f.w;
+  int status = 0;
+  e = mf::run_layer(ly, s, &status);
+  if (status) return fail(status, "moe: could not build TMA descriptors");
+  return cuda_status(e, "moe layer");
+}
+
+static int check_moe_ptrs(const char* name, const void* x, const float* logits, const void* w13, const void* w13_sp,
+                          const void* w2, const void* w2_sp, const void* out, const void* workspace) {
+  if (!x || !logits || !w13 || !w13_sp || !w2 || !w2_sp || !out || !workspace)
+    return fail(BS_ERR_INVALID_ARG, "%s: null pointer", name);
+  if (!aligned(x, 16) || !aligned(out, 16) || !aligned(w13, 32) || !aligned(w2, 32) || !aligned(workspace, 256) ||
+      !aligned(w13_sp, 16) || !aligned(w2_sp, 16))
+    return fail(BS_ERR_INVALID_ARG, "%s: alignment (x,out,scales 16 B; weights 32 B; workspace 256 B)", name);
+  return BS_OK;
+}
+
 int bs_moe_forward(const void* x, const float* logits, int64_t T, int H, int I, int E, int topk, const void* w13,
                    const void* w13_sp, const void* w2, const void* w2_sp, void* out, void* workspace,
                    size_t workspace_bytes, void* stream) {
   int st = check_moe_dims(T, H, I, E, topk);
   if (st) return st;
   if (T == 0) return BS_OK;
-  if (!x || !logits || !w13 || !w13_sp || !w2 || !w2_sp || !out || !workspace)
-    return fail(BS_ERR_INVALID_ARG, "moe: null pointer");
-  if (!aligned(x, 16) || !aligned(out, 16) || !aligned(w13, 32) || !aligned(w2, 32) || !aligned(workspace, 256) ||
-      !aligned(w13_sp, 16) || !aligned(w2_sp, 16))
-    return fail(BS_ERR_INVALID_ARG, "moe: alignment (x,out,scales 16 B; weights 32 B; workspace 256 B)");
+  st = check_moe_ptrs("moe", x, logits, w13, w13_sp, w2, w2_sp, out, workspace);
+  if (st) return st;
+  if (fused_ok(T, H, topk))
+    return moe_forward_fused(x, logits, T, H, I, E, topk, w13, w13_sp, w2, w2_sp, out, workspace, workspace_bytes,
+                             stream);
+  return moe_forward_staged(x, logits, T, H, I, E, topk, w13, w13_sp, w2, w2_sp, out, workspace, workspace_bytes,
+                            stream);
+}
+
+int bs_moe_forward_staged(const void* x, const float* logits, int64_t T, int H, int I, int E, int topk,
+                          const void* w13, const void* w13_sp, const void* w2, const void* w2_sp, void* out,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  int st = check_moe_dims(T, H, I, E, topk);
+  if (st) return st;
+  if (T == 0) return BS_OK;
+  st = check_moe_ptrs("moe_staged", x, logits, w13, w13_sp, w2, w2_sp, out, workspace);
+  if (st) return st;
+  return moe_forward_staged(x, logits, T, H, I, E, topk, w13, w13_sp, w2, w2_sp, out, workspace, workspace_bytes,
+                            stream);
+}
+
+namespace {
+// act_quant, route, scan, dispatch, two grouped GEMM launches, combine (the
+// building blocks the NCCL expert-parallel form also uses)
+int moe_forward_staged(const void* x, const float* logits, int64_t T, int H, int I, int E, int topk, const void* w13,
+                       const void* w13_sp, const void* w2, const void* w2_sp, void* out, void* workspace,
+                       size_t workspace_bytes, void* stream) {
   const MoeLayout L = moe_layout(T, H, I, E, topk);
   if (workspace_bytes < L.total)
     return fail(BS_ERR_INVALID_ARG, "moe: workspace of %zu bytes, %zu needed", workspace_bytes, L.total);
@@ -310,6 +436,90 @@ int bs_moe_forward(const void* x, const float* logits, int64_t T, int H, int I, 
   if (r) return cuda_status(e, "moe grouped GEMM");
   e = bs_launch_moe_combine((const __nv_bfloat16*)(ws + L.y), pos, w, (int)T, topk, H, (__nv_bfloat16*)out, s);
   return cuda_status(e, "moe combine");
+}
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// expert-parallel layer over peer memory (three kernels, no NCCL, no host sync)
+// ---------------------------------------------------------------------------
+
+static int check_ep(const char* name, int64_t T_max, int H, int I, int E, int topk, int rank, int n_ranks) {
+  int st = check_moe_dims(T_max, H, I, E, topk);
+  if (st) return st;
+  if (n_ranks < 1 || n_ranks > mf::kMaxRanks || rank < 0 || rank >= n_ranks)
+    return fail(BS_ERR_INVALID_ARG, "%s: rank %d of %d (1..%d ranks)", name, rank, n_ranks, mf::kMaxRanks);
+  if (E % n_ranks) return fail(BS_ERR_UNSUPPORTED, "%s: %d experts do not split over %d ranks", name, E, n_ranks);
+  if (!fused_ok((int64_t)n_ranks * T_max, H, topk))
+    return fail(BS_ERR_UNSUPPORTED, "%s: hidden %d must be a multiple of 256 and ranks x max_tokens x topk < 2^24",
+                name, H);
+  return BS_OK;
+}
+
+int bs_ep_moe_sizes(int64_t max_tokens, int H, int I, int E, int topk, int n_ranks, int64_t* sizes) {
+  int st = check_ep("ep_moe_sizes", max_tokens, H, I, E, topk, 0, n_ranks);
+  if (st) return st;
+  if (!sizes) return fail(BS_ERR_INVALID_ARG, "ep_moe_sizes: null output");
+  const FusedLayout L = fused_layout(max_tokens, H, I, E, topk, n_ranks, true);
+  sizes[0] = (int64_t)L.total;                                   // workspace (this rank only)
+  sizes[1] = 4 * (int64_t)n_ranks * E;                           // cnt_all
+  sizes[2] = L.cap * H;                                          // rows
+  sizes[3] = L.chunk_cap * (H / 128) * 512;                      // rows_sp
+  sizes[4] = 4 * L.cap;                                          // ret
+  sizes[5] = max_tokens * topk * H * 2;                          // y_back
+  sizes[6] = 8 * mf::kSyncWords;                                 // sync
+  return BS_OK;
+}
+
+int bs_ep_moe_forward(const void* x, const float* logits, int64_t T, int64_t max_tokens, int H, int I, int E,
+                      int topk, int rank, int n_ranks, const void* w13, const void* w13_sp, const void* w2,
+                      const void* w2_sp, void* out, void* const* peer_bufs, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  int st = check_ep("ep_moe_forward", max_tokens, H, I, E, topk, rank, n_ranks);
+  if (st) return st;
+  if (T < 0 || T > max_tokens)
+    return fail(BS_ERR_INVALID_ARG, "ep_moe_forward: %lld tokens > max_tokens %lld", (long long)T,
+                (long long)max_tokens);
+  if ((T > 0 && (!x || !logits || !out)) || !w13 || !w13_sp || !w2 || !w2_sp || !peer_bufs || !workspace)
+    return fail(BS_ERR_INVALID_ARG, "ep_moe_forward: null pointer");
+  if ((T > 0 && (!aligned(x, 16) || !aligned(out, 16))) || !aligned(w13, 32) || !aligned(w2, 32) ||
+      !aligned(workspace, 256) || !aligned(w13_sp, 16) || !aligned(w2_sp, 16))
+    return fail(BS_ERR_INVALID_ARG, "ep_moe_forward: alignment (x,out,scales 16 B; weights 32 B; workspace 256 B)");
+  static const int kAlign[6] = {4, 16, 16, 4, 16, 8};
+  for (int k = 0; k < 6; ++k)
+    for (int q = 0; q < n_ranks; ++q)
+      if (!peer_bufs[k * n_ranks + q] || !aligned(peer_bufs[k * n_ranks + q], kAlign[k]))
+        return fail(BS_ERR_INVALID_ARG, "ep_moe_forward: peer buffer %d of rank %d null or misaligned", k, q);
+  const FusedLayout L = fused_layout(max_tokens, H, I, E, topk, n_ranks, true);
+  if (workspace_bytes < L.total)
+    return fail(BS_ERR_INVALID_ARG, "ep_moe_forward: workspace of %zu bytes, %zu needed", workspace_bytes, L.total);
+  uint8_t* ws = (uint8_t*)workspace;
+  const int El = E / n_ranks;
+  mf::Layer ly = {};
+  mf::FrontArgs& f = ly.f;
+  f.x = (const __nv_bfloat16*)x; f.logits = logits;
+  f.T = (int)T; f.H = H; f.E = E; f.topk = topk; f.El = El; f.n = n_ranks; f.me = rank;
+  f.cap = L.cap; f.chunk_cap = L.chunk_cap;
+  f.xq = ws + L.xq; f.xs = ws + L.xs; f.idx = (int*)(ws + L.idx); f.w = (float*)(ws + L.w);
+  f.counts = (int*)(ws + L.counts); f.cursor = (int*)(ws + L.cursor);
+  f.offsets = (int*)(ws + L.offsets); f.chunk_prefix = (int*)(ws + L.chunks); f.h_done = (int*)(ws + L.hdone);
+  for (int q = 0; q < n_ranks; ++q) {
+    ly.pr.cnt_all[q] = (int*)peer_bufs[0 * n_ranks + q];
+    ly.pr.rows[q] = (uint8_t*)peer_bufs[1 * n_ranks + q];
+    ly.pr.rows_sp[q] = (uint8_t*)peer_bufs[2 * n_ranks + q];
+    ly.pr.ret[q] = (int*)peer_bufs[3 * n_ranks + q];
+    ly.pr.y_back[q] = (__nv_bfloat16*)peer_bufs[4 * n_ranks + q];
+    ly.pr.sync[q] = (unsigned long long*)peer_bufs[5 * n_ranks + q];
+  }
+  mf::ExpArgs& xa = ly.x;
+  xa.E = El; xa.H = H; xa.I = I; xa.n = n_ranks; xa.me = rank; xa.cap = L.cap;
+  xa.offsets = f.offsets; xa.chunk_prefix = f.chunk_prefix; xa.a_sp = ly.pr.rows_sp[rank]; xa.ret = ly.pr.ret[rank];
+  xa.w13_sp = (const uint8_t*)w13_sp; xa.w2_sp = (const uint8_t*)w2_sp;
+  xa.hq = ws + L.hq; xa.hs_p = ws + L.hsp; xa.h_done = f.h_done;
+  ly.w13 = w13; ly.w2 = w2; ly.out = (__nv_bfloat16*)out; ly.wts = f.w;
+  int status = 0;
+  cudaError_t e = mf::run_layer(ly, (cudaStream_t)stream, &status);
+  if (status) return fail(status, "ep_moe_forward: could not build TMA descriptors");
+  return cuda_status(e, "ep_moe_forward");
 }
 
 int bs_moe_route(const float* logits, int64_t T, int E, int topk, int* idx, float* w, int* counts, void* stream) {

@@ -7,5 +7,6 @@
 #include "moe.cu"
 #include "peer.cu"
 #include "ep.cu"
+#include "moe_fused.cu"
 #include "capi.cu"
 #include "noalloc.cu"

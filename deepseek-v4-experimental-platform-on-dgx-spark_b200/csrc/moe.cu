@@ -42,17 +42,13 @@ constexpr int kTok = 112;
 // routing
 // ---------------------------------------------------------------------------
 
-// One warp per token.  Ties keep the lower expert index (a stable sort of
-// -logits).  Weights: softmax over the k selected logits.  kMaxPer logits per
-// lane (E <= 32 * kMaxPer), chosen per launch so that no round scans empty
-// slots.
+// Top-k of one token's E gate logits by one warp (every lane calls it with
+// the same row).  Ties keep the lower expert index (a stable sort of
+// -logits); NaN logits rank below every number.  kMaxPer logits per lane
+// (E <= 32 * kMaxPer).  sel_v / sel_e (valid on every lane) hold the k
+// selected logits and experts in descending order.
 template <int kMaxPer>
-__global__ void route_kernel(const float* __restrict__ logits, int T, int E, int topk, int* __restrict__ idx,
-                             float* __restrict__ w, int* __restrict__ counts) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (warp >= T) return;
-  const float* row = logits + (int64_t)warp * E;
+BS_DEVINL void route_one(const float* __restrict__ row, int E, int topk, int lane, float* sel_v, int* sel_e) {
   float v[kMaxPer];
   const int per = (E + 31) / 32;
 #pragma unroll
@@ -61,8 +57,6 @@ __global__ void route_kernel(const float* __restrict__ logits, int T, int E, int
     v[i] = (i < per && e < E) ? row[e] : -INFINITY;
     if (v[i] != v[i]) v[i] = -INFINITY;
   }
-  float sel_v[8];
-  int sel_e[8];
   for (int k = 0; k < topk; ++k) {
     float bv = -INFINITY;
     int be = 0x7fffffff;
@@ -84,13 +78,31 @@ __global__ void route_kernel(const float* __restrict__ logits, int T, int E, int
         if (i == (be >> 5)) v[i] = -INFINITY;
     }
   }
+}
+
+// Softmax over the k selected logits (fp32, in slot order).
+BS_DEVINL float route_weight(const float* sel_v, int topk, int k) {
+  const float m = sel_v[0];
+  float den = 0.f;
+  for (int j = 0; j < topk; ++j) den += expf(sel_v[j] - m);
+  return expf(sel_v[k] - m) / den;
+}
+
+// One warp per token: top-k experts, their softmax weights, and the expert
+// histogram.
+template <int kMaxPer>
+__global__ void route_kernel(const float* __restrict__ logits, int T, int E, int topk, int* __restrict__ idx,
+                             float* __restrict__ w, int* __restrict__ counts) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  float sel_v[8];
+  int sel_e[8];
+  route_one<kMaxPer>(logits + (int64_t)warp * E, E, topk, lane, sel_v, sel_e);
   if (lane == 0) {
-    const float m = sel_v[0];
-    float den = 0.f;
-    for (int k = 0; k < topk; ++k) den += expf(sel_v[k] - m);
     for (int k = 0; k < topk; ++k) {
       idx[(int64_t)warp * topk + k] = sel_e[k];
-      w[(int64_t)warp * topk + k] = expf(sel_v[k] - m) / den;
+      w[(int64_t)warp * topk + k] = route_weight(sel_v, topk, k);
       atomicAdd(&counts[sel_e[k]], 1);
     }
   }

@@ -1,0 +1,766 @@
+// The MoE layer as three kernels, on one GPU or expert parallel over NVLink
+// peer memory with the same code (one GPU = one rank that owns every expert).
+//
+//   front    (cooperative, one CTA per SM)
+//            A: e4m3 quantisation of this rank's tokens (ue8m0 1x128),
+//               top-k routing + softmax weights, expert histogram
+//            -- grid barrier --
+//            B: this rank's histogram into row `me` of every rank's count
+//               matrix, then a flag at every rank; wait for every rank's
+//               flag; from the full count matrix every CTA plans, in shared
+//               memory, where each (rank, expert) group of rows lands at its
+//               owner (owner ranges of E/n experts: rows of the owner's
+//               experts in order, inside an expert the rows of lower ranks
+//               first) and which <=112-row chunk each row falls in
+//            C: one warp per (token, slot): the e4m3 row, its scale words (in
+//               the grouped GEMM's packed chunk layout) and a return address
+//               (rank << 24 | token * topk + slot) stored straight into the
+//               owner's receive buffers; then each CTA adds 1 to every
+//               rank's rows-arrived counter
+//   experts  (cooperative, one CTA per SM, persistent) waits until every
+//            rank's front CTAs have arrived, then runs W1|W3 work items
+//            (gate + up tiles, fused SwiGLU + e4m3 quantisation of the
+//            hidden rows) and W2 work items (two 128-row output tiles) from
+//            one static list; a W2 item waits until all W1|W3 items of its
+//            token chunk are done (per-chunk counters), and its epilogue
+//            stores each output row into the source rank's return buffer;
+//            each CTA then adds 1 to every rank's returns-arrived counter
+//   combine  waits for every rank's experts CTAs, then
+//            out[t] = bf16(sum_k w[t,k] * ret[t*topk + k]) in fp32, slot order
+//
+// Waits on other CTAs or other GPUs are bounded (2 s of %globaltimer); one
+// that runs out records BS_ERR_DEVICE_TIMEOUT and the kernel winds down.
+// No kernel waits on another kernel of the same GPU: the grid barrier and
+// the chunk dependencies are between CTAs of one cooperative launch (all
+// resident), and the counters are written by kernels of other GPUs or by
+// earlier kernels of the same stream.
+//
+// Counters are monotonic: the front kernel of call number ep (a per-rank
+// epoch kept in device memory, the same on every rank) waits for values
+// ep * (CTAs per rank) * ranks, so nothing is reset between calls.  Every
+// rank must run the same CTA counts (the SM count; all ranks are B200s).
+//
+// Per-row arithmetic (quantiser, routing, MMA K order, SwiGLU epilogue,
+// combine order) is the staged path's, so both give the same bits; only the
+// order of rows inside an expert can differ, which no row's result depends
+// on.
+#include "common.cuh"
+
+namespace mf {
+
+constexpr int kMaxRanks = 8;
+constexpr int kFrontThreads = 256;
+constexpr unsigned long long kWaitNs = 2000000000ull;   // 2 s
+
+// per-rank sync words (uint64)
+enum : int { kEpoch = 0, kGridArrive = 1, kRowsIn = 2, kRetIn = 3, kCntFlag = 8 };
+constexpr int kSyncWords = kCntFlag + kMaxRanks;
+
+// Buffers peers write, as mapped into this process; index = rank.
+struct Peers {
+  int* cnt_all[kMaxRanks];                // [n][E] int32 count matrix (row s: rank s's histogram)
+  uint8_t* rows[kMaxRanks];               // [cap][H] e4m3 expert-major receive rows
+  uint8_t* rows_sp[kMaxRanks];            // [chunk_cap][H/128][512] their packed scales
+  int* ret[kMaxRanks];                    // [cap] return addresses
+  __nv_bfloat16* y_back[kMaxRanks];       // [T_max*topk][H] expert outputs returned to rank q
+  unsigned long long* sync[kMaxRanks];    // [kSyncWords]
+};
+
+BS_DEVINL unsigned long long gtimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+BS_DEVINL unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+BS_DEVINL int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+BS_DEVINL void red_release_sys_add(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+BS_DEVINL void red_release_gpu_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+BS_DEVINL void st_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// generic-proxy writes and async-proxy (TMA / bulk copy) reads of global memory
+BS_DEVINL void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+// Bounded wait until *p >= target (acquire, system scope).
+BS_DEVINL bool wait_geq(const unsigned long long* p, unsigned long long target) {
+  if (ld_acquire_sys(p) >= target) return true;
+  const unsigned long long t0 = gtimer_ns();
+  for (;;) {
+    if (ld_acquire_sys(p) >= target) return true;
+    if (gtimer_ns() - t0 > kWaitNs) break;
+    __nanosleep(32);
+  }
+  bs_set_error(BS_ERR_DEVICE_TIMEOUT);
+  return false;
+}
+
+// Exclusive prefix sums of a[0..n) and b[0..n) in shared memory, in place,
+// with the totals in a[n], b[n].  All threads of the block call it.
+template <int kThreads>
+BS_DEVINL void block_scan2(int* a, int* b, int n) {
+  __shared__ int wa[kThreads / 32], wb[kThreads / 32];
+  const int per = (n + kThreads - 1) / kThreads;
+  const int i0 = threadIdx.x * per;
+  int sa = 0, sb = 0;
+  for (int i = i0; i < i0 + per && i < n; ++i) { sa += a[i]; sb += b[i]; }
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  int ia = sa, ib = sb;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int x = __shfl_up_sync(0xffffffffu, ia, o);
+    const int y = __shfl_up_sync(0xffffffffu, ib, o);
+    if (lane >= o) { ia += x; ib += y; }
+  }
+  if (lane == 31) { wa[wid] = ia; wb[wid] = ib; }
+  __syncthreads();
+  if (wid == 0) {
+    int xa = lane < kThreads / 32 ? wa[lane] : 0, xb = lane < kThreads / 32 ? wb[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int x = __shfl_up_sync(0xffffffffu, xa, o);
+      const int y = __shfl_up_sync(0xffffffffu, xb, o);
+      if (lane >= o) { xa += x; xb += y; }
+    }
+    if (lane < kThreads / 32) { wa[lane] = xa; wb[lane] = xb; }
+  }
+  __syncthreads();
+  int ra = (wid ? wa[wid - 1] : 0) + ia - sa, rb = (wid ? wb[wid - 1] : 0) + ib - sb;
+  for (int i = i0; i < i0 + per && i < n; ++i) {
+    const int va = a[i], vb = b[i];
+    a[i] = ra;
+    b[i] = rb;
+    ra += va;
+    rb += vb;
+  }
+  if (threadIdx.x == kThreads - 1) { a[n] = wa[kThreads / 32 - 1]; b[n] = wb[kThreads / 32 - 1]; }
+  __syncthreads();
+}
+
+struct FrontArgs {
+  const __nv_bfloat16* x;     // [T, H] this rank's tokens
+  const float* logits;        // [T, E]
+  int T, H, E, topk, El, n, me;
+  int64_t cap;                // receive rows per rank
+  int64_t chunk_cap;          // receive scale chunks per rank
+  uint8_t* xq;                // [T, H] e4m3
+  uint8_t* xs;                // [T, H/128] ue8m0
+  int* idx;                   // [T, topk]
+  float* w;                   // [T, topk]
+  int* counts;                // [2][E] (parity of the epoch), zero before first use
+  int* cursor;                // [2][E]
+  int* offsets;               // [El + 1] this rank's experts (owner side)
+  int* chunk_prefix;          // [El + 1]
+  int* h_done;                // [chunk_cap] zeroed here for the experts kernel
+};
+
+// Dynamic shared memory: 3 * E + 2 ints (plan).
+template <int kMaxPer>
+__global__ void __launch_bounds__(kFrontThreads) front_kernel(FrontArgs a, Peers pr) {
+  extern __shared__ int sh[];
+  __shared__ unsigned long long s_ep;
+  __shared__ int s_ok;
+  const int lane = threadIdx.x & 31;
+  constexpr int kWarps = kFrontThreads / 32;
+  const int64_t gwarp = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  const int64_t nwarps = (int64_t)gridDim.x * kWarps;
+  const int64_t gtid = (int64_t)blockIdx.x * kFrontThreads + threadIdx.x;
+  const int64_t nthreads = (int64_t)gridDim.x * kFrontThreads;
+  unsigned long long* my_sync = pr.sync[a.me];
+  if (threadIdx.x == 0) {
+    s_ep = *reinterpret_cast<volatile unsigned long long*>(my_sync + kEpoch) + 1;
+    s_ok = 1;
+  }
+  __syncthreads();
+  const unsigned long long ep = s_ep;
+  const int par = (int)(ep & 1);
+  int* counts = a.counts + par * a.E;
+  int* cursor = a.cursor + par * a.E;
+  const int H = a.H, nb = H / 128;
+
+  // ---- A: next call's counters, this call's chunk counters
+  for (int64_t i = gtid; i < a.E; i += nthreads) {
+    a.counts[(par ^ 1) * a.E + i] = 0;
+    a.cursor[(par ^ 1) * a.E + i] = 0;
+  }
+  for (int64_t i = gtid; i < a.chunk_cap; i += nthreads) a.h_done[i] = 0;
+
+  // ---- A: quantise (half a warp per 1x128 block, power-of-two scales)
+  {
+    const int half = lane >> 4, l16 = lane & 15;
+    const int64_t n_groups = (int64_t)a.T * nb;
+    for (int64_t base = gwarp * 2; base < n_groups; base += nwarps * 2) {
+      const int64_t g = base + half;
+      const bool valid = g < n_groups;
+      const uint4 raw = valid ? __ldg(reinterpret_cast<const uint4*>(a.x + g * 128) + l16) : make_uint4(0, 0, 0, 0);
+      const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
+      const uint32_t m2 = max_u16x2(max_u16x2(wv[0] & 0x7FFF7FFFu, wv[1] & 0x7FFF7FFFu),
+                                    max_u16x2(wv[2] & 0x7FFF7FFFu, wv[3] & 0x7FFF7FFFu));
+      uint32_t mb = max(m2 << 16, m2 & 0xFFFF0000u);
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+      float amax = __uint_as_float(mb);
+      amax = amax < 1e-4f ? 1e-4f : amax;
+      const float scale = bs_round_pow2(__fdiv_rn(amax, 448.0f));
+      if (valid) {
+        float f[8], q[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          f[2 * i] = __uint_as_float(wv[i] << 16);
+          f[2 * i + 1] = __uint_as_float(wv[i] & 0xFFFF0000u);
+        }
+        if ((__float_as_uint(scale) & 0x7F800000u) != 0x7F800000u) {
+          const float r = bs_inv_pow2(scale);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) q[i] = __fmul_rn(f[i], r);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) q[i] = __fdiv_rn(f[i], scale);
+        }
+        uint2 c;
+        c.x = bs_cvt_e4m3x2(q[0], q[1]) | ((uint32_t)bs_cvt_e4m3x2(q[2], q[3]) << 16);
+        c.y = bs_cvt_e4m3x2(q[4], q[5]) | ((uint32_t)bs_cvt_e4m3x2(q[6], q[7]) << 16);
+        *reinterpret_cast<uint2*>(a.xq + g * 128 + l16 * 8) = c;
+        if (l16 == 0) a.xs[g] = bs_f32_to_e8m0(scale);
+      }
+    }
+  }
+
+  // ---- A: routing (one warp per token)
+  for (int64_t t = gwarp; t < a.T; t += nwarps) {
+    float sel_v[8];
+    int sel_e[8];
+    moe::route_one<kMaxPer>(a.logits + t * a.E, a.E, a.topk, lane, sel_v, sel_e);
+    if (lane == 0) {
+      for (int k = 0; k < a.topk; ++k) {
+        a.idx[t * a.topk + k] = sel_e[k];
+        a.w[t * a.topk + k] = moe::route_weight(sel_v, a.topk, k);
+        atomicAdd(&counts[sel_e[k]], 1);
+      }
+    }
+  }
+
+  // ---- grid barrier
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    atomicAdd(my_sync + kGridArrive, 1ull);
+    if (!wait_geq(my_sync + kGridArrive, ep * gridDim.x)) s_ok = 0;
+  }
+  __syncthreads();
+  if (!s_ok) return;
+  if (blockIdx.x == 0 && threadIdx.x == 0) my_sync[kEpoch] = ep;   // read again only by later kernels
+
+  // ---- B: histogram to every rank, flag, wait for every rank's flag
+  const int E = a.E, El = a.El, n = a.n, me = a.me;
+  if ((int)blockIdx.x < n) {
+    const int q = blockIdx.x;
+    int* dst = pr.cnt_all[q] + (int64_t)me * E;
+    for (int e = threadIdx.x; e < E; e += kFrontThreads) dst[e] = __ldcg(counts + e);
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) st_release_sys(pr.sync[q] + kCntFlag + me, ep);
+  }
+  if (threadIdx.x < n && !wait_geq(my_sync + kCntFlag + threadIdx.x, ep)) s_ok = 0;
+  __syncthreads();
+  if (!s_ok) return;
+
+  // ---- B: plan.  P[e]: rows of experts before e (all ranks); Cc[e]: chunks
+  // of experts before e; Bf[e]: rows of expert e from ranks below me.
+  int* P = sh;
+  int* Cc = sh + E + 1;
+  int* Bf = sh + 2 * E + 2;
+  const int* cnt_mine = pr.cnt_all[me];
+  for (int e = threadIdx.x; e < E; e += kFrontThreads) {
+    int tot = 0, before = 0;
+    for (int s = 0; s < n; ++s) {
+      const int c = __ldcg(cnt_mine + (int64_t)s * E + e);
+      tot += c;
+      if (s < me) before += c;
+    }
+    P[e] = tot;
+    Cc[e] = (tot + moe::kTok - 1) / moe::kTok;
+    Bf[e] = before;
+  }
+  __syncthreads();
+  block_scan2<kFrontThreads>(P, Cc, E);
+  if (blockIdx.x == 0) {
+    const int e0 = me * El;
+    for (int l = threadIdx.x; l <= El; l += kFrontThreads) {
+      a.offsets[l] = P[e0 + l] - P[e0];
+      a.chunk_prefix[l] = Cc[e0 + l] - Cc[e0];
+    }
+  }
+
+  // ---- C: rows, scale words and return addresses into the owners' buffers
+  const int64_t pairs = (int64_t)a.T * a.topk;
+  for (int64_t j = gwarp; j < pairs; j += nwarps) {
+    const int64_t t = j / a.topk;
+    const int e = __ldcg(a.idx + j);
+    const int d = e / El;
+    int slot = 0;
+    if (lane == 0) slot = atomicAdd(&cursor[e], 1);
+    slot = __shfl_sync(0xffffffffu, slot, 0);
+    const int cin = Bf[e] + slot;                                // row inside expert e at its owner
+    const int64_t pos = (int64_t)(P[e] - P[d * El]) + cin;        // row in the owner's receive buffer
+    const int64_t cg = (int64_t)(Cc[e] - Cc[d * El]) + cin / moe::kTok;
+    const int r = cin % moe::kTok;
+    if (pos >= a.cap || cg >= a.chunk_cap) {                     // only if ranks disagree on sizes
+      if (lane == 0) bs_set_error(BS_ERR_DEVICE_FAULT);
+      continue;
+    }
+    const uint4* src = reinterpret_cast<const uint4*>(a.xq + t * H);
+    uint4* dst = reinterpret_cast<uint4*>(pr.rows[d] + pos * H);
+#pragma unroll 4
+    for (int i = lane; i < H / 16; i += 32) dst[i] = __ldcg(src + i);
+    uint8_t* sp = pr.rows_sp[d];
+    for (int i = lane; i < nb; i += 32)
+      *reinterpret_cast<uint32_t*>(sp + (cg * nb + i) * 512 + moe::sf_word_off(r)) =
+          0x01010101u * __ldcg(a.xs + t * nb + i);
+    if (lane == 0) pr.ret[d][pos] = (me << 24) | (int)j;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < n) red_release_sys_add(pr.sync[threadIdx.x] + kRowsIn, 1ull);
+}
+
+struct ExpArgs {
+  int E, H, I, n, me;
+  int64_t cap;
+  const int* offsets;         // [E+1] token-row offsets of this rank's experts
+  const int* chunk_prefix;    // [E+1]
+  const uint8_t* a_sp;        // this rank's received packed scales
+  const int* ret;             // this rank's received return addresses
+  const uint8_t* w13_sp;      // [E][2I/128][H/128][512]
+  const uint8_t* w2_sp;       // [E][H/128][I/128][512]
+  uint8_t* hq;                // [cap, I] e4m3 hidden rows
+  uint8_t* hs_p;              // [chunk][I/128][512]
+  int* h_done;                // [chunk] W1|W3 tile parts stored per token chunk (kEpiWarps per tile)
+  unsigned long long rows_per_epoch;   // n * front CTAs
+};
+
+using C = moe::Cfg<moe::kModeW13>;   // W2 pair items use the same stage and TMEM layout
+static_assert(moe::Cfg<moe::kModeW13>::kStageBytes == moe::Cfg<moe::kModeW2Pair>::kStageBytes, "stage layouts");
+static_assert(moe::Cfg<moe::kModeW13>::kAccCols == moe::Cfg<moe::kModeW2Pair>::kAccCols, "accumulator layouts");
+
+__global__ void __launch_bounds__(C::kThreads, 1)
+    experts_kernel(const __grid_constant__ CUtensorMap tm_w13, const __grid_constant__ CUtensorMap tm_a,
+                   const __grid_constant__ CUtensorMap tm_w2, const __grid_constant__ CUtensorMap tm_h, ExpArgs p,
+                   Peers pr) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint8_t* stage_base = smem;
+  uint8_t* sf_base = smem + C::kStages * C::kStageBytes;
+  int* s_off = reinterpret_cast<int*>(sf_base + C::kStages * C::kSfBytes);
+  int* s_chunk = s_off + C::kMaxE + 1;
+  uint32_t* s_red = reinterpret_cast<uint32_t*>(s_chunk + C::kMaxE + 1);
+  uint64_t* full = reinterpret_cast<uint64_t*>(s_red + 2 * 80);
+  uint64_t* empty = full + C::kStages;
+  uint64_t* acc_full = empty + C::kStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int E = p.E;
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) {
+    s_off[i] = p.offsets[i];
+    s_chunk[i] = p.chunk_prefix[i];
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], C::kEpiWarps);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_w13);
+    tma_prefetch_desc(&tm_a);
+    tma_prefetch_desc(&tm_w2);
+    tma_prefetch_desc(&tm_h);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int nt13 = p.I / 128, nt2 = p.H / 256;
+  const int n13 = s_chunk[E] * nt13;
+  const int n_items = n13 + s_chunk[E] * nt2;
+  unsigned long long* my_sync = pr.sync[p.me];
+
+  // item -> (W2?, expert, first row, rows, output tile, global chunk).  Inside
+  // an expert, items run tile-major: consecutive items stream the same weight
+  // tile(s) for the expert's successive token chunks.
+  auto decode = [&](int item, bool& w2, int& e, int& row0, int& cnt, int& nt, int& cg) {
+    w2 = item >= n13;
+    const int li = w2 ? item - n13 : item;
+    const int ntiles = w2 ? nt2 : nt13;
+    int lo = 0, hi = E;  // largest e with s_chunk[e] * ntiles <= li
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (s_chunk[mid] * ntiles <= li) lo = mid; else hi = mid;
+    }
+    e = lo;
+    const int ch = s_chunk[e + 1] - s_chunk[e];
+    const int local = li - s_chunk[e] * ntiles;
+    nt = local / ch;
+    const int c = local - nt * ch;
+    cg = s_chunk[e] + c;
+    row0 = s_off[e] + c * moe::kTok;
+    const int left = s_off[e + 1] - row0;
+    cnt = left < moe::kTok ? left : moe::kTok;
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    bool ok = true;
+    if (lane == 0) {
+      const unsigned long long ep = *reinterpret_cast<volatile unsigned long long*>(my_sync + kEpoch);
+      ok = wait_geq(my_sync + kRowsIn, ep * p.rows_per_epoch);   // every rank's rows are here
+      fence_proxy_async_global();
+    }
+    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+    if (!ok) *abort_flag = 1;
+    int it = 0;
+    const int w13_tiles = 2 * p.I / 128, w2_tiles = p.H / 128;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+      bool w2;
+      int e, row0, cnt, nt, cg;
+      decode(item, w2, e, row0, cnt, nt, cg);
+      const int nbox = (cnt + 31) / 32;
+      const int nkb = (w2 ? p.I : p.H) / 128;
+      if (w2) {
+        // the hidden rows of this chunk: every W1|W3 tile of it has been stored
+        int done = 1;
+        if (lane == 0) {
+          done = 0;
+          const int need = nt13 * C::kEpiWarps;
+          if (ld_acquire_gpu(p.h_done + cg) >= need) done = 1;
+          const unsigned long long t0 = gtimer_ns();
+          while (!done && !*abort_flag) {
+            if (ld_acquire_gpu(p.h_done + cg) >= need) done = 1;
+            else if (gtimer_ns() - t0 > kWaitNs) break;
+            else __nanosleep(64);
+          }
+          if (!done && !*abort_flag) bs_set_error(BS_ERR_DEVICE_TIMEOUT);
+          fence_proxy_async_global();
+        }
+        if (!__shfl_sync(0xffffffffu, done, 0)) { *abort_flag = 1; ok = false; break; }
+      }
+      const CUtensorMap* mw = w2 ? &tm_w2 : &tm_w13;
+      const CUtensorMap* ma = w2 ? &tm_h : &tm_a;
+      const uint8_t* wsp = w2 ? p.w2_sp : p.w13_sp;
+      const uint8_t* asp = w2 ? p.hs_p : p.a_sp;
+      const int wt = w2 ? w2_tiles : w13_tiles;
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const int s = it % C::kStages;
+        const uint32_t ph = (it / C::kStages) & 1;
+        if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1, abort_flag))) { ok = false; break; }
+        if (elect_one()) {
+          uint8_t* sx = stage_base + s * C::kStageBytes;
+          uint8_t* sy = sx + C::kXBytes;
+          uint8_t* sf = sf_base + s * C::kSfBytes;
+          mbar_arrive_expect_tx(&full[s], 2 * (8192 + 512) + nbox * 32 * 128 + 512);
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const int wr0 = w2 ? nt * 256 + t * 128 : t * p.I + nt * 128;
+            tma_load_3d(sx + t * 16384, mw, &full[s], kb * 128, wr0, e);
+            bulk_load(sf + t * 512, wsp + (((int64_t)e * wt + wr0 / 128) * nkb + kb) * 512, 512, &full[s]);
+          }
+          for (int b = 0; b < nbox; ++b) tma_load_2d(sy + b * 32 * 128, ma, &full[s], kb * 128, row0 + b * 32);
+          bulk_load(sf + 2 * 512, asp + ((int64_t)cg * nkb + kb) * 512, 512, &full[s]);
+        }
+        __syncwarp();
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    const uint64_t dx0 = sdesc_k128_sw128(smem_u32(stage_base));
+    const uint64_t dsf0 = sdesc_sf_chunk(smem_u32(sf_base));
+    constexpr uint64_t kStageStep = (uint64_t)(C::kStageBytes >> 4);
+    constexpr uint64_t kSfStep = (uint64_t)(C::kSfBytes >> 4);
+    constexpr uint64_t kYOff = (uint64_t)(C::kXBytes >> 4);
+    const uint32_t sf_tmem0 = tmem_base + C::kSfCol0;
+    int it = 0, acc_it = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++acc_it) {
+      bool w2;
+      int e, row0, cnt, nt, cg;
+      decode(item, w2, e, row0, cnt, nt, cg);
+      const int nkb = (w2 ? p.I : p.H) / 128;
+      const int n_mma = (cnt + 15) / 16 * 16;
+      const uint32_t idesc0 = idesc_mxf8f6f4(5, 0, 128, n_mma, 0, 0);
+      const int buf = acc_it % C::kAccBufs;
+      const uint32_t aph = (acc_it / C::kAccBufs) & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&acc_empty[buf], aph ^ 1, abort_flag))) break;
+      tc_fence_after();
+      const uint32_t d0 = tmem_base + buf * C::kAccCols;
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const int s = it % C::kStages;
+        const uint32_t ph = (it / C::kStages) & 1;
+        if (!__all_sync(0xffffffffu, mbar_wait(&full[s], ph, abort_flag))) { ok = false; break; }
+        tc_fence_after();
+        if (elect_one()) {
+          const uint64_t dx = dx0 + (uint64_t)s * kStageStep;
+          const uint64_t dy = dx + kYOff;
+          const uint64_t dsf = dsf0 + (uint64_t)s * kSfStep;
+          const uint32_t slot = sf_tmem0 + (it & 1) * C::kSfSlot;
+#pragma unroll
+          for (int t = 0; t <= 2; ++t) tc_cp_32x128b_warpx4(slot + 4 * t, dsf + (uint64_t)(32 * t));
+          const uint32_t sfb = slot + 4 * 2;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t idesc = idesc0 | ((uint32_t)k << 4) | ((uint32_t)k << 29);
+            const uint32_t kid = (uint32_t)k << 30;
+            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+#pragma unroll
+            for (int t = 0; t < 2; ++t)
+              tc_mma_mxf8f6f4(d0 + t * moe::kTok, dx + (uint64_t)(t * 1024 + 2 * k), dy + (uint64_t)(2 * k), idesc,
+                              (slot + 4 * t) | kid, sfb | kid, acc);
+          }
+          tc_commit(&empty[s]);
+        }
+        __syncwarp();
+      }
+      if (!ok) break;
+      if (elect_one()) tc_commit(&acc_full[buf]);
+      __syncwarp();
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    // Two sets of four warps take alternate 16-token groups of an item.
+    const int quad = warp & 3;
+    const int set = (warp - 2) >> 2;
+    const int f = quad * 32 + lane;
+    int acc_it = 0;
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++acc_it) {
+      bool w2;
+      int e, row0, cnt, nt, cg;
+      decode(item, w2, e, row0, cnt, nt, cg);
+      const int buf = acc_it % C::kAccBufs;
+      const uint32_t aph = (acc_it / C::kAccBufs) & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[buf], aph, abort_flag))) break;
+      tc_fence_after();
+      const uint32_t tl = tmem_base + ((uint32_t)(quad * 32) << 16) + buf * C::kAccCols;
+      for (int c0 = set * 16; c0 < cnt; c0 += 32) {
+        uint32_t g[16], u[16];
+        BS_TMEM_LD16(tl + c0, g);
+        BS_TMEM_LD16(tl + moe::kTok + c0, u);
+        tmem_ld_wait();
+        if (!w2) {
+          uint32_t* red = s_red + set * 80;
+          float z[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            z[j] = moe::silu(moe::bf16_round(__uint_as_float(g[j]))) * moe::bf16_round(__uint_as_float(u[j]));
+            const uint32_t m = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(z[j])));
+            if (lane == 0) red[quad * 16 + j] = m;
+          }
+          moe::named_bar_epi(set);
+          if (quad == 0 && lane < 16) {
+            const uint32_t m = max(max(red[lane], red[16 + lane]), max(red[32 + lane], red[48 + lane]));
+            float amax = __uint_as_float(m);
+            amax = amax < 1e-4f ? 1e-4f : amax;
+            const float scale = bs_round_pow2(__fdiv_rn(amax, 448.0f));
+            red[64 + lane] = __float_as_uint(scale);
+            const int r = c0 + lane;
+            if (r < cnt)
+              *reinterpret_cast<uint32_t*>(p.hs_p + ((int64_t)cg * nt13 + nt) * 512 + moe::sf_word_off(r)) =
+                  0x01010101u * bs_f32_to_e8m0(scale);
+          }
+          moe::named_bar_epi(set);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int tok = c0 + j;
+            if (tok < cnt) {
+              const float q = bs_clamp(z[j] * bs_inv_pow2(__uint_as_float(red[64 + j])), -448.0f, 448.0f);
+              p.hq[(int64_t)(row0 + tok) * p.I + nt * 128 + f] = (uint8_t)(bs_cvt_e4m3x2(q, 0.0f) & 0xFF);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int tok = c0 + j;
+            if (tok < cnt) {
+              const int rr = __ldcg(p.ret + row0 + tok);
+              __nv_bfloat16* yrow = pr.y_back[rr >> 24] + (int64_t)(rr & 0xFFFFFF) * p.H + nt * 256;
+              yrow[f] = __float2bfloat16_rn(__uint_as_float(g[j]));
+              yrow[128 + f] = __float2bfloat16_rn(__uint_as_float(u[j]));
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      if (!w2) {
+        // this warp's part of the W1|W3 tile of chunk cg is stored: count it
+        // for the W2 items (kEpiWarps counts per tile)
+        __threadfence();
+        fence_proxy_async_global();
+        __syncwarp();
+        if (lane == 0) red_release_gpu_add(p.h_done + cg, 1);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __threadfence_system();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+  // this CTA's output rows are at their source ranks
+  if (threadIdx.x < p.n) red_release_sys_add(pr.sync[threadIdx.x] + kRetIn, 1ull);
+}
+
+// out[t] = bf16(sum_k w[t,k] * y_back[t*topk + k]), fp32 in slot order; waits
+// until every rank's experts CTAs have returned their rows.
+__global__ void combine_kernel(const __nv_bfloat16* __restrict__ y, const float* __restrict__ w, int topk, int H,
+                               __nv_bfloat16* __restrict__ out, unsigned long long* my_sync,
+                               unsigned long long ret_per_epoch) {
+  constexpr int kMaxTopk = 8;
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) {
+    const unsigned long long ep = *reinterpret_cast<volatile unsigned long long*>(my_sync + kEpoch);
+    s_ok = wait_geq(my_sync + kRetIn, ep * ret_per_epoch) ? 1 : 0;
+  }
+  __syncthreads();
+  if (!s_ok) return;
+  const int t = blockIdx.x;
+  float wk[kMaxTopk];
+#pragma unroll
+  for (int k = 0; k < kMaxTopk; ++k) wk[k] = k < topk ? w[(int64_t)t * topk + k] : 0.0f;
+  for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
+    uint4 raw[kMaxTopk];
+#pragma unroll
+    for (int k = 0; k < kMaxTopk; ++k)
+      if (k < topk) raw[k] = __ldcg(reinterpret_cast<const uint4*>(y + ((int64_t)t * topk + k) * H + c));
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+    for (int k = 0; k < kMaxTopk; ++k) {
+      if (k >= topk) break;
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[k]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 fv = __bfloat1622float2(h[j]);
+        acc[2 * j] = fmaf(wk[k], fv.x, acc[2 * j]);
+        acc[2 * j + 1] = fmaf(wk[k], fv.y, acc[2 * j + 1]);
+      }
+    }
+    uint4 o;
+    __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) oh[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
+    *reinterpret_cast<uint4*>(out + (int64_t)t * H + c) = o;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+
+int sm_count() {
+  static int slots[hostcache::kMaxDevices];
+  return hostcache::device_attr(slots, cudaDevAttrMultiProcessorCount);
+}
+
+// Events recorded around the experts kernel of the next fused layer call
+// on this host thread (a profiling hook; both null = off).
+thread_local cudaEvent_t t_ev_begin = nullptr, t_ev_end = nullptr;
+
+template <class K, class... Args>
+cudaError_t launch_coop(K kern, int grid, int threads, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+struct Layer {
+  FrontArgs f;
+  ExpArgs x;
+  Peers pr;
+  const void* w13;
+  const void* w2;
+  __nv_bfloat16* out;
+  const float* wts;
+};
+
+cudaError_t run_layer(const Layer& L, cudaStream_t st, int* status) {
+  *status = 0;
+  const int G = sm_count();
+  const int E = L.f.E, El = L.f.El;
+  // front
+  const size_t fsm = (size_t)(3 * E + 2) * sizeof(int);
+  const int per = (E + 31) / 32;
+  cudaError_t e;
+  if (per <= 1) e = launch_coop(front_kernel<1>, G, kFrontThreads, fsm, st, L.f, L.pr);
+  else if (per <= 2) e = launch_coop(front_kernel<2>, G, kFrontThreads, fsm, st, L.f, L.pr);
+  else if (per <= 4) e = launch_coop(front_kernel<4>, G, kFrontThreads, fsm, st, L.f, L.pr);
+  else if (per <= 8) e = launch_coop(front_kernel<8>, G, kFrontThreads, fsm, st, L.f, L.pr);
+  else if (per <= 16) e = launch_coop(front_kernel<16>, G, kFrontThreads, fsm, st, L.f, L.pr);
+  else e = launch_coop(front_kernel<32>, G, kFrontThreads, fsm, st, L.f, L.pr);
+  if (e != cudaSuccess) return e;
+  // experts
+  CUtensorMap mw13, ma, mw2, mh;
+  const int64_t cap = L.x.cap;
+  if (!moe::make_weight_map(&mw13, L.w13, El, 2 * L.x.I, L.x.H) ||
+      !moe::make_act_map(&ma, L.pr.rows[L.f.me], cap, L.x.H) || !moe::make_weight_map(&mw2, L.w2, El, L.x.H, L.x.I) ||
+      !moe::make_act_map(&mh, L.x.hq, cap, L.x.I)) {
+    *status = BS_ERR_UNSUPPORTED;
+    return cudaSuccess;
+  }
+  static int attr_slots[hostcache::kMaxDevices];
+  e = (cudaError_t)hostcache::get(attr_slots, [&] {
+    return (int)cudaFuncSetAttribute(experts_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  });
+  if (e != cudaSuccess) return e;
+  ExpArgs xa = L.x;
+  xa.rows_per_epoch = (unsigned long long)L.f.n * G;
+  if (t_ev_begin) cudaEventRecord(t_ev_begin, st);
+  e = launch_coop(experts_kernel, G, C::kThreads, (size_t)C::kSmemBytes, st, mw13, ma, mw2, mh, xa, L.pr);
+  if (t_ev_end) cudaEventRecord(t_ev_end, st);
+  t_ev_begin = t_ev_end = nullptr;
+  if (e != cudaSuccess) return e;
+  // combine
+  if (L.f.T > 0) {
+    int threads = L.x.H / 8;
+    if (threads > 512) threads = 512;
+    combine_kernel<<<L.f.T, threads, 0, st>>>(L.pr.y_back[L.f.me], L.wts, L.f.topk, L.x.H, L.out,
+                                               L.pr.sync[L.f.me], (unsigned long long)L.f.n * G);
+    e = cudaGetLastError();
+  }
+  return e;
+}
+
+}  // namespace mf

@@ -171,10 +171,28 @@ size_t bs_moe_workspace_size(int64_t T, int H, int I, int E, int topk);
 
 /* Whole layer on one GPU: x bf16 [T,H], gate logits fp32 [T,E] -> out bf16
  * [T,H].  Routing: top-k logits, weights = softmax over the k selected.
- * w13_sp / w2_sp are the packed scales from bs_moe_pack_scales. */
+ * w13_sp / w2_sp are the packed scales from bs_moe_pack_scales.
+ * With H a multiple of 256 the layer runs as three kernels (front: quantise +
+ * route + expert-sorted dispatch; experts: one persistent launch over the
+ * W1|W3 and W2 grouped GEMMs; combine) after a small memset of the
+ * workspace's counters; otherwise as the staged sequence below.  Both give
+ * the same bits. */
 int bs_moe_forward(const void* x, const float* logits, int64_t T, int H, int I, int E, int topk, const void* w13,
                    const void* w13_sp, const void* w2, const void* w2_sp, void* out, void* workspace,
                    size_t workspace_bytes, void* stream);
+
+/* The staged form of bs_moe_forward (act_quant, route, scan, dispatch, one
+ * grouped GEMM launch each for W1|W3 and W2, combine: the building blocks the
+ * NCCL expert-parallel form uses), with its own workspace size. */
+size_t bs_moe_staged_workspace_size(int64_t T, int H, int I, int E, int topk);
+int bs_moe_forward_staged(const void* x, const float* logits, int64_t T, int H, int I, int E, int topk,
+                          const void* w13, const void* w13_sp, const void* w2, const void* w2_sp, void* out,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+/* Profiling hook: the next three-kernel layer call (bs_moe_forward or
+ * bs_ep_moe_forward) made on this host thread records ev_begin / ev_end
+ * (cudaEvent_t) on its stream around its experts kernel, then forgets them. */
+void bs_moe_time_experts(void* ev_begin, void* ev_end);
 
 /* Building blocks (expert-parallel form; the caller moves rows between
  * ranks).  route: idx/w [T,topk], counts [E] (zeroed, then filled). */
@@ -265,6 +283,37 @@ int bs_ep_experts_return(int E_local, int64_t capacity, int H, int I, const void
                          const int* offsets, const int* chunk_prefix, const void* w13, const void* w13_sp,
                          const void* w2, const void* w2_sp, const int* ret, void* const* y_ranks, int n_ranks,
                          void* hq, void* hs_p, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Expert-parallel layer in three kernels over peer memory (the default
+ * expert-parallel path; no NCCL, no host round trip).  Experts split into
+ * contiguous ranges of E/n_ranks (the reference's loader ranges,
+ * weight_loader.py:112-115); each rank brings its own tokens
+ * (T <= max_tokens, the same max_tokens on every rank) and gets their layer
+ * output back in `out`.
+ *   front    quantise + route this rank's tokens, exchange the per-expert
+ *            counts, write every (token, slot) row, its scales and its
+ *            return address straight into the owning rank's receive buffers
+ *   experts  persistent W1|W3 + W2 grouped GEMMs on the received rows; each
+ *            output row is stored into its source rank's return buffer
+ *   combine  weighted sum of the returned rows
+ * Every rank must call it the same number of times (an epoch counted in the
+ * sync words orders the calls).
+ * bs_ep_moe_sizes fills sizes[7] with bytes of: [0] the workspace (this rank
+ * only; zero it once before the first call and keep it between calls), then
+ * the per-rank buffers peers write, each mapped into every rank (symmetric
+ * memory / CUDA IPC): [1] cnt_all, [2] rows, [3] rows_sp, [4] ret, [5] y_back,
+ * [6] sync (zero before the first call).  peer_bufs holds 6 * n_ranks
+ * pointers, buffer kind k (cnt_all, rows, rows_sp, ret, y_back, sync) of rank
+ * q at [k * n_ranks + q].  Every rank must have the same SM count.  Waits on
+ * peers are bounded (2 s) and report BS_ERR_DEVICE_TIMEOUT through
+ * bs_device_error_check.  No counterpart in the reference.
+ * ------------------------------------------------------------------------ */
+int bs_ep_moe_sizes(int64_t max_tokens, int H, int I, int E, int topk, int n_ranks, int64_t* sizes);
+int bs_ep_moe_forward(const void* x, const float* logits, int64_t T, int64_t max_tokens, int H, int I, int E,
+                      int topk, int rank, int n_ranks, const void* w13, const void* w13_sp, const void* w2,
+                      const void* w2_sp, void* out, void* const* peer_bufs, void* workspace, size_t workspace_bytes,
+                      void* stream);
 
 /* out[t] = bf16(sum_k w[t,k] * y[pos_of[t,k]]) */
 int bs_moe_combine(const void* y, const int* pos_of, const float* w, int64_t T, int topk, int H, void* out,

@@ -17,7 +17,7 @@ HEADER = os.path.join(ROOT, "include", "bsgemm.h")
 
 def declared_symbols():
     src = open(HEADER).read()
-    return sorted(set(re.findall(r"^\s*(?:int|int64_t|size_t|const char\*)\s+(bs_\w+)\s*\(", src, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|int64_t|size_t|void|const char\*)\s+(bs_\w+)\s*\(", src, re.M)))
 
 
 @pytest.fixture(scope="module")

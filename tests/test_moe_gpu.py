@@ -56,6 +56,50 @@ def test_moe_vs_oracle(T, H, inter, E, topk):
     check(bits(run(m, topk)), ref, f"moe T={T} H={H} I={inter} E={E} k={topk}")
 
 
+def _staged(x, logits, W, topk):
+    """The staged form (act_quant, route, scan, dispatch, two grouped GEMM
+    launches, combine) through its own C entry point."""
+    L = importlib.import_module(PKG_NAME + "._lib")
+    lib = L.load()
+    T, H = x.shape
+    ws = torch.empty(lib.bs_moe_staged_workspace_size(T, H, W.I, W.E, topk), dtype=torch.uint8, device=x.device)
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=x.device)
+    L.check(lib.bs_moe_forward_staged(x.data_ptr(), logits.data_ptr(), T, H, W.I, W.E, topk, W.w13.data_ptr(),
+                                      W.w13_sp.data_ptr(), W.w2.data_ptr(), W.w2_sp.data_ptr(), out.data_ptr(),
+                                      ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream))
+    return out
+
+
+@pytest.mark.parametrize("T,H,inter,E,topk,skew", [(64, 512, 256, 16, 4, False), (1, 256, 128, 8, 2, False),
+                                                   (700, 1024, 512, 64, 8, True), (333, 4096, 2048, 256, 8, False),
+                                                   (2048, 4096, 2048, 32, 8, True)])
+def test_three_kernel_layer_equals_staged(T, H, inter, E, topk, skew):
+    """The three-kernel layer (front / persistent W1|W3 + W2 / combine) gives
+    the staged sequence's bits, including experts with several token chunks
+    (skewed routing) and a single token; two calls in a row agree."""
+    mm = moe_mod()
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev)
+    g.manual_seed(T * 7 + E)
+    x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    logits = torch.randn(T, E, generator=g, device=dev)
+    if skew:
+        logits[:, : E // 8] += 3.0
+    w13 = torch.randint(0, 256, (E, 2 * inter, H // 2), generator=g, device=dev, dtype=torch.uint8)
+    w13_s = 127 - torch.randint(0, 7, (E, 2 * inter, H // 32), generator=g, device=dev, dtype=torch.uint8)
+    w2 = torch.randint(0, 256, (E, H, inter // 2), generator=g, device=dev, dtype=torch.uint8)
+    w2_s = 127 - torch.randint(0, 7, (E, H, inter // 32), generator=g, device=dev, dtype=torch.uint8)
+    W = mm.MoEWeights(w13, w13_s, w2, w2_s)
+    ref = _staged(x, logits, W, topk)
+    a = mm.moe_forward(x, logits, W, topk)
+    b = mm.moe_forward(x, logits, W, topk)
+    torch.cuda.synchronize()
+    importlib.import_module(PKG_NAME)._lib.device_error_check()
+    assert torch.isfinite(ref.float()).all()
+    assert torch.equal(a, ref)
+    assert torch.equal(b, ref)
+
+
 def test_moe_routing_matches_oracle():
     """The device top-k picks the same experts as the oracle (stable ties)."""
     L = importlib.import_module(PKG_NAME + "._lib")

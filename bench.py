@@ -2,20 +2,22 @@
 """Benchmark of the block-scaled GEMM path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload fp8_prefill|fp4_decode|moe|moe_stack|act_quant|fp4_act_quant]
+                    [--workload moe|fp8_prefill|fp4_decode|moe_stack|act_quant|fp4_act_quant]
 
-Default workload (one "step"): the dense prefill fp8_gemm, M=N=K=4096, A
-quantised per 1x128 (fp32 scales), W e4m3 with fp32 128x128 block scales,
-bf16 output.  At N>1 GPUs the weight is column-sharded (tensor parallel):
-each rank computes C[:, N/g slice] and an NCCL all-gather (plus the column
-interleave) rebuilds C on every rank; total work is fixed (strong scaling).
+Default workload (one "step"): the grouped FP8 x FP4 MoE layer -- 1024 tokens,
+hidden 4096, inter 2048, 256 experts, top-8 -- through the library's
+three-kernel layer; at N>1 GPUs expert parallel (each rank its own tokens and
+E/N experts, rows exchanged over NVLink peer memory inside the layer's
+kernels), total batch fixed (strong scaling).  The same line carries the
+4096^3 prefill fp8_gemm / fp4_gemm rates (one GPU).
 
 Rank 0 prints one JSON line.  ``value`` is device-timed (CUDA events on the
-launching stream, max over ranks) with inputs resident in HBM; input sets
-rotate so that no step finds its operands in L2.  ``e2e`` times the public
-API (act_quant + fp8_gemm) from pinned host activations to a host copy of the
-result.  ``--impl reference`` times the reference algorithm's CPU port
-(oracle/) on the host cores instead.
+launching stream, max over ranks) with inputs resident in HBM; every step
+streams all expert weights (GiBs, far above L2).  ``roofline`` is the
+dominant kernel's algorithmic bytes over its event-timed duration.  ``e2e``
+times the public API from pinned host tokens and logits to a pinned host
+copy of the output.  ``--impl reference`` times the reference's CPU
+arithmetic (a torch restatement, oracle/torch_cpu.py) on the host cores.
 """
 
 from __future__ import annotations
@@ -34,14 +36,14 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 PKG = "deepseek-v4-experimental-platform-on-dgx-spark_b200"
 
-# DRAM bytes (read + write) per launch of the dominant kernel, from one ncu
-# capture of the same workload (dram__bytes_read.sum + dram__bytes_write.sum;
-# the summaries and commands are in profiles/).  Output writes that are still
-# in L2 when the kernel ends are not counted by ncu for that launch.
+# DRAM bytes (read + write) per launch of the dominant kernel, taken from one
+# ncu capture of the same kernel at the same size (dram__bytes_read.sum +
+# dram__bytes_write.sum); a recorded figure, not measured by this run.
+# Output writes still in L2 when the kernel ends are not counted by ncu.
 NCU_TRAFFIC = {
-    "fp8_gemm_4096x4096x4096": 34_120_960 + 2_532_864,      # profiles/fp8_gemm_4096_prefill.md
-    "fp4_decode_16x4096x4096": 9_046_784 + 0,               # profiles/fp4_gemm_decode_m16_n4096.md
-    # dram__bytes.sum.per_second x duration (profiles/quantisers_bf16_16384x7168.md)
+    "fp8_gemm_4096x4096x4096": 34_120_960 + 2_532_864,
+    "fp4_decode_16x4096x4096": 9_046_784 + 0,
+    # dram__bytes.sum.per_second x duration
     "act_quant_16384x7168": 325_000_000,
     "fp4_act_quant_16384x7168": 410_000_000,
 }
@@ -141,16 +143,17 @@ def make_fp8_prefill(torch, dev, M, N, K, seed, n_sets):
 
 class pipelined_e2e:
     """Single-GPU e2e steps on three streams with two buffers: step i copies
-    the pinned host activations in (stream in), runs `compute(i, x_dev)`
+    the pinned host inputs in (stream in), runs `compute(i, *inputs_dev)`
     through the public API (stream compute) and copies the result out to
     pinned host memory (stream out).  Step i+2 reuses step i's buffers only
     after step i's compute and copy-out are done, so steps overlap without
-    sharing data."""
+    sharing data.  `x_host` is one pinned tensor or a tuple of them."""
 
     def __init__(self, torch, x_host, out_shape, compute):
-        self.torch, self.x_host, self.compute = torch, x_host, compute
+        self.torch, self.compute = torch, compute
+        self.x_host = tuple(x_host) if isinstance(x_host, (tuple, list)) else (x_host,)
         dev = torch.device("cuda", torch.cuda.current_device())
-        self.x_dev = [torch.empty(x_host.shape, dtype=x_host.dtype, device=dev) for _ in range(2)]
+        self.x_dev = [[torch.empty(h.shape, dtype=h.dtype, device=dev) for h in self.x_host] for _ in range(2)]
         self.o_host = [torch.empty(out_shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
         self.s_in, self.s_comp, self.s_out = (torch.cuda.Stream() for _ in range(3))
         self.in_done = [torch.cuda.Event() for _ in range(2)]
@@ -166,11 +169,13 @@ class pipelined_e2e:
         torch, b = self.torch, i & 1
         with torch.cuda.stream(self.s_in):
             self.s_in.wait_event(self.comp_done[b])          # step i-2 has read x_dev[b]
-            self.x_dev[b].copy_(self.x_host, non_blocking=True)
+            for d, h in zip(self.x_dev[b], self.x_host):
+                d.copy_(h, non_blocking=True)
             self.in_done[b].record()
         with torch.cuda.stream(self.s_comp):
             self.s_comp.wait_event(self.in_done[b])
-            c = self.compute(i, self.x_dev[b])
+            self.s_comp.wait_event(self.out_done[b])         # step i-2's result has left its buffer
+            c = self.compute(i, *self.x_dev[b])
             c.record_stream(self.s_out)
             self.comp_done[b].record()
         with torch.cuda.stream(self.s_out):
@@ -476,17 +481,105 @@ def bench_fp4_decode(args, torch, dist, ws, rank, dev):
             "eager_ms_per_call": round(ms_eager, 5)}
 
 
-def bench_moe(args, torch, dist, ws, rank, dev):
-    """Config-4 MoE layer: T=1024 tokens in total, H=4096, I=2048, E=256, top-8.
+def moe_weights(torch, dev, El, H, I, seed):
+    """One rank's experts: packed e2m1 codes uniform over all 16 values,
+    ue8m0 1x32 scales with exponents uniform in [-6, 0]."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    w13 = torch.randint(0, 256, (El, 2 * I, H // 2), generator=g, device=dev, dtype=torch.uint8)
+    w13_s = 127 - torch.randint(0, 7, (El, 2 * I, H // 32), generator=g, device=dev, dtype=torch.uint8)
+    w2 = torch.randint(0, 256, (El, H, I // 2), generator=g, device=dev, dtype=torch.uint8)
+    w2_s = 127 - torch.randint(0, 7, (El, H, I // 32), generator=g, device=dev, dtype=torch.uint8)
+    return w13, w13_s, w2, w2_s
 
-    One GPU: the whole layer in one call.  N GPUs: expert parallel -- rank r
-    owns tokens [r*T/N, (r+1)*T/N) and experts [r*E/N, (r+1)*E/N); rows travel
-    to the expert owners and back over NVLink peer memory (or, with
-    --ep-transport nccl, by NCCL all-to-all); strong scaling: the total batch
-    is fixed.
+
+def prefill_gemm_rates(torch, dev, peaks):
+    """Device-timed 4096^3 prefill GEMMs through the C ABI: fp8_gemm (1x128
+    activation, 128x128 weight fp32 scales: the dense projection shape) and
+    fp4_gemm (1x128 fp32 activation scales, packed e2m1 weights with ue8m0 1x32
+    scales); five rotating operand sets (> L2)."""
+    pkg = __import__("importlib").import_module(PKG)
+    lib = pkg._lib.load()
+    M = N = K = 4096
+    sets = make_fp8_prefill(torch, dev, M, N, K, 1234, 5)
+    g = torch.Generator(device=dev)
+    g.manual_seed(99)
+    w4 = [(torch.randint(0, 256, (N, K // 2), generator=g, device=dev, dtype=torch.uint8),
+           127 - torch.randint(0, 7, (N, K // 32), generator=g, device=dev, dtype=torch.uint8)) for _ in sets]
+    out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    st = torch.cuda.current_stream().cuda_stream
+    res = {}
+    for name in ("fp8_gemm", "fp4_gemm"):
+        def call(i):
+            a, a_s, b, s, _ = sets[i % len(sets)]
+            if name == "fp8_gemm":
+                pkg._lib.check(lib.bs_fp8_gemm(a.data_ptr(), a_s.data_ptr(), pkg._lib.DT_F32, b.data_ptr(),
+                                               s.data_ptr(), pkg._lib.DT_F32, M, N, K, out.data_ptr(), st))
+            else:
+                b4, s4 = w4[i % len(w4)]
+                pkg._lib.check(lib.bs_fp4_gemm(a.data_ptr(), a_s.data_ptr(), pkg._lib.DT_F32, b4.data_ptr(),
+                                               s4.data_ptr(), pkg._lib.DT_E8M0, M, N, K, out.data_ptr(), st))
+        for i in range(5):
+            call(i)
+        n = 20
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        t0.record()
+        for i in range(n):
+            call(i)
+        t1.record()
+        torch.cuda.synchronize()
+        ms = t0.elapsed_time(t1) / n
+        tf = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+        res[name] = {"tflops": round(tf, 1), "ms": round(ms, 4), "frac": round(tf / (2.0 * peaks["bf16_tflops"]), 3),
+                     "shape": "M=N=K=4096"}
+    res["peak_note"] = "frac of 2 x measured dense bf16 (the e4m3 / e2m1 tensor rate)"
+    return res
+
+
+def cpu_moe_sample(torch, x, logits, weights_cpu_fetch, E, k, budget_s=12.0, min_experts=4, max_experts=None,
+                   seed=0):
+    """The reference's CPU arithmetic for the MoE layer (oracle/torch_cpu.py:
+    act_quant + three LUT-dequant bf16 fp4_gemm per active expert) on the
+    host cores, over a sample of the active experts (seeded order) until
+    `budget_s` is spent.  Returns (layer seconds extrapolated to every active
+    expert, experts timed, active experts)."""
+    from oracle import torch_cpu as tc
+    idx = torch.topk(logits, k, dim=1).indices
+    active = torch.unique(idx).tolist()
+    order = torch.randperm(len(active), generator=torch.Generator().manual_seed(seed)).tolist()
+    xs = x.float().to(torch.bfloat16)
+    w = torch.softmax(torch.topk(logits, k, dim=1).values, dim=1)
+    out = torch.zeros(x.shape, dtype=torch.float32)
+    done, t_total = 0, 0.0
+    for o in order:
+        e = active[o]
+        W = weights_cpu_fetch(e)
+        t = time.perf_counter()
+        tc.moe_experts(xs, idx, w, [e], *({e: t} for t in W), out)
+        t_total += time.perf_counter() - t
+        done += 1
+        if (t_total >= budget_s and done >= min_experts) or (max_experts and done >= max_experts):
+            break
+    return t_total * len(active) / done, done, len(active)
+
+
+def bench_moe(args, torch, dist, ws, rank, dev):
+    """MoE layer (the grouped FP8 x FP4 form): T tokens in total (default
+    1024), H=4096, I=2048, E=256 experts, top-8 of N(0,1) gate logits,
+    weights = softmax over the top 8.
+
+    One GPU: the whole layer (bs_moe_forward: front, experts, combine).  N
+    GPUs: expert parallel -- rank r owns tokens [r*T/N, (r+1)*T/N) and
+    experts [r*E/N, (r+1)*E/N); rows travel to the expert owners and back
+    over NVLink peer memory inside the layer's own kernels (or, with
+    --ep-transport nccl, by NCCL all-to-all); strong scaling: the total
+    batch is fixed.
     """
     import importlib
+    pkg = importlib.import_module(PKG)
     moe = importlib.import_module(PKG + ".moe")
+    lib = pkg._lib.load()
     T, H, I, E, k = args.tokens, 4096, 2048, args.experts, 8
     if T % ws or E % ws:
         raise SystemExit("tokens and experts must split evenly over the ranks")
@@ -495,41 +588,36 @@ def bench_moe(args, torch, dist, ws, rank, dev):
     x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)        # same on every rank
     logits = torch.randn(T, E, generator=g, device=dev)
     El, tl = E // ws, T // ws
-    g.manual_seed(1000 + rank)                                                  # this rank's experts
-    w13 = torch.randint(0, 256, (El, 2 * I, H // 2), generator=g, device=dev, dtype=torch.uint8)
-    w13_s = 127 - torch.randint(0, 7, (El, 2 * I, H // 32), generator=g, device=dev, dtype=torch.uint8)
-    w2 = torch.randint(0, 256, (El, H, I // 2), generator=g, device=dev, dtype=torch.uint8)
-    w2_s = 127 - torch.randint(0, 7, (El, H, I // 32), generator=g, device=dev, dtype=torch.uint8)
+    w13, w13_s, w2, w2_s = moe_weights(torch, dev, El, H, I, 1000 + rank)     # this rank's experts
     weights = moe.MoEWeights(w13, w13_s, w2, w2_s)
     xl, ll = x[rank * tl:(rank + 1) * tl].contiguous(), logits[rank * tl:(rank + 1) * tl].contiguous()
-    out = torch.empty(tl, H, dtype=torch.bfloat16, device=dev)
+    outs = [torch.empty(tl, H, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    layer, graph = None, None
     if ws == 1:
-        def step():
-            moe.moe_forward(xl, ll, weights, k, out=out)
-        launches = 8
+        def call(xd, ld, o):
+            return moe.moe_forward(xd, ld, weights, k, out=o)
+        launches = 3
     else:
         ep = importlib.import_module(PKG + ".ep")
         layer = ep.EPMoE(weights, E, k, max_tokens=tl, transport=args.ep_transport)
 
-        launches = 14 if args.ep_transport == "peer" else 9
-        if args.ep_transport == "peer":
-            # no host sync inside the layer: capture it once, replay one graph per step
-            for _ in range(2):
-                layer.forward(xl, ll, out=out)
-            torch.cuda.synchronize()
-            graph = torch.cuda.CUDAGraph()
-            cap = torch.cuda.Stream()
-            cap.wait_stream(torch.cuda.current_stream())
-            with torch.cuda.stream(cap):
-                with torch.cuda.graph(graph, stream=cap):
-                    layer.forward(xl, ll, out=out)
-            torch.cuda.current_stream().wait_stream(cap)
-
-            def step():
-                graph.replay()
-        else:
-            def step():
-                layer.forward(xl, ll, out=out)
+        def call(xd, ld, o):
+            return layer.forward(xd, ld, out=o)
+        launches = 3 if args.ep_transport == "peer" else 9
+    step = lambda: call(xl, ll, outs[0])                                        # noqa: E731
+    if ws > 1 and args.ep_transport == "peer":
+        # no host sync inside the layer: capture it once, replay one graph per step
+        for _ in range(2):
+            step()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        cap = torch.cuda.Stream()
+        cap.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(cap):
+            with torch.cuda.graph(graph, stream=cap):
+                step()
+        torch.cuda.current_stream().wait_stream(cap)
+        step = graph.replay
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
@@ -548,58 +636,96 @@ def bench_moe(args, torch, dist, ws, rank, dev):
     clk = clocks.stop()
     ms = max_over_ranks(torch, dist, t0.elapsed_time(t1) / args.steps)
 
+    # the dominant kernel (persistent W1|W3 + W2 grouped GEMMs), timed live
+    # with events the library records around it on the launching stream
+    kern_ms = None
+    if args.ep_transport == "peer" or ws == 1:
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for e0, e1 in evs:
+            e0.record()
+            e1.record()                       # creates the events
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        for e0, e1 in evs:
+            lib.bs_moe_time_experts(e0.cuda_event, e1.cuda_event)
+            call(xl, ll, outs[0])
+        torch.cuda.synchronize()
+        kern_ms = max_over_ranks(torch, dist, statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs))
+    # rows this rank's experts receive (routing is a pure function of the logits)
+    top = torch.topk(logits, k, dim=1).indices
+    recv = int(((top >= rank * El) & (top < (rank + 1) * El)).sum().item())
+    wbytes = w13.numel() + w13_s.numel() + w2.numel() + w2_s.numel()            # this rank's weights + scales
+    # activation bytes of the experts kernel: received rows + their scales in,
+    # hidden rows written and read back, bf16 outputs out
+    abytes = recv * (H + H // 32) + 2 * recv * (I + I // 32) + recv * H * 2
+    kbytes = wbytes + abytes
+    peaks, src = load_peaks()
+    gbs = kbytes / (kern_ms * 1e-3) / 1e9 if kern_ms else None
+
     # end to end through the public API: pinned host bf16 tokens and fp32 gate
-    # logits -> device -> the layer (eager) -> pinned host output
+    # logits -> device -> the layer -> pinned host output, consecutive steps
+    # overlapped on copy-in / compute / copy-out streams
     x_host, l_host = xl.cpu().pin_memory(), ll.cpu().pin_memory()
-    o_host = torch.empty(tl, H, dtype=torch.bfloat16).pin_memory()
-    x_dev, l_dev = torch.empty_like(xl), torch.empty_like(ll)
-
-    def e2e_step():
-        x_dev.copy_(x_host, non_blocking=True)
-        l_dev.copy_(l_host, non_blocking=True)
-        if ws == 1:
-            moe.moe_forward(x_dev, l_dev, weights, k, out=out)
-        else:
-            layer.forward(x_dev, l_dev, out=out)
-        o_host.copy_(out, non_blocking=True)
-
-    for _ in range(2):
-        e2e_step()
+    e2e_step = pipelined_e2e(torch, (x_host, l_host), (tl, H), lambda i, xd, ld: call(xd, ld, outs[i & 1]))
+    for i in range(2):
+        e2e_step(i)
     torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.steps):
-        e2e_step()
+    e2e_step.start()
+    for i in range(args.steps):
+        e2e_step(i)
+    e2e_step.join()
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(torch, dist, e0.elapsed_time(e1) / args.steps)
     if ws > 1:
-        if args.ep_transport == "peer":
-            del graph
-        pkg_lib = importlib.import_module(PKG + "._lib")
-        pkg_lib.device_error_check()
+        del graph
+        torch.cuda.synchronize()
+        pkg._lib.device_error_check()
         layer.close()
-    wbytes = w13.numel() + w13_s.numel() + w2.numel() + w2_s.numel()          # per rank
-    peaks, src = load_peaks()
-    gbs = wbytes / (ms * 1e-3) / 1e9
-    return {"metric": "MoE-layer tokens/s", "value": round(T / (ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": ws,
+    line = {"metric": "MoE-layer tokens/s", "value": round(T / (ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "e4m3 x e2m1", "data": "synthetic",
-            "config": {"workload": f"MoE layer T={T} H={H} I={I} E={E} top-{k}",
+            "scaling": "strong", "vs_baseline": None, "dtype": "e4m3 x e2m1",
+            "data": "synthetic (seeded N(0,1) tokens and gate logits, uniform e2m1 codes, ue8m0 exponents in [-6,0])",
+            "config": {"workload": f"MoE layer T={T} H={H} I={I} E={E} top-{k} (grouped FP8xFP4 GEMMs)",
                        "parallelism": f"ep{ws}" if ws > 1 else "none",
-                       "exchange": (("NVLink peer memory (no NCCL, no host sync)" if args.ep_transport == "peer"
-                                     else "NCCL all-to-all") if ws > 1 else None),
-                       "l2": f"weights {wbytes * ws / 2**30:.2f} GiB >> L2"},
-            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": round(gbs / peaks["hbm_gbs"], 3), "traffic": None,
-                         "note": "this rank's expert weight bytes per layer / layer time", "peak_source": src},
+                       "exchange": (("NVLink peer memory inside the layer's kernels (no NCCL, no host sync)"
+                                     if args.ep_transport == "peer" else "NCCL all-to-all") if ws > 1 else None),
+                       "l2": f"expert weights {wbytes * ws / 2**30:.2f} GiB >> L2 (every step streams them)"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1) if gbs else None, "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 3) if gbs else None,
+                         "traffic": NCU_TRAFFIC.get(f"moe_experts_{T // ws}x{E // ws}") if ws == 1 else None,
+                         "kernel": "mf::experts_kernel (persistent W1|W3 + W2 grouped GEMMs)",
+                         "kernel_ms": round(kern_ms, 4) if kern_ms else None,
+                         "algorithmic_bytes": kbytes,
+                         "note": "this rank's expert weights + scales, received rows, hidden rows written and read, "
+                                 "outputs, per launch / the kernel's event-timed duration (max over ranks)",
+                         "peak_source": f"hbm_gbs of {src} MEASURED_PEAKS.json"},
             "e2e": {"value": round(T / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": ws * tl * (H * 2 + E * 4), "d2h_bytes_per_step": ws * tl * H * 2,
                     "ms_per_step": round(e2e_ms, 4),
-                    "path": "moe_forward / EPMoE.forward public API, pinned host tokens + logits in, output out"},
+                    "path": "moe_forward / EPMoE.forward public API, pinned host tokens + logits in, output out; "
+                            "consecutive steps overlapped on copy-in / compute / copy-out streams"},
             "gpu_launches": args.steps * launches, "clocks": clk}
+    if ws == 1:
+        line["prefill_gemm"] = prefill_gemm_rates(torch, dev, peaks)
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        torch.set_num_threads(cpu_threads())
+        xc, lc = x.cpu(), logits.cpu()
+        fetch = lambda e: (w13[e].cpu(), w13_s[e].cpu().view(torch.float8_e8m0fnu), w2[e].cpu(),   # noqa: E731
+                           w2_s[e].cpu().view(torch.float8_e8m0fnu))
+        layer_s, n_done, n_act = cpu_moe_sample(torch, xc, lc, fetch, E, k)
+        line["cpu_baseline"] = {"value": round(T / layer_s, 2), "unit": "tokens/s", "cores": cpu_threads(),
+                                "kind": "port",
+                                "sample": f"{n_done} of the {n_act} active experts with all their routed tokens "
+                                          f"through the torch restatement of the reference's CPU ops (act_quant + "
+                                          f"LUT-dequant bf16 fp4_gemm x3 per expert); layer time extrapolated to "
+                                          f"all active experts: {layer_s:.2f} s"}
+    return line
 
 
 def bench_quant(args, torch, dist, ws, rank, dev):
@@ -732,22 +858,6 @@ def cpu_threads():
     return len(os.sched_getaffinity(0))
 
 
-def cpu_fp8_prefill(steps: int, warmup: int, m_rows: int = 4096):
-    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
-    import cases
-    from oracle import blockscaled as ob
-    c = cases.cfg2_fp8(M=m_rows)
-    for _ in range(warmup):
-        ob.fp8_gemm(c["a"], c["a_s"], c["b"], c["b_s"])
-    times = []
-    for _ in range(steps):
-        t = time.perf_counter()
-        ob.fp8_gemm(c["a"], c["a_s"], c["b"], c["b_s"])
-        times.append(time.perf_counter() - t)
-    s = min(times)
-    return 2.0 * m_rows * 4096 * 4096 / s / 1e12, s
-
-
 def cpu_fp4_decode(M: int, N: int, K: int = 4096, steps: int = 3):
     """The oracle's fp4_gemm (the reference CPU path: LUT dequant of all of B ->
     bf16 -> matmul) on the decode shape; GB/s of the same bytes the GPU line
@@ -851,22 +961,15 @@ def bench_moe_stack(args, torch, dist, ws, rank, dev):
         dist.barrier()
     clk = clocks.stop()
     ms = max_over_ranks(torch, dist, t0.elapsed_time(t1) / args.steps)
-    # load balance: rows each rank's experts received per layer (max / mean over ranks)
-    recv = torch.zeros(L, dtype=torch.float64, device=dev)
+    # load balance: rows each rank's experts receive per layer, max / mean over
+    # the owners; routing is a pure function of the logits
+    per_owner = torch.zeros(L, ws, dtype=torch.float64, device=dev)
     for l in range(L):
-        if ws > 1:
-            recv[l] = float(eps[l].loc_off[El].item()) if args.ep_transport == "peer" else float(
-                eps[l].recv_counts.sum().item())
-        else:
-            recv[l] = float(tl * k)
+        owner = torch.topk(logits[l], k, dim=1).indices // El
+        per_owner[l] = torch.bincount(owner.flatten(), minlength=ws).double()
     if dist is not None:
-        mx, mean = recv.clone(), recv.clone()
-        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        dist.all_reduce(mean)
-        mean /= ws
-        imbalance = [round(float(a / b), 3) for a, b in zip(mx, mean)]
-    else:
-        imbalance = [1.0] * L
+        dist.all_reduce(per_owner)
+    imbalance = [round(float(r.max() / r.mean()), 3) for r in per_owner]
     # end to end: pinned host tokens in, the last layer's output out
     x_host = x0.cpu().pin_memory()
     o_host = torch.empty(tl, H, dtype=torch.bfloat16).pin_memory()
@@ -909,8 +1012,90 @@ def bench_moe_stack(args, torch, dist, ws, rank, dev):
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
                          "frac": round(achieved / peak, 3), "traffic": None,
                          "note": "per-GPU FLOP of the stack / stack time vs the dense e4m3 rate"},
-            "gpu_launches": args.steps * L * (2 + (14 if ws > 1 and args.ep_transport == "peer" else 9)),
+            "gpu_launches": args.steps * L * (2 + (3 if ws == 1 or args.ep_transport == "peer" else 9)),
             "clocks": clk}
+
+
+def reference_moe(args, ws):
+    """The MoE workload on the host CPU: each step runs a bounded sample of the
+    layer (8 of the active experts, all their routed tokens) through the
+    torch restatement of the reference's CPU ops, and the step's layer time
+    is that sample's time scaled to every active expert."""
+    import torch
+    torch.set_num_threads(cpu_threads())
+    T, H, I, E, k = args.tokens, 4096, 2048, args.experts, 8
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    logits = torch.randn(T, E, generator=g)
+    cache = {}
+
+    def fetch(e):
+        if e not in cache:
+            ge = torch.Generator().manual_seed(50_000 + e)
+            cache[e] = (torch.randint(0, 256, (2 * I, H // 2), generator=ge, dtype=torch.uint8),
+                        (127 - torch.randint(0, 7, (2 * I, H // 32), generator=ge, dtype=torch.uint8)).view(
+                            torch.float8_e8m0fnu),
+                        torch.randint(0, 256, (H, I // 2), generator=ge, dtype=torch.uint8),
+                        (127 - torch.randint(0, 7, (H, I // 32), generator=ge, dtype=torch.uint8)).view(
+                            torch.float8_e8m0fnu))
+        return cache[e]
+
+    per_step = 8
+    for w in range(args.warmup):
+        cpu_moe_sample(torch, x, logits, fetch, E, k, budget_s=0.0, min_experts=per_step, max_experts=per_step,
+                       seed=w)
+    times = []
+    for i in range(args.steps):
+        layer_s, _, n_act = cpu_moe_sample(torch, x, logits, fetch, E, k, budget_s=0.0, min_experts=per_step,
+                                           max_experts=per_step, seed=100 + i)
+        times.append(layer_s)
+    layer_s = statistics.mean(times)
+    v = T / layer_s
+    return {"impl": "reference", "metric": "MoE-layer tokens/s", "value": round(v, 3), "unit": "tokens/s",
+            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(layer_s * 1e3, 1),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "e4m3 x e2m1",
+            "data": "synthetic (seeded N(0,1) tokens and gate logits, uniform e2m1 codes, ue8m0 exponents in [-6,0])",
+            "config": {"workload": f"MoE layer T={T} H={H} I={I} E={E} top-{k} (grouped FP8xFP4 GEMMs)",
+                       "parallelism": "host CPU"},
+            "cpu_baseline": {"value": round(v, 3), "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
+                             "sample": f"per step {per_step} of the {n_act} active experts with all their routed "
+                                       "tokens (act_quant + LUT-dequant bf16 fp4_gemm x3 per expert, torch on the "
+                                       "host cores); layer time scaled to all active experts"},
+            "e2e": {"value": round(v, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def reference_fp8(args, ws):
+    """The dense fp8_gemm (M=N=K=4096) through the torch restatement of the
+    reference's CPU branch: dequantise both operands, round to bf16, one
+    bf16 torch.mm."""
+    import torch
+    from oracle import torch_cpu as tc
+    torch.set_num_threads(cpu_threads())
+    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+    import cases
+    c = cases.cfg2_fp8(M=4096)
+    a = torch.from_numpy(c["a"]).view(torch.float8_e4m3fn)
+    a_s = torch.from_numpy(c["a_s"])
+    b = torch.from_numpy(c["b"]).view(torch.float8_e4m3fn)
+    b_s = torch.from_numpy(c["b_s"])
+    for _ in range(args.warmup):
+        tc.fp8_gemm(a, a_s, b, b_s)
+    times = []
+    for _ in range(args.steps):
+        t = time.perf_counter()
+        tc.fp8_gemm(a, a_s, b, b_s)
+        times.append(time.perf_counter() - t)
+    s = statistics.mean(times)
+    v = 2.0 * 4096 ** 3 / s / 1e12
+    return {"impl": "reference",
+            "metric": "block-scaled FP8 GEMM TFLOP/s (dense fp8_gemm, 1x128 act + 128x128 weight fp32 scales)",
+            "value": round(v, 4), "unit": "TFLOP/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(s * 1e3, 2), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "e4m3", "data": "synthetic",
+            "config": {"workload": "fp8_gemm M=N=K=4096 on the host CPU", "M": 4096, "N": 4096, "K": 4096},
+            "cpu_baseline": {"value": round(v, 4), "unit": "TFLOP/s", "cores": cpu_threads(), "kind": "port",
+                             "sample": "one full 4096^3 fp8_gemm per step: dequantise -> bf16 -> torch.mm (torch)"},
+            "e2e": {"value": round(v, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
 def main():
@@ -919,8 +1104,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["fp8_prefill", "fp4_decode", "moe", "moe_stack", "act_quant",
-                                           "fp4_act_quant"], default="fp8_prefill")
+    ap.add_argument("--workload", choices=["moe", "fp8_prefill", "fp4_decode", "moe_stack", "act_quant",
+                                           "fp4_act_quant"], default="moe")
     ap.add_argument("--tokens", type=int, default=None,
                     help="moe: 1024, moe_stack: 8192, act_quant / fp4_act_quant: 16384 rows")
     ap.add_argument("--experts", type=int, default=256)
@@ -938,21 +1123,13 @@ def main():
     ws, rank, local = dist_env()
 
     if args.impl == "reference":
-        # CPU port of the reference algorithm, rank 0 only; other ranks exit.
+        # the reference's CPU arithmetic on the host cores, rank 0 only; other ranks exit
         if rank != 0:
             return
-        steps = max(1, min(args.steps, 3))
-        v, s = cpu_fp8_prefill(steps, 1)
-        print(json.dumps({
-            "impl": "reference", "metric": "block-scaled FP8 GEMM TFLOP/s (dense fp8_gemm, 1x128 act + 128x128 weight fp32 scales)",
-            "value": round(v, 4), "unit": "TFLOP/s", "n_gpus": ws, "steps": steps, "warmup": 1,
-            "ms_per_step": round(s * 1e3, 2), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "e4m3", "data": "synthetic",
-            "config": {"workload": "fp8_gemm M=N=K=4096 on the host CPU", "M": 4096, "N": 4096, "K": 4096},
-            "cpu_baseline": {"value": round(v, 4), "unit": "TFLOP/s", "cores": cpu_threads(), "kind": "port",
-                             "sample": "one full 4096^3 fp8_gemm per step: LUT dequant -> bf16 -> fp32 matmul (numpy)"},
-            "e2e": {"value": round(v, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        }), flush=True)
+        if args.workload == "moe":
+            print(json.dumps(reference_moe(args, ws)), flush=True)
+        else:
+            print(json.dumps(reference_fp8(args, ws)), flush=True)
         return
 
     import torch
@@ -988,10 +1165,8 @@ def main():
                                 "sample": f"fp4_gemm M={args.m} N={args.n} K=4096 on the host ({s * 1e3:.1f} ms per "
                                           "call): LUT dequant of all of B -> bf16 -> fp32 matmul (numpy), best of 3"}
     if rank == 0 and ws == 1 and args.workload == "fp8_prefill" and not args.no_cpu_baseline:
-        torch.set_num_threads(cpu_threads())
-        v, s = cpu_fp8_prefill(1, 0, m_rows=4096)
-        line["cpu_baseline"] = {"value": round(v, 4), "unit": "TFLOP/s", "cores": cpu_threads(), "kind": "port",
-                                "sample": f"one full 4096^3 fp8_gemm ({s:.2f} s): LUT dequant -> bf16 -> fp32 matmul (numpy)"}
+        r = reference_fp8(argparse.Namespace(steps=2, warmup=1), 1)
+        line["cpu_baseline"] = r["cpu_baseline"]
     pkg = importlib.import_module(PKG)
     pkg._lib.device_error_check()
     if rank == 0:

@@ -23,6 +23,6 @@ def test_reference_arm_json_line():
     d = json.loads(lines[0])
     for k in REQUIRED:
         assert k in d, k
-    assert d["impl"] == "reference" and d["value"] > 0 and d["unit"] == "TFLOP/s"
+    assert d["impl"] == "reference" and d["value"] > 0 and d["unit"] == "tokens/s"
     assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["cores"] >= 1
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0

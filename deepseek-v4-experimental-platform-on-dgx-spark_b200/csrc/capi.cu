@@ -176,6 +176,26 @@ int bs_fp4_gemm(const void* a, const void* a_s, int as_dtype, const void* b, con
   return gemm_common(true, a, a_s, as_dtype, b, b_s, bs_dtype, M, N, K, &c, 1, N, 0, stream, "fp4_gemm");
 }
 
+int bs_fp4_weights_to_bf16(const void* b, const float* b_s, int64_t N, int64_t K, void* out, void* stream) {
+  if (N < 0 || K <= 0 || K % 32) return fail(BS_ERR_INVALID_ARG, "fp4_weights_to_bf16: N=%lld K=%lld (K a multiple of 32)",
+                                             (long long)N, (long long)K);
+  if (N > 0 && (!b || !b_s || !out || !aligned(b, 16) || !aligned(b_s, 4) || !aligned(out, 16)))
+    return fail(BS_ERR_INVALID_ARG, "fp4_weights_to_bf16: null or misaligned pointer (b, out 16 B; b_s 4 B)");
+  return cuda_status(bs_launch_fp4_to_bf16(b, b_s, N, K, out, (cudaStream_t)stream), "fp4_weights_to_bf16");
+}
+
+int bs_e4m3_rows_to_bf16(const void* a, const void* a_s, int as_dtype, int64_t M, int64_t K, void* out, void* stream) {
+  if (M < 0 || K <= 0 || K % 128) return fail(BS_ERR_INVALID_ARG, "e4m3_rows_to_bf16: M=%lld K=%lld (K a multiple of 128)",
+                                              (long long)M, (long long)K);
+  if (as_dtype != BS_DT_F32 && as_dtype != BS_DT_E8M0)
+    return fail(BS_ERR_UNSUPPORTED, "e4m3_rows_to_bf16: scale dtype tag %d (f32 or e8m0)", as_dtype);
+  if (M > 0 && (!a || !a_s || !out || !aligned(a, 16) || !aligned(out, 16) ||
+                !aligned(a_s, as_dtype == BS_DT_F32 ? 4 : 1)))
+    return fail(BS_ERR_INVALID_ARG, "e4m3_rows_to_bf16: null or misaligned pointer (a, out 16 B)");
+  return cuda_status(bs_launch_e4m3_to_bf16(a, a_s, as_dtype == BS_DT_E8M0, M, K, out, (cudaStream_t)stream),
+                     "e4m3_rows_to_bf16");
+}
+
 int bs_fp8_gemm_allgather(const void* a, const void* a_s, int as_dtype, const void* b, const void* b_s,
                           int bs_dtype, int64_t M, int64_t N, int64_t K, void* const* c_ranks, int n_ranks,
                           int64_t ldc, int64_t col0, void* stream) {

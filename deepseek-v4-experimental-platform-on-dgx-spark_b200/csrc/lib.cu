@@ -2,6 +2,7 @@
 // and the extern "C" entry points share the device error word directly.
 #include "common.cuh"
 #include "quant.cu"
+#include "dequant.cu"
 #include "gemm.cu"
 #include "gemm_pair.cu"
 #include "moe.cu"

@@ -155,17 +155,22 @@ def fp8_gemm(a: torch.Tensor, a_s: torch.Tensor, b: torch.Tensor, b_s: torch.Ten
     return out.view(out_shape)
 
 
-def _fp4_weight_scales(b_s: torch.Tensor) -> torch.Tensor:
-    if b_s.dtype == torch.float8_e8m0fnu:
-        return b_s.contiguous()
-    # fp32 weight scales are usable only if they are exact powers of two in
-    # the e8m0 range (the reference's CPU path multiplies by them exactly).
-    f = b_s.float().contiguous()
-    bits = f.view(torch.int32)
-    exact = bool(((bits & 0x807FFFFF) == 0).all()) and bool(((bits >> 23) > 0).all())
-    if not exact:
-        raise NotImplementedError("fp4_gemm: fp32 weight scales must be powers of two (ue8m0)")
-    return (bits >> 23).to(torch.uint8).view(torch.float8_e8m0fnu)
+def _fp4_gemm_fp32_scales(a_flat: torch.Tensor, a_sf: torch.Tensor, as_dt: int, b_u8: torch.Tensor,
+                          b_s: torch.Tensor, M: int, N: int, K: int) -> torch.Tensor:
+    """fp32 weight scales of any value: the reference CPU branch's arithmetic
+    (kernel_sm121.py:402-417) -- both operands dequantised to bf16 on the
+    device, then one bf16 GEMM with fp32 accumulation (torch.mm, a plain
+    library GEMM).  No host sync."""
+    lib = _lib.load()
+    st = _stream(a_flat)
+    bs = b_s.float().contiguous()
+    if bs.shape != (N, K // 32):
+        raise ValueError(f"fp4_gemm: weight scale shape {tuple(bs.shape)} does not match N={N}, K={K}")
+    a_bf = torch.empty(M, K, dtype=torch.bfloat16, device=a_flat.device)
+    b_bf = torch.empty(N, K, dtype=torch.bfloat16, device=a_flat.device)
+    _lib.check(lib.bs_e4m3_rows_to_bf16(a_flat.data_ptr(), a_sf.data_ptr(), as_dt, M, K, a_bf.data_ptr(), st))
+    _lib.check(lib.bs_fp4_weights_to_bf16(b_u8.data_ptr(), bs.data_ptr(), N, K, b_bf.data_ptr(), st))
+    return torch.mm(a_bf, b_bf.t())
 
 
 def fp4_gemm(a: torch.Tensor, a_s: torch.Tensor, b: torch.Tensor, b_s: torch.Tensor,
@@ -186,8 +191,14 @@ def fp4_gemm(a: torch.Tensor, a_s: torch.Tensor, b: torch.Tensor, b_s: torch.Ten
     if b_u8.shape != (N, K // 2):
         raise ValueError(f"fp4_gemm: weight shape {tuple(b.shape)} does not match K={K}")
     a_sf, as_dt = _scale_arg(a_s.view(M, -1))
-    b_sf = _fp4_weight_scales(b_s)
-    if a_sf.shape != (M, K // 128) or b_sf.shape != (N, K // 32):
+    if a_sf.shape != (M, K // 128):
+        raise ValueError(f"fp4_gemm: activation scale shape {tuple(a_sf.shape)} does not match M={M}, K={K}")
+    if b_s.dtype != torch.float8_e8m0fnu:
+        out = _fp4_gemm_fp32_scales(a_flat, a_sf, as_dt, b_u8, b_s, M, N, K)
+        _tally("fp4_gemm", t0)
+        return out.view(out_shape)
+    b_sf = b_s.contiguous()
+    if b_sf.shape != (N, K // 32):
         raise ValueError(f"fp4_gemm: scale shapes {tuple(a_sf.shape)} / {tuple(b_sf.shape)} do not match "
                          f"M={M}, N={N}, K={K}")
     out = torch.empty(M, N, device=a.device, dtype=torch.bfloat16)

@@ -109,6 +109,18 @@ int bs_fp4_gemm(const void* a, const void* a_s, int as_dtype, const void* b, con
                 int64_t M, int64_t N, int64_t K, void* c, void* stream);
 
 /*
+ * fp4_gemm with fp32 weight scales of any value (kernel_sm121.py:402-417,
+ * the reference's CPU branch, multiplies by them exactly; the block-scaled
+ * MMA applies only power-of-two scales).  Such a call is computed the way
+ * that branch computes it: out = bf16(e2m1(b) * b_s[n, k/32]) [N, K] and
+ * out = bf16(e4m3(a) * a_s[m, k/128]) [M, K] (a_s BS_DT_F32 or BS_DT_E8M0),
+ * then one bf16 GEMM with fp32 accumulation by the caller (kernel.fp4_gemm
+ * uses torch.mm).  Both kernels are HBM-bound streams.
+ */
+int bs_fp4_weights_to_bf16(const void* b, const float* b_s, int64_t N, int64_t K, void* out, void* stream);
+int bs_e4m3_rows_to_bf16(const void* a, const void* a_s, int as_dtype, int64_t M, int64_t K, void* out, void* stream);
+
+/*
  * Tensor-parallel GEMM with the all-gather fused into its epilogue.  This
  * rank holds the weight rows [col0, col0+N) (b, b_s as for bs_fp8_gemm /
  * bs_fp4_gemm) and computes the column slice C[:, col0:col0+N]; every output

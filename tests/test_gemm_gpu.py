@@ -146,6 +146,51 @@ def test_fp4_prefill_ue8m0_act_scales_vs_oracle(pkg, shape):
     check(bits(out), bits(run_fp4(pkg, c32)), f"fp4 ue8m0 act vs fp32 scales M={M}")
 
 
+@pytest.mark.parametrize("shape", [(16, 2048, 4096), (200, 512, 1024), (1, 256, 512)])
+@pytest.mark.parametrize("as_dt", ["f32", "e8m0"])
+def test_fp4_gemm_fp32_weight_scales_vs_oracle(pkg, shape, as_dt):
+    """fp32 weight scales that are not powers of two (kernel_sm121.py:402-406
+    multiplies by any fp32 scale): dequantised to bf16 on the device, then
+    one bf16 GEMM, as the reference's CPU branch computes it."""
+    M, N, K = shape
+    c = cases.cfg1_fp4(M=M, N=N, K=K, scale_fmt="ue8m0" if as_dt == "e8m0" else None, seed=M + N + 7)
+    if as_dt == "e8m0":
+        c = dict(c, a_s=ob.from_f32(c["a_s"], ob.DT_E8M0), as_dt="e8m0")
+    rng = np.random.default_rng(N + K)
+    b_s32 = (rng.uniform(0.3, 3.0, size=(N, K // 32)) * 2.0 ** rng.integers(-6, 1, size=(N, K // 32))).astype(np.float32)
+    ref = ob.fp4_gemm(c["a"], c["a_s"], c["b"], b_s32, DT[c["as_dt"]], ob.DT_F32)
+    out = pkg.fp4_gemm(cuda_u8(c["a"], torch.float8_e4m3fn), _scale(c["a_s"], c["as_dt"]),
+                       cuda_u8(c["b"], torch.float4_e2m1fn_x2), cuda_f32(b_s32))
+    check(bits(out), ref, f"fp4 fp32 weight scales M={M} N={N} K={K} act={as_dt}")
+
+
+def test_fp8_mx_form_special_scale_bytes(pkg):
+    """Both scales ue8m0 (the MX form, scales applied by the MMA).  A block
+    whose activation scale byte is 0 contributes 0 in the reference
+    (byte << 23 is 0.0) and at most 2^-127 times its products here: the rows
+    stay within tolerance.  A byte of 255 is +inf in the reference and NaN in
+    the MMA: the affected rows are non-finite in both."""
+    M, N, K = 256, 512, 1024
+    rng = np.random.default_rng(21)
+    x = ob.f32_to_bf16(rng.standard_normal((M, K)).astype(np.float32))
+    a, a_s = ob.act_quant(x, ob.DT_BF16, 128, "ue8m0", ob.DT_E8M0)
+    b, b_s = _e8m0_weight_case(rng, N, K)
+    a_s = a_s.copy()
+    a_s[3, 2] = 0          # one zero block scale
+    a_s[10, :] = 0         # a whole row of zero scales
+    ref = ob.fp8_gemm(a, a_s, b, b_s, ob.DT_E8M0, ob.DT_E8M0)
+    out = bits(run_fp8(pkg, dict(a=a, a_s=a_s, b=b, b_s=b_s, as_dt="e8m0", bs_dt="e8m0")))
+    check(out, ref, "fp8 MX form, zero scale bytes")
+    assert np.abs(ob.bf16_to_f32(out[10])).max() < 1e-30
+    a_s[20, 1] = 255
+    ref = ob.bf16_to_f32(ob.fp8_gemm(a, a_s, b, b_s, ob.DT_E8M0, ob.DT_E8M0))
+    out = ob.bf16_to_f32(bits(run_fp8(pkg, dict(a=a, a_s=a_s, b=b, b_s=b_s, as_dt="e8m0", bs_dt="e8m0"))))
+    bad_ref, bad_out = ~np.isfinite(ref), ~np.isfinite(out)
+    assert bad_ref[20].any() and bad_out[20].all()
+    assert not bad_out[np.arange(M) != 20].any() and not bad_ref[np.arange(M) != 20].any()
+    np.testing.assert_array_equal(bad_out[20] | ~bad_ref[20], np.ones(N, bool))
+
+
 def test_gemm_leading_dims(pkg):
     c = cases.cfg1_fp4(M=12, N=256, K=512, seed=3)
     a = cuda_u8(c["a"], torch.float8_e4m3fn).view(3, 4, 512)

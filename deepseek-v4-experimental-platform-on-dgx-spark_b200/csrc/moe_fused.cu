@@ -49,7 +49,7 @@
 namespace mf {
 
 constexpr int kMaxRanks = 8;
-constexpr int kFrontThreads = 256;
+constexpr int kFrontThreads = 512;
 constexpr unsigned long long kWaitNs = 2000000000ull;   // 2 s
 
 // per-rank sync words (uint64)
@@ -196,43 +196,53 @@ __global__ void __launch_bounds__(kFrontThreads) front_kernel(FrontArgs a, Peers
   }
   for (int64_t i = gtid; i < a.chunk_cap; i += nthreads) a.h_done[i] = 0;
 
-  // ---- A: quantise (half a warp per 1x128 block, power-of-two scales)
+  // ---- A: quantise (half a warp per 1x128 block, power-of-two scales);
+  // each half warp issues the loads of kQ blocks before quantising any
   {
+    constexpr int kQ = 4;
     const int half = lane >> 4, l16 = lane & 15;
     const int64_t n_groups = (int64_t)a.T * nb;
-    for (int64_t base = gwarp * 2; base < n_groups; base += nwarps * 2) {
-      const int64_t g = base + half;
-      const bool valid = g < n_groups;
-      const uint4 raw = valid ? __ldg(reinterpret_cast<const uint4*>(a.x + g * 128) + l16) : make_uint4(0, 0, 0, 0);
-      const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
-      const uint32_t m2 = max_u16x2(max_u16x2(wv[0] & 0x7FFF7FFFu, wv[1] & 0x7FFF7FFFu),
-                                    max_u16x2(wv[2] & 0x7FFF7FFFu, wv[3] & 0x7FFF7FFFu));
-      uint32_t mb = max(m2 << 16, m2 & 0xFFFF0000u);
+    for (int64_t base = gwarp * 2 * kQ; base < n_groups; base += nwarps * 2 * kQ) {
+      uint4 raw[kQ];
 #pragma unroll
-      for (int o = 8; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, o));
-      float amax = __uint_as_float(mb);
-      amax = amax < 1e-4f ? 1e-4f : amax;
-      const float scale = bs_round_pow2(__fdiv_rn(amax, 448.0f));
-      if (valid) {
-        float f[8], q[8];
+      for (int u = 0; u < kQ; ++u) {
+        const int64_t g = base + 2 * u + half;
+        raw[u] = g < n_groups ? __ldg(reinterpret_cast<const uint4*>(a.x + g * 128) + l16) : make_uint4(0, 0, 0, 0);
+      }
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          f[2 * i] = __uint_as_float(wv[i] << 16);
-          f[2 * i + 1] = __uint_as_float(wv[i] & 0xFFFF0000u);
+      for (int u = 0; u < kQ; ++u) {
+        const int64_t g = base + 2 * u + half;
+        const bool valid = g < n_groups;
+        const uint32_t wv[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
+        const uint32_t m2 = max_u16x2(max_u16x2(wv[0] & 0x7FFF7FFFu, wv[1] & 0x7FFF7FFFu),
+                                      max_u16x2(wv[2] & 0x7FFF7FFFu, wv[3] & 0x7FFF7FFFu));
+        uint32_t mb = max(m2 << 16, m2 & 0xFFFF0000u);
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+        float amax = __uint_as_float(mb);
+        amax = amax < 1e-4f ? 1e-4f : amax;
+        const float scale = bs_round_pow2(__fdiv_rn(amax, 448.0f));
+        if (valid) {
+          float f[8], q[8];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            f[2 * i] = __uint_as_float(wv[i] << 16);
+            f[2 * i + 1] = __uint_as_float(wv[i] & 0xFFFF0000u);
+          }
+          if ((__float_as_uint(scale) & 0x7F800000u) != 0x7F800000u) {
+            const float r = bs_inv_pow2(scale);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) q[i] = __fmul_rn(f[i], r);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) q[i] = __fdiv_rn(f[i], scale);
+          }
+          uint2 c;
+          c.x = bs_cvt_e4m3x2(q[0], q[1]) | ((uint32_t)bs_cvt_e4m3x2(q[2], q[3]) << 16);
+          c.y = bs_cvt_e4m3x2(q[4], q[5]) | ((uint32_t)bs_cvt_e4m3x2(q[6], q[7]) << 16);
+          *reinterpret_cast<uint2*>(a.xq + g * 128 + l16 * 8) = c;
+          if (l16 == 0) a.xs[g] = bs_f32_to_e8m0(scale);
         }
-        if ((__float_as_uint(scale) & 0x7F800000u) != 0x7F800000u) {
-          const float r = bs_inv_pow2(scale);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) q[i] = __fmul_rn(f[i], r);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) q[i] = __fdiv_rn(f[i], scale);
-        }
-        uint2 c;
-        c.x = bs_cvt_e4m3x2(q[0], q[1]) | ((uint32_t)bs_cvt_e4m3x2(q[2], q[3]) << 16);
-        c.y = bs_cvt_e4m3x2(q[4], q[5]) | ((uint32_t)bs_cvt_e4m3x2(q[6], q[7]) << 16);
-        *reinterpret_cast<uint2*>(a.xq + g * 128 + l16 * 8) = c;
-        if (l16 == 0) a.xs[g] = bs_f32_to_e8m0(scale);
       }
     }
   }
@@ -320,12 +330,30 @@ __global__ void __launch_bounds__(kFrontThreads) front_kernel(FrontArgs a, Peers
       if (lane == 0) bs_set_error(BS_ERR_DEVICE_FAULT);
       continue;
     }
-    const uint4* src = reinterpret_cast<const uint4*>(a.xq + t * H);
-    uint4* dst = reinterpret_cast<uint4*>(pr.rows[d] + pos * H);
-#pragma unroll 4
-    for (int i = lane; i < H / 16; i += 32) dst[i] = __ldcg(src + i);
-    uint8_t* sp = pr.rows_sp[d];
-    for (int i = lane; i < nb; i += 32)
+    // the whole row (and its scale words) is loaded before any of it is
+    // stored: loads behind a store to a possibly aliasing address would
+    // otherwise wait for it, one L2 round trip per 16 bytes
+    const uint4* __restrict__ src = reinterpret_cast<const uint4*>(a.xq + t * H);
+    uint4* __restrict__ dst = reinterpret_cast<uint4*>(pr.rows[d] + pos * H);
+    uint8_t* __restrict__ sp = pr.rows_sp[d];
+    constexpr int kRowVec = 8;                                   // 16-byte vectors per lane per pass (H <= 4096)
+    for (int i0 = 0; i0 < H / 16; i0 += 32 * kRowVec) {
+      uint4 v[kRowVec];
+#pragma unroll
+      for (int u = 0; u < kRowVec; ++u) {
+        const int i = i0 + u * 32 + lane;
+        if (i < H / 16) v[u] = __ldcg(src + i);
+      }
+      const uint32_t sc = (i0 == 0 && lane < nb) ? 0x01010101u * __ldcg(a.xs + t * nb + lane) : 0u;
+#pragma unroll
+      for (int u = 0; u < kRowVec; ++u) {
+        const int i = i0 + u * 32 + lane;
+        if (i < H / 16) dst[i] = v[u];
+      }
+      if (i0 == 0 && lane < nb)
+        *reinterpret_cast<uint32_t*>(sp + (cg * nb + lane) * 512 + moe::sf_word_off(r)) = sc;
+    }
+    for (int i = 32 + lane; i < nb; i += 32)                    // H > 4096: the remaining scale words
       *reinterpret_cast<uint32_t*>(sp + (cg * nb + i) * 512 + moe::sf_word_off(r)) =
           0x01010101u * __ldcg(a.xs + t * nb + i);
     if (lane == 0) pr.ret[d][pos] = (me << 24) | (int)j;

@@ -30,7 +30,7 @@ def _free_port():
     return p
 
 
-def _problem(dev, T, H, I, E, seed, skew=False):
+def _problem(dev, T, H, I, E, seed, skew=False, topk=8):
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
     x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
@@ -60,7 +60,7 @@ def _worker(rank, world, port, q, T, H, I, E, topk, transport, skew):
     try:
         ep = importlib.import_module(PKG + ".ep")
         moe = importlib.import_module(PKG + ".moe")
-        x, logits, w13, w13_s, w2, w2_s = _problem(dev, T, H, I, E, 5, skew)
+        x, logits, w13, w13_s, w2, w2_s = _problem(dev, T, H, I, E, 5, skew, topk)
         e0, e1 = ep.expert_range(E, world, rank)
         W = moe.MoEWeights(w13[e0:e1], w13_s[e0:e1], w2[e0:e1], w2_s[e0:e1])
         tl = T // world
@@ -76,6 +76,9 @@ def _worker(rank, world, port, q, T, H, I, E, topk, transport, skew):
         importlib.import_module(PKG + "._lib").device_error_check()
         q.put((rank, res))
         dist.barrier()
+    except BaseException as exc:   # report at once instead of leaving the parent waiting
+        q.put((rank, {"error": repr(exc)}))
+        raise
     finally:
         if layer is not None and hasattr(layer, "close"):
             layer.close()
@@ -101,7 +104,11 @@ def test_ep_matches_single_gpu(T, H, I, E, topk, skew, transport, world):
              for r in range(world)]
     for p in procs:
         p.start()
-    res = dict(q.get(timeout=240) for _ in range(world))
+    res = {}
+    for _ in range(world):
+        r, v = q.get(timeout=240)
+        assert "error" not in v, (r, v.get("error"))
+        res[r] = v
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0

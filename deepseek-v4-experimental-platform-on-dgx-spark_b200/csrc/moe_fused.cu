@@ -93,12 +93,21 @@ BS_DEVINL void st_release_sys(unsigned long long* p, unsigned long long v) {
 // generic-proxy writes and async-proxy (TMA / bulk copy) reads of global memory
 BS_DEVINL void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
-// Bounded wait until *p >= target (acquire, system scope).
+BS_DEVINL unsigned long long ld_acquire_gpu_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait until *p >= target.  kSys: the counter is written by other
+// GPUs (acquire at system scope); otherwise by CTAs of this GPU (gpu scope).
+template <bool kSys>
 BS_DEVINL bool wait_geq(const unsigned long long* p, unsigned long long target) {
-  if (ld_acquire_sys(p) >= target) return true;
+  auto ld = [&] { return kSys ? ld_acquire_sys(p) : ld_acquire_gpu_u64(p); };
+  if (ld() >= target) return true;
   const unsigned long long t0 = gtimer_ns();
   for (;;) {
-    if (ld_acquire_sys(p) >= target) return true;
+    if (ld() >= target) return true;
     if (gtimer_ns() - t0 > kWaitNs) break;
     __nanosleep(32);
   }
@@ -261,12 +270,13 @@ __global__ void __launch_bounds__(kFrontThreads) front_kernel(FrontArgs a, Peers
     }
   }
 
-  // ---- grid barrier
-  __threadfence();
+  // ---- grid barrier (the CTA barrier orders every thread's writes before
+  // thread 0's fence and arrival, which are cumulative)
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence();
     atomicAdd(my_sync + kGridArrive, 1ull);
-    if (!wait_geq(my_sync + kGridArrive, ep * gridDim.x)) s_ok = 0;
+    if (!wait_geq<false>(my_sync + kGridArrive, ep * gridDim.x)) s_ok = 0;
   }
   __syncthreads();
   if (!s_ok) return;
@@ -278,11 +288,13 @@ __global__ void __launch_bounds__(kFrontThreads) front_kernel(FrontArgs a, Peers
     const int q = blockIdx.x;
     int* dst = pr.cnt_all[q] + (int64_t)me * E;
     for (int e = threadIdx.x; e < E; e += kFrontThreads) dst[e] = __ldcg(counts + e);
-    __threadfence_system();
     __syncthreads();
-    if (threadIdx.x == 0) st_release_sys(pr.sync[q] + kCntFlag + me, ep);
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      st_release_sys(pr.sync[q] + kCntFlag + me, ep);
+    }
   }
-  if (threadIdx.x < n && !wait_geq(my_sync + kCntFlag + threadIdx.x, ep)) s_ok = 0;
+  if (threadIdx.x < n && !wait_geq<true>(my_sync + kCntFlag + threadIdx.x, ep)) s_ok = 0;
   __syncthreads();
   if (!s_ok) return;
 
@@ -358,9 +370,11 @@ __global__ void __launch_bounds__(kFrontThreads) front_kernel(FrontArgs a, Peers
           0x01010101u * __ldcg(a.xs + t * nb + i);
     if (lane == 0) pr.ret[d][pos] = (me << 24) | (int)j;
   }
-  __threadfence_system();
   __syncthreads();
-  if (threadIdx.x < n) red_release_sys_add(pr.sync[threadIdx.x] + kRowsIn, 1ull);
+  if (threadIdx.x < n) {
+    __threadfence_system();
+    red_release_sys_add(pr.sync[threadIdx.x] + kRowsIn, 1ull);
+  }
 }
 
 struct ExpArgs {
@@ -465,7 +479,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     bool ok = true;
     if (lane == 0) {
       const unsigned long long ep = *reinterpret_cast<volatile unsigned long long*>(my_sync + kEpoch);
-      ok = wait_geq(my_sync + kRowsIn, ep * p.rows_per_epoch);   // every rank's rows are here
+      ok = wait_geq<true>(my_sync + kRowsIn, ep * p.rows_per_epoch);   // every rank's rows are here
       fence_proxy_async_global();
     }
     ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
@@ -627,11 +641,14 @@ __global__ void __launch_bounds__(C::kThreads, 1)
             }
           }
         } else {
+          // the 16 rows' return addresses: one load per lane, before any
+          // store (a load behind a store to a possibly aliasing address
+          // would wait for it), then broadcast
+          const int my_rr = (lane < 16 && c0 + lane < cnt) ? __ldcg(p.ret + row0 + c0 + lane) : 0;
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            const int tok = c0 + j;
-            if (tok < cnt) {
-              const int rr = __ldcg(p.ret + row0 + tok);
+            const int rr = __shfl_sync(0xffffffffu, my_rr, j);
+            if (c0 + j < cnt) {
               __nv_bfloat16* yrow = pr.y_back[rr >> 24] + (int64_t)(rr & 0xFFFFFF) * p.H + nt * 256;
               yrow[f] = __float2bfloat16_rn(__uint_as_float(g[j]));
               yrow[128 + f] = __float2bfloat16_rn(__uint_as_float(u[j]));
@@ -644,24 +661,30 @@ __global__ void __launch_bounds__(C::kThreads, 1)
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
       if (!w2) {
         // this warp's part of the W1|W3 tile of chunk cg is stored: count it
-        // for the W2 items (kEpiWarps counts per tile)
-        __threadfence();
-        fence_proxy_async_global();
+        // for the W2 items (kEpiWarps counts per tile).  __syncwarp orders
+        // the lanes' stores before lane 0's fence and release, which are
+        // cumulative; the consumer orders them before its TMA loads with a
+        // proxy fence after its acquire.
         __syncwarp();
-        if (lane == 0) red_release_gpu_add(p.h_done + cg, 1);
+        if (lane == 0) {
+          __threadfence();
+          red_release_gpu_add(p.h_done + cg, 1);
+        }
       }
     }
   }
 
   tc_fence_before();
-  __threadfence_system();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::kTmemCols);
   }
   // this CTA's output rows are at their source ranks
-  if (threadIdx.x < p.n) red_release_sys_add(pr.sync[threadIdx.x] + kRetIn, 1ull);
+  if (threadIdx.x < p.n) {
+    __threadfence_system();
+    red_release_sys_add(pr.sync[threadIdx.x] + kRetIn, 1ull);
+  }
 }
 
 // out[t] = bf16(sum_k w[t,k] * y_back[t*topk + k]), fp32 in slot order; waits
@@ -673,7 +696,7 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ y, const float*
   __shared__ int s_ok;
   if (threadIdx.x == 0) {
     const unsigned long long ep = *reinterpret_cast<volatile unsigned long long*>(my_sync + kEpoch);
-    s_ok = wait_geq(my_sync + kRetIn, ep * ret_per_epoch) ? 1 : 0;
+    s_ok = wait_geq<true>(my_sync + kRetIn, ep * ret_per_epoch) ? 1 : 0;
   }
   __syncthreads();
   if (!s_ok) return;

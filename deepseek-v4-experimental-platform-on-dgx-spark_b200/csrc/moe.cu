@@ -45,10 +45,10 @@ constexpr int kTok = 112;
 // Top-k of one token's E gate logits by one warp (every lane calls it with
 // the same row).  Ties keep the lower expert index (a stable sort of
 // -logits); NaN logits rank below every number.  kMaxPer logits per lane
-// (E <= 32 * kMaxPer).  sel_v / sel_e (valid on every lane) hold the k
-// selected logits and experts in descending order.
+// (E <= 32 * kMaxPer).  Lane k < topk returns the k-th selection (descending)
+// in my_v / my_e; lane 0 also returns the largest logit in m.
 template <int kMaxPer>
-BS_DEVINL void route_one(const float* __restrict__ row, int E, int topk, int lane, float* sel_v, int* sel_e) {
+BS_DEVINL void route_one(const float* __restrict__ row, int E, int topk, int lane, float& my_v, int& my_e) {
   float v[kMaxPer];
   const int per = (E + 31) / 32;
 #pragma unroll
@@ -57,6 +57,8 @@ BS_DEVINL void route_one(const float* __restrict__ row, int E, int topk, int lan
     v[i] = (i < per && e < E) ? row[e] : -INFINITY;
     if (v[i] != v[i]) v[i] = -INFINITY;
   }
+  my_v = -INFINITY;
+  my_e = 0;
   for (int k = 0; k < topk; ++k) {
     float bv = -INFINITY;
     int be = 0x7fffffff;
@@ -70,8 +72,7 @@ BS_DEVINL void route_one(const float* __restrict__ row, int E, int topk, int lan
       const int oe = __shfl_xor_sync(0xffffffffu, be, o);
       if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; }
     }
-    sel_v[k] = bv;
-    sel_e[k] = be;
+    if (lane == k) { my_v = bv; my_e = be; }
     if ((be & 31) == lane) {
 #pragma unroll
       for (int i = 0; i < kMaxPer; ++i)
@@ -80,31 +81,33 @@ BS_DEVINL void route_one(const float* __restrict__ row, int E, int topk, int lan
   }
 }
 
-// Softmax over the k selected logits (fp32, in slot order).
-BS_DEVINL float route_weight(const float* sel_v, int topk, int k) {
-  const float m = sel_v[0];
+// Softmax over the k selected logits, fp32: lane k gets exp(v_k - v_0)
+// divided by the sum of those terms taken in slot order (every lane forms
+// the same sum).
+BS_DEVINL float route_weight(float my_v, int topk, int lane) {
+  const float m = __shfl_sync(0xffffffffu, my_v, 0);
+  const float ex = lane < topk ? expf(my_v - m) : 0.0f;
   float den = 0.f;
-  for (int j = 0; j < topk; ++j) den += expf(sel_v[j] - m);
-  return expf(sel_v[k] - m) / den;
+  for (int j = 0; j < topk; ++j) den += __shfl_sync(0xffffffffu, ex, j);
+  return ex / den;
 }
 
 // One warp per token: top-k experts, their softmax weights, and the expert
-// histogram.
+// histogram (lane k writes slot k).
 template <int kMaxPer>
 __global__ void route_kernel(const float* __restrict__ logits, int T, int E, int topk, int* __restrict__ idx,
                              float* __restrict__ w, int* __restrict__ counts) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= T) return;
-  float sel_v[8];
-  int sel_e[8];
-  route_one<kMaxPer>(logits + (int64_t)warp * E, E, topk, lane, sel_v, sel_e);
-  if (lane == 0) {
-    for (int k = 0; k < topk; ++k) {
-      idx[(int64_t)warp * topk + k] = sel_e[k];
-      w[(int64_t)warp * topk + k] = route_weight(sel_v, topk, k);
-      atomicAdd(&counts[sel_e[k]], 1);
-    }
+  float my_v;
+  int my_e;
+  route_one<kMaxPer>(logits + (int64_t)warp * E, E, topk, lane, my_v, my_e);
+  const float wk = route_weight(my_v, topk, lane);
+  if (lane < topk) {
+    idx[(int64_t)warp * topk + lane] = my_e;
+    w[(int64_t)warp * topk + lane] = wk;
+    atomicAdd(&counts[my_e], 1);
   }
 }
 

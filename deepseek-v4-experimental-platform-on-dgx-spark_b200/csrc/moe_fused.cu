@@ -172,6 +172,7 @@ struct FrontArgs {
   int* offsets;               // [El + 1] this rank's experts (owner side)
   int* chunk_prefix;          // [El + 1]
   int* h_done;                // [chunk_cap] zeroed here for the experts kernel
+  int* sched;                 // the experts kernel's work-item counter, zeroed here
 };
 
 // Dynamic shared memory: 3 * E + 2 ints (plan).
@@ -204,6 +205,7 @@ __global__ void __launch_bounds__(kFrontThreads) front_kernel(FrontArgs a, Peers
     a.cursor[(par ^ 1) * a.E + i] = 0;
   }
   for (int64_t i = gtid; i < a.chunk_cap; i += nthreads) a.h_done[i] = 0;
+  if (gtid == 0) *a.sched = 0;
 
   // ---- A: quantise (half a warp per 1x128 block, power-of-two scales);
   // each half warp issues the loads of kQ blocks before quantising any
@@ -258,15 +260,14 @@ __global__ void __launch_bounds__(kFrontThreads) front_kernel(FrontArgs a, Peers
 
   // ---- A: routing (one warp per token)
   for (int64_t t = gwarp; t < a.T; t += nwarps) {
-    float sel_v[8];
-    int sel_e[8];
-    moe::route_one<kMaxPer>(a.logits + t * a.E, a.E, a.topk, lane, sel_v, sel_e);
-    if (lane == 0) {
-      for (int k = 0; k < a.topk; ++k) {
-        a.idx[t * a.topk + k] = sel_e[k];
-        a.w[t * a.topk + k] = moe::route_weight(sel_v, a.topk, k);
-        atomicAdd(&counts[sel_e[k]], 1);
-      }
+    float my_v;
+    int my_e;
+    moe::route_one<kMaxPer>(a.logits + t * a.E, a.E, a.topk, lane, my_v, my_e);
+    const float wk = moe::route_weight(my_v, a.topk, lane);
+    if (lane < a.topk) {
+      a.idx[t * a.topk + lane] = my_e;
+      a.w[t * a.topk + lane] = wk;
+      atomicAdd(&counts[my_e], 1);
     }
   }
 
@@ -389,10 +390,13 @@ struct ExpArgs {
   uint8_t* hq;                // [cap, I] e4m3 hidden rows
   uint8_t* hs_p;              // [chunk][I/128][512]
   int* h_done;                // [chunk] W1|W3 tile parts stored per token chunk (kEpiWarps per tile)
+  int* sched;                 // next work item to hand out (zero before the launch)
   unsigned long long rows_per_epoch;   // n * front CTAs
 };
 
 using C = moe::Cfg<moe::kModeW13>;   // W2 pair items use the same stage and TMEM layout
+constexpr int kItemRing = 8;          // work items handed from the producer to the MMA and epilogue warps
+constexpr int kExpSmemBytes = C::kSmemBytes + 256;
 static_assert(moe::Cfg<moe::kModeW13>::kStageBytes == moe::Cfg<moe::kModeW2Pair>::kStageBytes, "stage layouts");
 static_assert(moe::Cfg<moe::kModeW13>::kAccCols == moe::Cfg<moe::kModeW2Pair>::kAccCols, "accumulator layouts");
 
@@ -413,6 +417,9 @@ __global__ void __launch_bounds__(C::kThreads, 1)
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* item_full = acc_empty + 4;                // after tmem_slot and abort_flag
+  uint64_t* item_empty = item_full + kItemRing;
+  volatile int* s_items = reinterpret_cast<volatile int*>(item_empty + kItemRing);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int E = p.E;
@@ -428,6 +435,10 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], C::kEpiWarps);
+    }
+    for (int r = 0; r < kItemRing; ++r) {
+      mbar_init(&item_full[r], 1);
+      mbar_init(&item_empty[r], 1 + C::kEpiWarps);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -486,7 +497,22 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     if (!ok) *abort_flag = 1;
     int it = 0;
     const int w13_tiles = 2 * p.I / 128, w2_tiles = p.H / 128;
-    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+    // Items are handed out from one counter in list order (all W1|W3 items
+    // before any W2 item), so the CTA that finishes first takes the next
+    // item; every W1|W3 item is taken by a resident CTA and needs nothing
+    // but its own pipeline, so the W2 items' waits always end.
+    for (int k = 0;; ++k) {
+      const int slot = k % kItemRing;
+      if (!__all_sync(0xffffffffu, mbar_wait(&item_empty[slot], ((k / kItemRing) & 1) ^ 1, abort_flag))) break;
+      int item = -1;
+      if (lane == 0) {
+        item = ok ? atomicAdd(p.sched, 1) : -1;
+        if (item >= n_items) item = -1;
+        s_items[slot] = item;
+        mbar_arrive(&item_full[slot]);
+      }
+      item = __shfl_sync(0xffffffffu, item, 0);
+      if (item < 0) break;
       bool w2;
       int e, row0, cnt, nt, cg;
       decode(item, w2, e, row0, cnt, nt, cg);
@@ -544,9 +570,15 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     constexpr uint64_t kSfStep = (uint64_t)(C::kSfBytes >> 4);
     constexpr uint64_t kYOff = (uint64_t)(C::kXBytes >> 4);
     const uint32_t sf_tmem0 = tmem_base + C::kSfCol0;
-    int it = 0, acc_it = 0;
+    int it = 0;
     bool ok = true;
-    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++acc_it) {
+    for (int acc_it = 0; ok; ++acc_it) {
+      const int slot = acc_it % kItemRing;
+      if (!__all_sync(0xffffffffu, mbar_wait(&item_full[slot], (acc_it / kItemRing) & 1, abort_flag))) break;
+      const int item = s_items[slot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&item_empty[slot]);
+      if (item < 0) break;
       bool w2;
       int e, row0, cnt, nt, cg;
       decode(item, w2, e, row0, cnt, nt, cg);
@@ -595,8 +627,13 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     const int quad = warp & 3;
     const int set = (warp - 2) >> 2;
     const int f = quad * 32 + lane;
-    int acc_it = 0;
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++acc_it) {
+    for (int acc_it = 0;; ++acc_it) {
+      const int slot = acc_it % kItemRing;
+      if (!__all_sync(0xffffffffu, mbar_wait(&item_full[slot], (acc_it / kItemRing) & 1, abort_flag))) break;
+      const int item = s_items[slot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&item_empty[slot]);
+      if (item < 0) break;
       bool w2;
       int e, row0, cnt, nt, cg;
       decode(item, w2, e, row0, cnt, nt, cg);
@@ -793,13 +830,13 @@ cudaError_t run_layer(const Layer& L, cudaStream_t st, int* status) {
   }
   static int attr_slots[hostcache::kMaxDevices];
   e = (cudaError_t)hostcache::get(attr_slots, [&] {
-    return (int)cudaFuncSetAttribute(experts_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    return (int)cudaFuncSetAttribute(experts_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kExpSmemBytes);
   });
   if (e != cudaSuccess) return e;
   ExpArgs xa = L.x;
   xa.rows_per_epoch = (unsigned long long)L.f.n * G;
   if (t_ev_begin) cudaEventRecord(t_ev_begin, st);
-  e = launch_coop(experts_kernel, G, C::kThreads, (size_t)C::kSmemBytes, st, mw13, ma, mw2, mh, xa, L.pr);
+  e = launch_coop(experts_kernel, G, C::kThreads, (size_t)kExpSmemBytes, st, mw13, ma, mw2, mh, xa, L.pr);
   if (t_ev_end) cudaEventRecord(t_ev_end, st);
   t_ev_begin = t_ev_end = nullptr;
   if (e != cudaSuccess) return e;

@@ -501,15 +501,18 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     // before any W2 item), so the CTA that finishes first takes the next
     // item; every W1|W3 item is taken by a resident CTA and needs nothing
     // but its own pipeline, so the W2 items' waits always end.
+    // the next item is fetched one ahead, so its round trip overlaps the
+    // current item's loads
+    int next = (lane == 0 && ok) ? atomicAdd(p.sched, 1) : -1;
     for (int k = 0;; ++k) {
       const int slot = k % kItemRing;
       if (!__all_sync(0xffffffffu, mbar_wait(&item_empty[slot], ((k / kItemRing) & 1) ^ 1, abort_flag))) break;
       int item = -1;
       if (lane == 0) {
-        item = ok ? atomicAdd(p.sched, 1) : -1;
-        if (item >= n_items) item = -1;
+        item = (ok && next < n_items) ? next : -1;
         s_items[slot] = item;
         mbar_arrive(&item_full[slot]);
+        if (item >= 0) next = atomicAdd(p.sched, 1);
       }
       item = __shfl_sync(0xffffffffu, item, 0);
       if (item < 0) break;
@@ -518,37 +521,20 @@ __global__ void __launch_bounds__(C::kThreads, 1)
       decode(item, w2, e, row0, cnt, nt, cg);
       const int nbox = (cnt + 31) / 32;
       const int nkb = (w2 ? p.I : p.H) / 128;
-      if (w2) {
-        // the hidden rows of this chunk: every W1|W3 tile of it has been stored
-        int done = 1;
-        if (lane == 0) {
-          done = 0;
-          const int need = nt13 * C::kEpiWarps;
-          if (ld_acquire_gpu(p.h_done + cg) >= need) done = 1;
-          const unsigned long long t0 = gtimer_ns();
-          while (!done && !*abort_flag) {
-            if (ld_acquire_gpu(p.h_done + cg) >= need) done = 1;
-            else if (gtimer_ns() - t0 > kWaitNs) break;
-            else __nanosleep(64);
-          }
-          if (!done && !*abort_flag) bs_set_error(BS_ERR_DEVICE_TIMEOUT);
-          fence_proxy_async_global();
-        }
-        if (!__shfl_sync(0xffffffffu, done, 0)) { *abort_flag = 1; ok = false; break; }
-      }
       const CUtensorMap* mw = w2 ? &tm_w2 : &tm_w13;
       const CUtensorMap* ma = w2 ? &tm_h : &tm_a;
       const uint8_t* wsp = w2 ? p.w2_sp : p.w13_sp;
       const uint8_t* asp = w2 ? p.hs_p : p.a_sp;
       const int wt = w2 ? w2_tiles : w13_tiles;
+      bool rows_ready = !w2;   // a W2 item's token rows are the hidden rows of its chunk
       for (int kb = 0; kb < nkb; ++kb, ++it) {
         const int s = it % C::kStages;
         const uint32_t ph = (it / C::kStages) & 1;
         if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1, abort_flag))) { ok = false; break; }
+        uint8_t* sx = stage_base + s * C::kStageBytes;
+        uint8_t* sy = sx + C::kXBytes;
+        uint8_t* sf = sf_base + s * C::kSfBytes;
         if (elect_one()) {
-          uint8_t* sx = stage_base + s * C::kStageBytes;
-          uint8_t* sy = sx + C::kXBytes;
-          uint8_t* sf = sf_base + s * C::kSfBytes;
           mbar_arrive_expect_tx(&full[s], 2 * (8192 + 512) + nbox * 32 * 128 + 512);
 #pragma unroll
           for (int t = 0; t < 2; ++t) {
@@ -556,11 +542,34 @@ __global__ void __launch_bounds__(C::kThreads, 1)
             tma_load_3d(sx + t * 16384, mw, &full[s], kb * 128, wr0, e);
             bulk_load(sf + t * 512, wsp + (((int64_t)e * wt + wr0 / 128) * nkb + kb) * 512, 512, &full[s]);
           }
+        }
+        __syncwarp();
+        if (!rows_ready) {
+          // every W1|W3 tile of this chunk has been stored (waited for after
+          // the first weight loads are on their way)
+          int done = 0;
+          if (lane == 0) {
+            const int need = nt13 * C::kEpiWarps;
+            if (ld_acquire_gpu(p.h_done + cg) >= need) done = 1;
+            const unsigned long long t0 = gtimer_ns();
+            while (!done && !*abort_flag) {
+              if (ld_acquire_gpu(p.h_done + cg) >= need) done = 1;
+              else if (gtimer_ns() - t0 > kWaitNs) break;
+              else __nanosleep(64);
+            }
+            if (!done && !*abort_flag) bs_set_error(BS_ERR_DEVICE_TIMEOUT);
+            fence_proxy_async_global();
+          }
+          if (!__shfl_sync(0xffffffffu, done, 0)) { *abort_flag = 1; ok = false; break; }
+          rows_ready = true;
+        }
+        if (elect_one()) {
           for (int b = 0; b < nbox; ++b) tma_load_2d(sy + b * 32 * 128, ma, &full[s], kb * 128, row0 + b * 32);
           bulk_load(sf + 2 * 512, asp + ((int64_t)cg * nkb + kb) * 512, 512, &full[s]);
         }
         __syncwarp();
       }
+      if (!ok) break;
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer

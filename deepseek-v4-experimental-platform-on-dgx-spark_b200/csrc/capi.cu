@@ -312,7 +312,7 @@ FusedLayout fused_layout(int64_t T_max, int H, int I, int E, int topk, int n_ran
   L.chunks = take(4 * (size_t)(El + 1));
   L.hq = take((size_t)L.cap * I);
   L.hsp = take((size_t)L.chunk_cap * (I / 128) * 512);
-  L.hdone = take(4 * (size_t)L.chunk_cap + 4);     // + the experts kernel's item counter
+  L.hdone = take(4 * (size_t)L.chunk_cap);
   if (!local_only) {
     L.rows = take((size_t)L.cap * H);
     L.rows_sp = take((size_t)L.chunk_cap * (H / 128) * 512);
@@ -372,12 +372,11 @@ static int moe_forward_fused(const void* x, const float* logits, int64_t T, int 
   f.xq = ws + L.xq; f.xs = ws + L.xs; f.idx = (int*)(ws + L.idx); f.w = (float*)(ws + L.w);
   f.counts = (int*)(ws + L.counts); f.cursor = (int*)(ws + L.cursor);
   f.offsets = (int*)(ws + L.offsets); f.chunk_prefix = (int*)(ws + L.chunks); f.h_done = (int*)(ws + L.hdone);
-  f.sched = f.h_done + L.chunk_cap;
   mf::ExpArgs& xa = ly.x;
   xa.E = E; xa.H = H; xa.I = I; xa.n = 1; xa.me = 0; xa.cap = L.cap;
   xa.offsets = f.offsets; xa.chunk_prefix = f.chunk_prefix; xa.a_sp = ws + L.rows_sp; xa.ret = (const int*)(ws + L.ret);
   xa.w13_sp = (const uint8_t*)w13_sp; xa.w2_sp = (const uint8_t*)w2_sp;
-  xa.hq = ws + L.hq; xa.hs_p = ws + L.hsp; xa.h_done = f.h_done; xa.sched = f.sched;
+  xa.hq = ws + L.hq; xa.hs_p = ws + L.hsp; xa.h_done = f.h_done;
   ly.pr.cnt_all[0] = (int*)(ws + L.cnt_all); ly.pr.rows[0] = ws + L.rows; ly.pr.rows_sp[0] = ws + L.rows_sp;
   ly.pr.ret[0] = (int*)(ws + L.ret); ly.pr.y_back[0] = (__nv_bfloat16*)(ws + L.y_back);
   ly.pr.sync[0] = (unsigned long long*)(ws + L.sync);
@@ -523,7 +522,6 @@ int bs_ep_moe_forward(const void* x, const float* logits, int64_t T, int64_t max
   f.xq = ws + L.xq; f.xs = ws + L.xs; f.idx = (int*)(ws + L.idx); f.w = (float*)(ws + L.w);
   f.counts = (int*)(ws + L.counts); f.cursor = (int*)(ws + L.cursor);
   f.offsets = (int*)(ws + L.offsets); f.chunk_prefix = (int*)(ws + L.chunks); f.h_done = (int*)(ws + L.hdone);
-  f.sched = f.h_done + L.chunk_cap;
   for (int q = 0; q < n_ranks; ++q) {
     ly.pr.cnt_all[q] = (int*)peer_bufs[0 * n_ranks + q];
     ly.pr.rows[q] = (uint8_t*)peer_bufs[1 * n_ranks + q];
@@ -536,7 +534,7 @@ int bs_ep_moe_forward(const void* x, const float* logits, int64_t T, int64_t max
   xa.E = El; xa.H = H; xa.I = I; xa.n = n_ranks; xa.me = rank; xa.cap = L.cap;
   xa.offsets = f.offsets; xa.chunk_prefix = f.chunk_prefix; xa.a_sp = ly.pr.rows_sp[rank]; xa.ret = ly.pr.ret[rank];
   xa.w13_sp = (const uint8_t*)w13_sp; xa.w2_sp = (const uint8_t*)w2_sp;
-  xa.hq = ws + L.hq; xa.hs_p = ws + L.hsp; xa.h_done = f.h_done; xa.sched = f.sched;
+  xa.hq = ws + L.hq; xa.hs_p = ws + L.hsp; xa.h_done = f.h_done;
   ly.w13 = w13; ly.w2 = w2; ly.out = (__nv_bfloat16*)out; ly.wts = f.w;
   int status = 0;
   cudaError_t e = mf::run_layer(ly, (cudaStream_t)stream, &status);

@@ -21,8 +21,11 @@
 //            rank's front CTAs have arrived, then runs W1|W3 work items
 //            (gate + up tiles, fused SwiGLU + e4m3 quantisation of the
 //            hidden rows) and W2 work items (two 128-row output tiles) from
-//            one static list; a W2 item waits until all W1|W3 items of its
-//            token chunk are done (per-chunk counters), and its epilogue
+//            one static list (W2 items of an expert placed a fixed lag of
+//            experts after its W1|W3 items); a W2 item waits until all W1|W3
+//            items of its token chunk are done (per-chunk counters: they
+//            come earlier in the list, and each CTA runs its items in list
+//            order, so every wait ends), and its epilogue
 //            stores each output row into the source rank's return buffer;
 //            each CTA then adds 1 to every rank's returns-arrived counter
 //   combine  waits for every rank's experts CTAs, then
@@ -172,7 +175,6 @@ struct FrontArgs {
   int* offsets;               // [El + 1] this rank's experts (owner side)
   int* chunk_prefix;          // [El + 1]
   int* h_done;                // [chunk_cap] zeroed here for the experts kernel
-  int* sched;                 // the experts kernel's work-item counter, zeroed here
 };
 
 // Dynamic shared memory: 3 * E + 2 ints (plan).
@@ -205,7 +207,6 @@ __global__ void __launch_bounds__(kFrontThreads) front_kernel(FrontArgs a, Peers
     a.cursor[(par ^ 1) * a.E + i] = 0;
   }
   for (int64_t i = gtid; i < a.chunk_cap; i += nthreads) a.h_done[i] = 0;
-  if (gtid == 0) *a.sched = 0;
 
   // ---- A: quantise (half a warp per 1x128 block, power-of-two scales);
   // each half warp issues the loads of kQ blocks before quantising any
@@ -390,13 +391,11 @@ struct ExpArgs {
   uint8_t* hq;                // [cap, I] e4m3 hidden rows
   uint8_t* hs_p;              // [chunk][I/128][512]
   int* h_done;                // [chunk] W1|W3 tile parts stored per token chunk (kEpiWarps per tile)
-  int* sched;                 // next work item to hand out (zero before the launch)
+  int lag;                    // experts between an expert's W1|W3 items and its W2 items in the item list
   unsigned long long rows_per_epoch;   // n * front CTAs
 };
 
 using C = moe::Cfg<moe::kModeW13>;   // W2 pair items use the same stage and TMEM layout
-constexpr int kItemRing = 8;          // work items handed from the producer to the MMA and epilogue warps
-constexpr int kExpSmemBytes = C::kSmemBytes + 256;
 static_assert(moe::Cfg<moe::kModeW13>::kStageBytes == moe::Cfg<moe::kModeW2Pair>::kStageBytes, "stage layouts");
 static_assert(moe::Cfg<moe::kModeW13>::kAccCols == moe::Cfg<moe::kModeW2Pair>::kAccCols, "accumulator layouts");
 
@@ -417,9 +416,6 @@ __global__ void __launch_bounds__(C::kThreads, 1)
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  uint64_t* item_full = acc_empty + 4;                // after tmem_slot and abort_flag
-  uint64_t* item_empty = item_full + kItemRing;
-  volatile int* s_items = reinterpret_cast<volatile int*>(item_empty + kItemRing);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int E = p.E;
@@ -435,10 +431,6 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], C::kEpiWarps);
-    }
-    for (int r = 0; r < kItemRing; ++r) {
-      mbar_init(&item_full[r], 1);
-      mbar_init(&item_empty[r], 1 + C::kEpiWarps);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -458,25 +450,35 @@ __global__ void __launch_bounds__(C::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int nt13 = p.I / 128, nt2 = p.H / 256;
-  const int n13 = s_chunk[E] * nt13;
-  const int n_items = n13 + s_chunk[E] * nt2;
+  const int n_items = s_chunk[E] * (nt13 + nt2);
   unsigned long long* my_sync = pr.sync[p.me];
 
-  // item -> (W2?, expert, first row, rows, output tile, global chunk).  Inside
-  // an expert, items run tile-major: consecutive items stream the same weight
-  // tile(s) for the expert's successive token chunks.
+  // The item list, in expert slots j = 0 .. E+lag-1: the W1|W3 items of
+  // expert j (j < E), then the W2 items of expert j - lag (j >= lag), so an
+  // expert's W2 items come about `lag` experts' worth of W1|W3 work after its
+  // own W1|W3 items, and the W2 work interleaves with the W1|W3 work instead
+  // of all waiting for its end.  Inside an expert, items run tile-major:
+  // consecutive items stream the same weight tile(s) for the expert's
+  // successive token chunks.
+  // item -> (W2?, expert, first row, rows, output tile, global chunk)
+  const int L = p.lag;
+  auto slot_off = [&](int j) {   // items before expert slot j
+    const int a13 = j < E ? j : E;
+    const int a2 = j - L < 0 ? 0 : (j - L < E ? j - L : E);
+    return s_chunk[a13] * nt13 + s_chunk[a2] * nt2;
+  };
   auto decode = [&](int item, bool& w2, int& e, int& row0, int& cnt, int& nt, int& cg) {
-    w2 = item >= n13;
-    const int li = w2 ? item - n13 : item;
-    const int ntiles = w2 ? nt2 : nt13;
-    int lo = 0, hi = E;  // largest e with s_chunk[e] * ntiles <= li
+    int lo = 0, hi = E + L;  // largest slot j with slot_off(j) <= item
     while (hi - lo > 1) {
       const int mid = (lo + hi) >> 1;
-      if (s_chunk[mid] * ntiles <= li) lo = mid; else hi = mid;
+      if (slot_off(mid) <= item) lo = mid; else hi = mid;
     }
-    e = lo;
+    int local = item - slot_off(lo);
+    const int n13_j = lo < E ? (s_chunk[lo + 1] - s_chunk[lo]) * nt13 : 0;
+    w2 = local >= n13_j;
+    if (w2) local -= n13_j;
+    e = w2 ? lo - L : lo;
     const int ch = s_chunk[e + 1] - s_chunk[e];
-    const int local = li - s_chunk[e] * ntiles;
     nt = local / ch;
     const int c = local - nt * ch;
     cg = s_chunk[e] + c;
@@ -497,25 +499,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     if (!ok) *abort_flag = 1;
     int it = 0;
     const int w13_tiles = 2 * p.I / 128, w2_tiles = p.H / 128;
-    // Items are handed out from one counter in list order (all W1|W3 items
-    // before any W2 item), so the CTA that finishes first takes the next
-    // item; every W1|W3 item is taken by a resident CTA and needs nothing
-    // but its own pipeline, so the W2 items' waits always end.
-    // the next item is fetched one ahead, so its round trip overlaps the
-    // current item's loads
-    int next = (lane == 0 && ok) ? atomicAdd(p.sched, 1) : -1;
-    for (int k = 0;; ++k) {
-      const int slot = k % kItemRing;
-      if (!__all_sync(0xffffffffu, mbar_wait(&item_empty[slot], ((k / kItemRing) & 1) ^ 1, abort_flag))) break;
-      int item = -1;
-      if (lane == 0) {
-        item = (ok && next < n_items) ? next : -1;
-        s_items[slot] = item;
-        mbar_arrive(&item_full[slot]);
-        if (item >= 0) next = atomicAdd(p.sched, 1);
-      }
-      item = __shfl_sync(0xffffffffu, item, 0);
-      if (item < 0) break;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
       bool w2;
       int e, row0, cnt, nt, cg;
       decode(item, w2, e, row0, cnt, nt, cg);
@@ -569,7 +553,6 @@ __global__ void __launch_bounds__(C::kThreads, 1)
         }
         __syncwarp();
       }
-      if (!ok) break;
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -579,15 +562,9 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     constexpr uint64_t kSfStep = (uint64_t)(C::kSfBytes >> 4);
     constexpr uint64_t kYOff = (uint64_t)(C::kXBytes >> 4);
     const uint32_t sf_tmem0 = tmem_base + C::kSfCol0;
-    int it = 0;
+    int it = 0, acc_it = 0;
     bool ok = true;
-    for (int acc_it = 0; ok; ++acc_it) {
-      const int slot = acc_it % kItemRing;
-      if (!__all_sync(0xffffffffu, mbar_wait(&item_full[slot], (acc_it / kItemRing) & 1, abort_flag))) break;
-      const int item = s_items[slot];
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&item_empty[slot]);
-      if (item < 0) break;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++acc_it) {
       bool w2;
       int e, row0, cnt, nt, cg;
       decode(item, w2, e, row0, cnt, nt, cg);
@@ -636,13 +613,8 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     const int quad = warp & 3;
     const int set = (warp - 2) >> 2;
     const int f = quad * 32 + lane;
-    for (int acc_it = 0;; ++acc_it) {
-      const int slot = acc_it % kItemRing;
-      if (!__all_sync(0xffffffffu, mbar_wait(&item_full[slot], (acc_it / kItemRing) & 1, abort_flag))) break;
-      const int item = s_items[slot];
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&item_empty[slot]);
-      if (item < 0) break;
+    int acc_it = 0;
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++acc_it) {
       bool w2;
       int e, row0, cnt, nt, cg;
       decode(item, w2, e, row0, cnt, nt, cg);
@@ -839,13 +811,19 @@ cudaError_t run_layer(const Layer& L, cudaStream_t st, int* status) {
   }
   static int attr_slots[hostcache::kMaxDevices];
   e = (cudaError_t)hostcache::get(attr_slots, [&] {
-    return (int)cudaFuncSetAttribute(experts_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kExpSmemBytes);
+    return (int)cudaFuncSetAttribute(experts_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
   });
   if (e != cudaSuccess) return e;
   ExpArgs xa = L.x;
   xa.rows_per_epoch = (unsigned long long)L.f.n * G;
+  // about two rounds of W1|W3 items (one chunk per expert) between an
+  // expert's W1|W3 and W2 items
+  const int nt13 = xa.I / 128;
+  xa.lag = (2 * G + nt13 - 1) / nt13;
+  if (xa.lag > El) xa.lag = El;
+  if (xa.lag < 1) xa.lag = 1;
   if (t_ev_begin) cudaEventRecord(t_ev_begin, st);
-  e = launch_coop(experts_kernel, G, C::kThreads, (size_t)kExpSmemBytes, st, mw13, ma, mw2, mh, xa, L.pr);
+  e = launch_coop(experts_kernel, G, C::kThreads, (size_t)C::kSmemBytes, st, mw13, ma, mw2, mh, xa, L.pr);
   if (t_ev_end) cudaEventRecord(t_ev_end, st);
   t_ev_begin = t_ev_end = nullptr;
   if (e != cudaSuccess) return e;

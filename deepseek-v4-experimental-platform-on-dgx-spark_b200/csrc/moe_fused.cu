@@ -21,11 +21,8 @@
 //            rank's front CTAs have arrived, then runs W1|W3 work items
 //            (gate + up tiles, fused SwiGLU + e4m3 quantisation of the
 //            hidden rows) and W2 work items (two 128-row output tiles) from
-//            one static list (W2 items of an expert placed a fixed lag of
-//            experts after its W1|W3 items); a W2 item waits until all W1|W3
-//            items of its token chunk are done (per-chunk counters: they
-//            come earlier in the list, and each CTA runs its items in list
-//            order, so every wait ends), and its epilogue
+//            one static list; a W2 item waits until all W1|W3 items of its
+//            token chunk are done (per-chunk counters), and its epilogue
 //            stores each output row into the source rank's return buffer;
 //            each CTA then adds 1 to every rank's returns-arrived counter
 //   combine  waits for every rank's experts CTAs, then
@@ -391,7 +388,6 @@ struct ExpArgs {
   uint8_t* hq;                // [cap, I] e4m3 hidden rows
   uint8_t* hs_p;              // [chunk][I/128][512]
   int* h_done;                // [chunk] W1|W3 tile parts stored per token chunk (kEpiWarps per tile)
-  int lag;                    // experts between an expert's W1|W3 items and its W2 items in the item list
   unsigned long long rows_per_epoch;   // n * front CTAs
 };
 
@@ -450,35 +446,25 @@ __global__ void __launch_bounds__(C::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int nt13 = p.I / 128, nt2 = p.H / 256;
-  const int n_items = s_chunk[E] * (nt13 + nt2);
+  const int n13 = s_chunk[E] * nt13;
+  const int n_items = n13 + s_chunk[E] * nt2;
   unsigned long long* my_sync = pr.sync[p.me];
 
-  // The item list, in expert slots j = 0 .. E+lag-1: the W1|W3 items of
-  // expert j (j < E), then the W2 items of expert j - lag (j >= lag), so an
-  // expert's W2 items come about `lag` experts' worth of W1|W3 work after its
-  // own W1|W3 items, and the W2 work interleaves with the W1|W3 work instead
-  // of all waiting for its end.  Inside an expert, items run tile-major:
-  // consecutive items stream the same weight tile(s) for the expert's
-  // successive token chunks.
-  // item -> (W2?, expert, first row, rows, output tile, global chunk)
-  const int L = p.lag;
-  auto slot_off = [&](int j) {   // items before expert slot j
-    const int a13 = j < E ? j : E;
-    const int a2 = j - L < 0 ? 0 : (j - L < E ? j - L : E);
-    return s_chunk[a13] * nt13 + s_chunk[a2] * nt2;
-  };
+  // item -> (W2?, expert, first row, rows, output tile, global chunk).  Inside
+  // an expert, items run tile-major: consecutive items stream the same weight
+  // tile(s) for the expert's successive token chunks.
   auto decode = [&](int item, bool& w2, int& e, int& row0, int& cnt, int& nt, int& cg) {
-    int lo = 0, hi = E + L;  // largest slot j with slot_off(j) <= item
+    w2 = item >= n13;
+    const int li = w2 ? item - n13 : item;
+    const int ntiles = w2 ? nt2 : nt13;
+    int lo = 0, hi = E;  // largest e with s_chunk[e] * ntiles <= li
     while (hi - lo > 1) {
       const int mid = (lo + hi) >> 1;
-      if (slot_off(mid) <= item) lo = mid; else hi = mid;
+      if (s_chunk[mid] * ntiles <= li) lo = mid; else hi = mid;
     }
-    int local = item - slot_off(lo);
-    const int n13_j = lo < E ? (s_chunk[lo + 1] - s_chunk[lo]) * nt13 : 0;
-    w2 = local >= n13_j;
-    if (w2) local -= n13_j;
-    e = w2 ? lo - L : lo;
+    e = lo;
     const int ch = s_chunk[e + 1] - s_chunk[e];
+    const int local = li - s_chunk[e] * ntiles;
     nt = local / ch;
     const int c = local - nt * ch;
     cg = s_chunk[e] + c;
@@ -505,20 +491,37 @@ __global__ void __launch_bounds__(C::kThreads, 1)
       decode(item, w2, e, row0, cnt, nt, cg);
       const int nbox = (cnt + 31) / 32;
       const int nkb = (w2 ? p.I : p.H) / 128;
+      if (w2) {
+        // the hidden rows of this chunk: every W1|W3 tile of it has been stored
+        int done = 1;
+        if (lane == 0) {
+          done = 0;
+          const int need = nt13 * C::kEpiWarps;
+          if (ld_acquire_gpu(p.h_done + cg) >= need) done = 1;
+          const unsigned long long t0 = gtimer_ns();
+          while (!done && !*abort_flag) {
+            if (ld_acquire_gpu(p.h_done + cg) >= need) done = 1;
+            else if (gtimer_ns() - t0 > kWaitNs) break;
+            else __nanosleep(64);
+          }
+          if (!done && !*abort_flag) bs_set_error(BS_ERR_DEVICE_TIMEOUT);
+          fence_proxy_async_global();
+        }
+        if (!__shfl_sync(0xffffffffu, done, 0)) { *abort_flag = 1; ok = false; break; }
+      }
       const CUtensorMap* mw = w2 ? &tm_w2 : &tm_w13;
       const CUtensorMap* ma = w2 ? &tm_h : &tm_a;
       const uint8_t* wsp = w2 ? p.w2_sp : p.w13_sp;
       const uint8_t* asp = w2 ? p.hs_p : p.a_sp;
       const int wt = w2 ? w2_tiles : w13_tiles;
-      bool rows_ready = !w2;   // a W2 item's token rows are the hidden rows of its chunk
       for (int kb = 0; kb < nkb; ++kb, ++it) {
         const int s = it % C::kStages;
         const uint32_t ph = (it / C::kStages) & 1;
         if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1, abort_flag))) { ok = false; break; }
-        uint8_t* sx = stage_base + s * C::kStageBytes;
-        uint8_t* sy = sx + C::kXBytes;
-        uint8_t* sf = sf_base + s * C::kSfBytes;
         if (elect_one()) {
+          uint8_t* sx = stage_base + s * C::kStageBytes;
+          uint8_t* sy = sx + C::kXBytes;
+          uint8_t* sf = sf_base + s * C::kSfBytes;
           mbar_arrive_expect_tx(&full[s], 2 * (8192 + 512) + nbox * 32 * 128 + 512);
 #pragma unroll
           for (int t = 0; t < 2; ++t) {
@@ -526,28 +529,6 @@ __global__ void __launch_bounds__(C::kThreads, 1)
             tma_load_3d(sx + t * 16384, mw, &full[s], kb * 128, wr0, e);
             bulk_load(sf + t * 512, wsp + (((int64_t)e * wt + wr0 / 128) * nkb + kb) * 512, 512, &full[s]);
           }
-        }
-        __syncwarp();
-        if (!rows_ready) {
-          // every W1|W3 tile of this chunk has been stored (waited for after
-          // the first weight loads are on their way)
-          int done = 0;
-          if (lane == 0) {
-            const int need = nt13 * C::kEpiWarps;
-            if (ld_acquire_gpu(p.h_done + cg) >= need) done = 1;
-            const unsigned long long t0 = gtimer_ns();
-            while (!done && !*abort_flag) {
-              if (ld_acquire_gpu(p.h_done + cg) >= need) done = 1;
-              else if (gtimer_ns() - t0 > kWaitNs) break;
-              else __nanosleep(64);
-            }
-            if (!done && !*abort_flag) bs_set_error(BS_ERR_DEVICE_TIMEOUT);
-            fence_proxy_async_global();
-          }
-          if (!__shfl_sync(0xffffffffu, done, 0)) { *abort_flag = 1; ok = false; break; }
-          rows_ready = true;
-        }
-        if (elect_one()) {
           for (int b = 0; b < nbox; ++b) tma_load_2d(sy + b * 32 * 128, ma, &full[s], kb * 128, row0 + b * 32);
           bulk_load(sf + 2 * 512, asp + ((int64_t)cg * nkb + kb) * 512, 512, &full[s]);
         }
@@ -816,12 +797,6 @@ cudaError_t run_layer(const Layer& L, cudaStream_t st, int* status) {
   if (e != cudaSuccess) return e;
   ExpArgs xa = L.x;
   xa.rows_per_epoch = (unsigned long long)L.f.n * G;
-  // about two rounds of W1|W3 items (one chunk per expert) between an
-  // expert's W1|W3 and W2 items
-  const int nt13 = xa.I / 128;
-  xa.lag = (2 * G + nt13 - 1) / nt13;
-  if (xa.lag > El) xa.lag = El;
-  if (xa.lag < 1) xa.lag = 1;
   if (t_ev_begin) cudaEventRecord(t_ev_begin, st);
   e = launch_coop(experts_kernel, G, C::kThreads, (size_t)C::kSmemBytes, st, mw13, ma, mw2, mh, xa, L.pr);
   if (t_ev_end) cudaEventRecord(t_ev_end, st);

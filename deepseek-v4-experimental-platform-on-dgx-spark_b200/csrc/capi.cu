@@ -295,7 +295,7 @@ FusedLayout fused_layout(int64_t T_max, int H, int I, int E, int topk, int n_ran
   FusedLayout L = {};
   const int El = E / n_ranks;
   L.cap = (int64_t)n_ranks * T_max * topk;
-  L.chunk_cap = bs_moe_max_chunks(L.cap, El);
+  L.chunk_cap = L.cap / mf::kTok + El;          // <= kTok-row chunks over El experts
   size_t o = 0;
   auto take = [&](size_t bytes) { size_t at = o; o += up256(bytes); return at; };
   // cleared before every single-GPU call (one memset): sync words, counters

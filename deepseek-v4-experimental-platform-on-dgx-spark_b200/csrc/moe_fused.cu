@@ -50,6 +50,8 @@ namespace mf {
 
 constexpr int kMaxRanks = 8;
 constexpr int kFrontThreads = 512;
+// token rows per work item (MMA N <= 64) and per packed scale chunk
+constexpr int kTok = 64;
 constexpr unsigned long long kWaitNs = 2000000000ull;   // 2 s
 
 // per-rank sync words (uint64)
@@ -311,7 +313,7 @@ __global__ void __launch_bounds__(kFrontThreads) front_kernel(FrontArgs a, Peers
       if (s < me) before += c;
     }
     P[e] = tot;
-    Cc[e] = (tot + moe::kTok - 1) / moe::kTok;
+    Cc[e] = (tot + kTok - 1) / kTok;
     Bf[e] = before;
   }
   __syncthreads();
@@ -335,8 +337,8 @@ __global__ void __launch_bounds__(kFrontThreads) front_kernel(FrontArgs a, Peers
     slot = __shfl_sync(0xffffffffu, slot, 0);
     const int cin = Bf[e] + slot;                                // row inside expert e at its owner
     const int64_t pos = (int64_t)(P[e] - P[d * El]) + cin;        // row in the owner's receive buffer
-    const int64_t cg = (int64_t)(Cc[e] - Cc[d * El]) + cin / moe::kTok;
-    const int r = cin % moe::kTok;
+    const int64_t cg = (int64_t)(Cc[e] - Cc[d * El]) + cin / kTok;
+    const int r = cin % kTok;
     if (pos >= a.cap || cg >= a.chunk_cap) {                     // only if ranks disagree on sizes
       if (lane == 0) bs_set_error(BS_ERR_DEVICE_FAULT);
       continue;
@@ -391,9 +393,31 @@ struct ExpArgs {
   unsigned long long rows_per_epoch;   // n * front CTAs
 };
 
-using C = moe::Cfg<moe::kModeW13>;   // W2 pair items use the same stage and TMEM layout
-static_assert(moe::Cfg<moe::kModeW13>::kStageBytes == moe::Cfg<moe::kModeW2Pair>::kStageBytes, "stage layouts");
-static_assert(moe::Cfg<moe::kModeW13>::kAccCols == moe::Cfg<moe::kModeW2Pair>::kAccCols, "accumulator layouts");
+// Stage and TMEM layout of the experts kernel.  Both item kinds stream two
+// 128-row weight tiles (e2m1, unpacked to a byte per element by TMA) and one
+// token tile per 128-wide K block.  Token chunks hold at most kTok = 64 rows,
+// so a stage is 32 KB of weight tiles + 8 KB of token rows, and five stages
+// (80 KB of HBM weight bytes in flight per SM) fit in shared memory: the
+// grouped GEMM is bound by weight bytes in flight, not by the tensor pipe.
+struct C {
+  static constexpr int kXBytes = 2 * 128 * 128;
+  static constexpr int kYBytes = kTok * 128;
+  static constexpr int kStageBytes = kXBytes + kYBytes;
+  static constexpr int kStages = 5;
+  static constexpr int kSfBytes = 512 * 3;
+  static constexpr int kAccBufs = 2;
+  static constexpr int kAccCols = 2 * kTok;                // gate|up or two W2 tiles, kTok columns each
+  static constexpr int kSfSlot = 4 * 3;
+  static constexpr int kSfCol0 = kAccBufs * kAccCols;
+  static_assert(kSfCol0 + 2 * kSfSlot <= 512, "TMEM budget");
+  static constexpr int kTmemCols = 512;
+  static constexpr int kEpiWarps = 8;
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;
+  static constexpr int kMaxE = 1024;
+  static constexpr int kSmemBytes = 1024 + kStages * (kStageBytes + kSfBytes) + 2 * (kMaxE + 1) * 4 + 2 * 80 * 4 + 256;
+  static_assert(kStageBytes % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
+  static_assert(kSmemBytes <= 232448, "shared memory per CTA");
+};
 
 __global__ void __launch_bounds__(C::kThreads, 1)
     experts_kernel(const __grid_constant__ CUtensorMap tm_w13, const __grid_constant__ CUtensorMap tm_a,
@@ -468,9 +492,9 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     nt = local / ch;
     const int c = local - nt * ch;
     cg = s_chunk[e] + c;
-    row0 = s_off[e] + c * moe::kTok;
+    row0 = s_off[e] + c * kTok;
     const int left = s_off[e + 1] - row0;
-    cnt = left < moe::kTok ? left : moe::kTok;
+    cnt = left < kTok ? left : kTok;
   };
 
   if (warp == 0) {
@@ -577,7 +601,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
             const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
 #pragma unroll
             for (int t = 0; t < 2; ++t)
-              tc_mma_mxf8f6f4(d0 + t * moe::kTok, dx + (uint64_t)(t * 1024 + 2 * k), dy + (uint64_t)(2 * k), idesc,
+              tc_mma_mxf8f6f4(d0 + t * kTok, dx + (uint64_t)(t * 1024 + 2 * k), dy + (uint64_t)(2 * k), idesc,
                               (slot + 4 * t) | kid, sfb | kid, acc);
           }
           tc_commit(&empty[s]);
@@ -607,7 +631,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
       for (int c0 = set * 16; c0 < cnt; c0 += 32) {
         uint32_t g[16], u[16];
         BS_TMEM_LD16(tl + c0, g);
-        BS_TMEM_LD16(tl + moe::kTok + c0, u);
+        BS_TMEM_LD16(tl + kTok + c0, u);
         tmem_ld_wait();
         if (!w2) {
           uint32_t* red = s_red + set * 80;

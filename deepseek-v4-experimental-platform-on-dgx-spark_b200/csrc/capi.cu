@@ -303,7 +303,7 @@ FusedLayout fused_layout(int64_t T_max, int H, int I, int E, int topk, int n_ran
   L.counts = take(4 * 2 * (size_t)E);
   L.cursor = take(4 * 2 * (size_t)E);
   L.zero_end = o;
-  L.cnt_all = local_only ? 0 : take(4 * (size_t)E);
+  L.cnt_all = local_only ? 0 : take(8 * (size_t)E);
   L.xq = take((size_t)T_max * H);
   L.xs = take((size_t)T_max * (H / 128));
   L.idx = take(4 * (size_t)T_max * topk);
@@ -372,6 +372,7 @@ static int moe_forward_fused(const void* x, const float* logits, int64_t T, int 
   f.xq = ws + L.xq; f.xs = ws + L.xs; f.idx = (int*)(ws + L.idx); f.w = (float*)(ws + L.w);
   f.counts = (int*)(ws + L.counts); f.cursor = (int*)(ws + L.cursor);
   f.offsets = (int*)(ws + L.offsets); f.chunk_prefix = (int*)(ws + L.chunks); f.h_done = (int*)(ws + L.hdone);
+  f.w13 = (const uint8_t*)w13; f.w13_sp = (const uint8_t*)w13_sp; f.I = I;
   mf::ExpArgs& xa = ly.x;
   xa.E = E; xa.H = H; xa.I = I; xa.n = 1; xa.me = 0; xa.cap = L.cap;
   xa.offsets = f.offsets; xa.chunk_prefix = f.chunk_prefix; xa.a_sp = ws + L.rows_sp; xa.ret = (const int*)(ws + L.ret);
@@ -481,7 +482,7 @@ int bs_ep_moe_sizes(int64_t max_tokens, int H, int I, int E, int topk, int n_ran
   if (!sizes) return fail(BS_ERR_INVALID_ARG, "ep_moe_sizes: null output");
   const FusedLayout L = fused_layout(max_tokens, H, I, E, topk, n_ranks, true);
   sizes[0] = (int64_t)L.total;                                   // workspace (this rank only)
-  sizes[1] = 4 * (int64_t)n_ranks * E;                           // cnt_all
+  sizes[1] = 8 * (int64_t)n_ranks * E;                           // cnt_all (epoch-tagged 64-bit words)
   sizes[2] = L.cap * H;                                          // rows
   sizes[3] = L.chunk_cap * (H / 128) * 512;                      // rows_sp
   sizes[4] = 4 * L.cap;                                          // ret
@@ -504,7 +505,7 @@ int bs_ep_moe_forward(const void* x, const float* logits, int64_t T, int64_t max
   if ((T > 0 && (!aligned(x, 16) || !aligned(out, 16))) || !aligned(w13, 32) || !aligned(w2, 32) ||
       !aligned(workspace, 256) || !aligned(w13_sp, 16) || !aligned(w2_sp, 16))
     return fail(BS_ERR_INVALID_ARG, "ep_moe_forward: alignment (x,out,scales 16 B; weights 32 B; workspace 256 B)");
-  static const int kAlign[6] = {4, 16, 16, 4, 16, 8};
+  static const int kAlign[6] = {8, 16, 16, 4, 16, 8};
   for (int k = 0; k < 6; ++k)
     for (int q = 0; q < n_ranks; ++q)
       if (!peer_bufs[k * n_ranks + q] || !aligned(peer_bufs[k * n_ranks + q], kAlign[k]))
@@ -522,6 +523,7 @@ int bs_ep_moe_forward(const void* x, const float* logits, int64_t T, int64_t max
   f.xq = ws + L.xq; f.xs = ws + L.xs; f.idx = (int*)(ws + L.idx); f.w = (float*)(ws + L.w);
   f.counts = (int*)(ws + L.counts); f.cursor = (int*)(ws + L.cursor);
   f.offsets = (int*)(ws + L.offsets); f.chunk_prefix = (int*)(ws + L.chunks); f.h_done = (int*)(ws + L.hdone);
+  f.w13 = (const uint8_t*)w13; f.w13_sp = (const uint8_t*)w13_sp; f.I = I;
   for (int q = 0; q < n_ranks; ++q) {
     ly.pr.cnt_all[q] = (int*)peer_bufs[0 * n_ranks + q];
     ly.pr.rows[q] = (uint8_t*)peer_bufs[1 * n_ranks + q];

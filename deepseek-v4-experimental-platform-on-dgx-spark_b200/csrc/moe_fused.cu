@@ -60,7 +60,7 @@ constexpr int kSyncWords = kCntFlag + kMaxRanks;
 
 // Buffers peers write, as mapped into this process; index = rank.
 struct Peers {
-  int* cnt_all[kMaxRanks];                // [n][E] int32 count matrix (row s: rank s's histogram)
+  int* cnt_all[kMaxRanks];                // [n][E] uint64 count matrix (row s: rank s's histogram, epoch-tagged)
   uint8_t* rows[kMaxRanks];               // [cap][H] e4m3 expert-major receive rows
   uint8_t* rows_sp[kMaxRanks];            // [chunk_cap][H/128][512] their packed scales
   int* ret[kMaxRanks];                    // [cap] return addresses
@@ -174,10 +174,42 @@ struct FrontArgs {
   int* offsets;               // [El + 1] this rank's experts (owner side)
   int* chunk_prefix;          // [El + 1]
   int* h_done;                // [chunk_cap] zeroed here for the experts kernel
+  const uint8_t* w13;         // this rank's W1|W3 weights and packed scales: the first
+  const uint8_t* w13_sp;      //   work item of each experts CTA is prefetched into L2
+  int I;
 };
 
+BS_DEVINL unsigned long long ld_relaxed_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+BS_DEVINL void st_relaxed_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+BS_DEVINL void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+// Release of this CTA's earlier writes (ordered before the calling thread by
+// a CTA barrier) to a counter of another GPU (kSys) or of this GPU.
+template <bool kSys>
+BS_DEVINL void signal_add(unsigned long long* p) {
+  if (kSys) {
+    __threadfence_system();
+    red_release_sys_add(p, 1ull);
+  } else {
+    __threadfence();
+    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(1ull) : "memory");
+  }
+}
+
 // Dynamic shared memory: 3 * E + 2 ints (plan).
-template <int kMaxPer>
+//
+// kMulti (more than one rank): the histograms travel as 64-bit words
+// (epoch << 32 | count) written straight into every rank's count matrix, so
+// a reader knows a word is this call's from the word itself -- no fence and
+// no separate flag; one rank skips the exchange and reads its histogram.
+template <int kMaxPer, bool kMulti>
 __global__ void __launch_bounds__(kFrontThreads) front_kernel(FrontArgs a, Peers pr) {
   extern __shared__ int sh[];
   __shared__ unsigned long long s_ep;
@@ -207,13 +239,15 @@ __global__ void __launch_bounds__(kFrontThreads) front_kernel(FrontArgs a, Peers
   }
   for (int64_t i = gtid; i < a.chunk_cap; i += nthreads) a.h_done[i] = 0;
 
-  // ---- A: quantise (half a warp per 1x128 block, power-of-two scales);
-  // each half warp issues the loads of kQ blocks before quantising any
-  {
+  // ---- A: even warps quantise, odd warps route (the two overlap)
+  const int64_t rw = gwarp >> 1, nrw = nwarps >> 1;
+  if ((gwarp & 1) == 0) {
+    // half a warp per 1x128 block, power-of-two scales; each half warp
+    // issues the loads of kQ blocks before quantising any
     constexpr int kQ = 4;
     const int half = lane >> 4, l16 = lane & 15;
     const int64_t n_groups = (int64_t)a.T * nb;
-    for (int64_t base = gwarp * 2 * kQ; base < n_groups; base += nwarps * 2 * kQ) {
+    for (int64_t base = rw * 2 * kQ; base < n_groups; base += nrw * 2 * kQ) {
       uint4 raw[kQ];
 #pragma unroll
       for (int u = 0; u < kQ; ++u) {
@@ -256,18 +290,18 @@ __global__ void __launch_bounds__(kFrontThreads) front_kernel(FrontArgs a, Peers
         }
       }
     }
-  }
-
-  // ---- A: routing (one warp per token)
-  for (int64_t t = gwarp; t < a.T; t += nwarps) {
-    float my_v;
-    int my_e;
-    moe::route_one<kMaxPer>(a.logits + t * a.E, a.E, a.topk, lane, my_v, my_e);
-    const float wk = moe::route_weight(my_v, a.topk, lane);
-    if (lane < a.topk) {
-      a.idx[t * a.topk + lane] = my_e;
-      a.w[t * a.topk + lane] = wk;
-      atomicAdd(&counts[my_e], 1);
+  } else {
+    // one warp per token: top-k, softmax weights, histogram
+    for (int64_t t = rw; t < a.T; t += nrw) {
+      float my_v;
+      int my_e;
+      moe::route_one<kMaxPer>(a.logits + t * a.E, a.E, a.topk, lane, my_v, my_e);
+      const float wk = moe::route_weight(my_v, a.topk, lane);
+      if (lane < a.topk) {
+        a.idx[t * a.topk + lane] = my_e;
+        a.w[t * a.topk + lane] = wk;
+        atomicAdd(&counts[my_e], 1);
+      }
     }
   }
 
@@ -283,46 +317,86 @@ __global__ void __launch_bounds__(kFrontThreads) front_kernel(FrontArgs a, Peers
   if (!s_ok) return;
   if (blockIdx.x == 0 && threadIdx.x == 0) my_sync[kEpoch] = ep;   // read again only by later kernels
 
-  // ---- B: histogram to every rank, flag, wait for every rank's flag
+  // ---- B: the full count matrix, and the plan.  P[e]: rows of experts
+  // before e (all ranks); Cc[e]: chunks of experts before e; Bf[e]: rows of
+  // expert e from ranks below me.
   const int E = a.E, El = a.El, n = a.n, me = a.me;
-  if ((int)blockIdx.x < n) {
-    const int q = blockIdx.x;
-    int* dst = pr.cnt_all[q] + (int64_t)me * E;
-    for (int e = threadIdx.x; e < E; e += kFrontThreads) dst[e] = __ldcg(counts + e);
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      __threadfence_system();
-      st_release_sys(pr.sync[q] + kCntFlag + me, ep);
-    }
-  }
-  if (threadIdx.x < n && !wait_geq<true>(my_sync + kCntFlag + threadIdx.x, ep)) s_ok = 0;
-  __syncthreads();
-  if (!s_ok) return;
-
-  // ---- B: plan.  P[e]: rows of experts before e (all ranks); Cc[e]: chunks
-  // of experts before e; Bf[e]: rows of expert e from ranks below me.
   int* P = sh;
   int* Cc = sh + E + 1;
   int* Bf = sh + 2 * E + 2;
-  const int* cnt_mine = pr.cnt_all[me];
-  for (int e = threadIdx.x; e < E; e += kFrontThreads) {
-    int tot = 0, before = 0;
-    for (int s = 0; s < n; ++s) {
-      const int c = __ldcg(cnt_mine + (int64_t)s * E + e);
-      tot += c;
-      if (s < me) before += c;
+  if constexpr (kMulti) {
+    const unsigned long long tag = (ep & 0xFFFFFFFFull) << 32;
+    if ((int)blockIdx.x < n) {
+      unsigned long long* dst = reinterpret_cast<unsigned long long*>(pr.cnt_all[blockIdx.x]) + (int64_t)me * E;
+      for (int e = threadIdx.x; e < E; e += kFrontThreads) st_relaxed_sys(dst + e, tag | (uint32_t)__ldcg(counts + e));
     }
-    P[e] = tot;
-    Cc[e] = (tot + kTok - 1) / kTok;
-    Bf[e] = before;
+    const unsigned long long* mine = reinterpret_cast<const unsigned long long*>(pr.cnt_all[me]);
+    for (int e = threadIdx.x; e < E; e += kFrontThreads) {
+      int tot = 0, before = 0;
+      for (int s = 0; s < n; ++s) {
+        const unsigned long long* wp = mine + (int64_t)s * E + e;
+        unsigned long long v = ld_relaxed_sys(wp);
+        if ((v & 0xFFFFFFFF00000000ull) != tag) {
+          const unsigned long long t0 = gtimer_ns();
+          while (((v = ld_relaxed_sys(wp)) & 0xFFFFFFFF00000000ull) != tag) {
+            if (gtimer_ns() - t0 > kWaitNs) {
+              bs_set_error(BS_ERR_DEVICE_TIMEOUT);
+              s_ok = 0;
+              break;
+            }
+            __nanosleep(32);
+          }
+        }
+        const int c = (int)(uint32_t)v;
+        tot += c;
+        if (s < me) before += c;
+      }
+      P[e] = tot;
+      Cc[e] = (tot + kTok - 1) / kTok;
+      Bf[e] = before;
+    }
+  } else {
+    for (int e = threadIdx.x; e < E; e += kFrontThreads) {
+      const int c = __ldcg(counts + e);
+      P[e] = c;
+      Cc[e] = (c + kTok - 1) / kTok;
+      Bf[e] = 0;
+    }
   }
   __syncthreads();
+  if (!s_ok) return;
   block_scan2<kFrontThreads>(P, Cc, E);
+  const int e0 = me * El;
   if (blockIdx.x == 0) {
-    const int e0 = me * El;
     for (int l = threadIdx.x; l <= El; l += kFrontThreads) {
       a.offsets[l] = P[e0 + l] - P[e0];
       a.chunk_prefix[l] = Cc[e0 + l] - Cc[e0];
+    }
+  }
+  // The experts kernel's CTA b starts with work item b (a W1|W3 item when
+  // there are enough): its weight tiles and their scales go to L2 now, while
+  // HBM is otherwise idle during the row dispatch.
+  if (threadIdx.x == 0 && a.w13) {
+    const int nt13 = a.I / 128;
+    const int item = blockIdx.x;
+    if (item < (Cc[e0 + El] - Cc[e0]) * nt13) {
+      int lo = 0, hi = El;  // largest local expert l with (chunks before l) * nt13 <= item
+      while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if ((Cc[e0 + mid] - Cc[e0]) * nt13 <= item) lo = mid; else hi = mid;
+      }
+      const int ch = Cc[e0 + lo + 1] - Cc[e0 + lo];
+      const int nt = (item - (Cc[e0 + lo] - Cc[e0]) * nt13) / ch;
+      const int64_t row_bytes = H / 2;
+      for (int t = 0; t < 2; ++t) {
+        const int64_t row0 = (int64_t)lo * 2 * a.I + t * a.I + nt * 128;
+        const uint8_t* wp = a.w13 + row0 * row_bytes;
+        for (int64_t off = 0; off < 128 * row_bytes; off += 65536)
+          prefetch_l2(wp + off, (uint32_t)min((int64_t)65536, 128 * row_bytes - off));
+        // the row tile's packed scales, all K blocks: [E][2I/128][H/128][512]
+        prefetch_l2(a.w13_sp + (((int64_t)lo * (2 * a.I / 128) + (t * a.I + nt * 128) / 128) * nb) * 512,
+                    (uint32_t)(nb * 512));
+      }
     }
   }
 
@@ -372,10 +446,7 @@ __global__ void __launch_bounds__(kFrontThreads) front_kernel(FrontArgs a, Peers
     if (lane == 0) pr.ret[d][pos] = (me << 24) | (int)j;
   }
   __syncthreads();
-  if (threadIdx.x < n) {
-    __threadfence_system();
-    red_release_sys_add(pr.sync[threadIdx.x] + kRowsIn, 1ull);
-  }
+  if (threadIdx.x < n) signal_add<kMulti>(pr.sync[threadIdx.x] + kRowsIn);
 }
 
 struct ExpArgs {
@@ -419,6 +490,7 @@ struct C {
   static_assert(kSmemBytes <= 232448, "shared memory per CTA");
 };
 
+template <bool kMulti>
 __global__ void __launch_bounds__(C::kThreads, 1)
     experts_kernel(const __grid_constant__ CUtensorMap tm_w13, const __grid_constant__ CUtensorMap tm_a,
                    const __grid_constant__ CUtensorMap tm_w2, const __grid_constant__ CUtensorMap tm_h, ExpArgs p,
@@ -502,7 +574,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     bool ok = true;
     if (lane == 0) {
       const unsigned long long ep = *reinterpret_cast<volatile unsigned long long*>(my_sync + kEpoch);
-      ok = wait_geq<true>(my_sync + kRowsIn, ep * p.rows_per_epoch);   // every rank's rows are here
+      ok = wait_geq<kMulti>(my_sync + kRowsIn, ep * p.rows_per_epoch);   // every rank's rows are here
       fence_proxy_async_global();
     }
     ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
@@ -704,14 +776,12 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     tmem_dealloc(tmem_base, C::kTmemCols);
   }
   // this CTA's output rows are at their source ranks
-  if (threadIdx.x < p.n) {
-    __threadfence_system();
-    red_release_sys_add(pr.sync[threadIdx.x] + kRetIn, 1ull);
-  }
+  if (threadIdx.x < p.n) signal_add<kMulti>(pr.sync[threadIdx.x] + kRetIn);
 }
 
 // out[t] = bf16(sum_k w[t,k] * y_back[t*topk + k]), fp32 in slot order; waits
 // until every rank's experts CTAs have returned their rows.
+template <bool kMulti>
 __global__ void combine_kernel(const __nv_bfloat16* __restrict__ y, const float* __restrict__ w, int topk, int H,
                                __nv_bfloat16* __restrict__ out, unsigned long long* my_sync,
                                unsigned long long ret_per_epoch) {
@@ -719,7 +789,7 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ y, const float*
   __shared__ int s_ok;
   if (threadIdx.x == 0) {
     const unsigned long long ep = *reinterpret_cast<volatile unsigned long long*>(my_sync + kEpoch);
-    s_ok = wait_geq<true>(my_sync + kRetIn, ep * ret_per_epoch) ? 1 : 0;
+    s_ok = wait_geq<kMulti>(my_sync + kRetIn, ep * ret_per_epoch) ? 1 : 0;
   }
   __syncthreads();
   if (!s_ok) return;
@@ -790,7 +860,8 @@ struct Layer {
   const float* wts;
 };
 
-cudaError_t run_layer(const Layer& L, cudaStream_t st, int* status) {
+template <bool kMulti>
+cudaError_t run_layer_t(const Layer& L, cudaStream_t st, int* status) {
   *status = 0;
   const int G = sm_count();
   const int E = L.f.E, El = L.f.El;
@@ -798,12 +869,12 @@ cudaError_t run_layer(const Layer& L, cudaStream_t st, int* status) {
   const size_t fsm = (size_t)(3 * E + 2) * sizeof(int);
   const int per = (E + 31) / 32;
   cudaError_t e;
-  if (per <= 1) e = launch_coop(front_kernel<1>, G, kFrontThreads, fsm, st, L.f, L.pr);
-  else if (per <= 2) e = launch_coop(front_kernel<2>, G, kFrontThreads, fsm, st, L.f, L.pr);
-  else if (per <= 4) e = launch_coop(front_kernel<4>, G, kFrontThreads, fsm, st, L.f, L.pr);
-  else if (per <= 8) e = launch_coop(front_kernel<8>, G, kFrontThreads, fsm, st, L.f, L.pr);
-  else if (per <= 16) e = launch_coop(front_kernel<16>, G, kFrontThreads, fsm, st, L.f, L.pr);
-  else e = launch_coop(front_kernel<32>, G, kFrontThreads, fsm, st, L.f, L.pr);
+  if (per <= 1) e = launch_coop(front_kernel<1, kMulti>, G, kFrontThreads, fsm, st, L.f, L.pr);
+  else if (per <= 2) e = launch_coop(front_kernel<2, kMulti>, G, kFrontThreads, fsm, st, L.f, L.pr);
+  else if (per <= 4) e = launch_coop(front_kernel<4, kMulti>, G, kFrontThreads, fsm, st, L.f, L.pr);
+  else if (per <= 8) e = launch_coop(front_kernel<8, kMulti>, G, kFrontThreads, fsm, st, L.f, L.pr);
+  else if (per <= 16) e = launch_coop(front_kernel<16, kMulti>, G, kFrontThreads, fsm, st, L.f, L.pr);
+  else e = launch_coop(front_kernel<32, kMulti>, G, kFrontThreads, fsm, st, L.f, L.pr);
   if (e != cudaSuccess) return e;
   // experts
   CUtensorMap mw13, ma, mw2, mh;
@@ -816,13 +887,14 @@ cudaError_t run_layer(const Layer& L, cudaStream_t st, int* status) {
   }
   static int attr_slots[hostcache::kMaxDevices];
   e = (cudaError_t)hostcache::get(attr_slots, [&] {
-    return (int)cudaFuncSetAttribute(experts_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    return (int)cudaFuncSetAttribute(experts_kernel<kMulti>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     C::kSmemBytes);
   });
   if (e != cudaSuccess) return e;
   ExpArgs xa = L.x;
   xa.rows_per_epoch = (unsigned long long)L.f.n * G;
   if (t_ev_begin) cudaEventRecord(t_ev_begin, st);
-  e = launch_coop(experts_kernel, G, C::kThreads, (size_t)C::kSmemBytes, st, mw13, ma, mw2, mh, xa, L.pr);
+  e = launch_coop(experts_kernel<kMulti>, G, C::kThreads, (size_t)C::kSmemBytes, st, mw13, ma, mw2, mh, xa, L.pr);
   if (t_ev_end) cudaEventRecord(t_ev_end, st);
   t_ev_begin = t_ev_end = nullptr;
   if (e != cudaSuccess) return e;
@@ -830,11 +902,15 @@ cudaError_t run_layer(const Layer& L, cudaStream_t st, int* status) {
   if (L.f.T > 0) {
     int threads = L.x.H / 8;
     if (threads > 512) threads = 512;
-    combine_kernel<<<L.f.T, threads, 0, st>>>(L.pr.y_back[L.f.me], L.wts, L.f.topk, L.x.H, L.out,
-                                               L.pr.sync[L.f.me], (unsigned long long)L.f.n * G);
+    combine_kernel<kMulti><<<L.f.T, threads, 0, st>>>(L.pr.y_back[L.f.me], L.wts, L.f.topk, L.x.H, L.out,
+                                                       L.pr.sync[L.f.me], (unsigned long long)L.f.n * G);
     e = cudaGetLastError();
   }
   return e;
+}
+
+cudaError_t run_layer(const Layer& L, cudaStream_t st, int* status) {
+  return L.f.n > 1 ? run_layer_t<true>(L, st, status) : run_layer_t<false>(L, st, status);
 }
 
 }  // namespace mf

@@ -32,6 +32,9 @@ SIGNATURES = {
     "bs_fp4_gemm": [_c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p, _i32, _i64, _i64, _i64, _c_void_p, _c_void_p],
     "bs_fp4_weights_to_bf16": [_c_void_p, _c_void_p, _i64, _i64, _c_void_p, _c_void_p],
     "bs_e4m3_rows_to_bf16": [_c_void_p, _c_void_p, _i32, _i64, _i64, _c_void_p, _c_void_p],
+    "bs_e4m3_blocks_to_bf16": [_c_void_p, _c_void_p, _i32, _i64, _i64, _c_void_p, _c_void_p],
+    "bs_hc_split_sinkhorn": [_c_void_p, _i32, _c_void_p, _c_void_p, _i64, _i32, _i32, ctypes.c_float, _c_void_p,
+                             _c_void_p, _c_void_p, _c_void_p],
     "bs_fp8_gemm_allgather": [_c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p, _i32, _i64, _i64, _i64,
                               ctypes.POINTER(_c_void_p), _i32, _i64, _i64, _c_void_p],
     "bs_fp4_gemm_allgather": [_c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p, _i32, _i64, _i64, _i64,

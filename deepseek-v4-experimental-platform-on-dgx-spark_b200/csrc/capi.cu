@@ -196,6 +196,37 @@ int bs_e4m3_rows_to_bf16(const void* a, const void* a_s, int as_dtype, int64_t M
                      "e4m3_rows_to_bf16");
 }
 
+int bs_e4m3_blocks_to_bf16(const void* w, const void* s, int s_dtype, int64_t N, int64_t K, void* out, void* stream) {
+  if (N < 0 || K <= 0 || K % 128)
+    return fail(BS_ERR_INVALID_ARG, "e4m3_blocks_to_bf16: N=%lld K=%lld (K a multiple of 128)", (long long)N,
+                (long long)K);
+  if (s_dtype != BS_DT_F32 && s_dtype != BS_DT_E8M0)
+    return fail(BS_ERR_UNSUPPORTED, "e4m3_blocks_to_bf16: scale dtype tag %d (f32 or e8m0)", s_dtype);
+  if (N > 0 && (!w || !s || !out || !aligned(w, 16) || !aligned(out, 16) || !aligned(s, s_dtype == BS_DT_F32 ? 4 : 1)))
+    return fail(BS_ERR_INVALID_ARG, "e4m3_blocks_to_bf16: null or misaligned pointer (w, out 16 B)");
+  return cuda_status(bs_launch_e4m3_blocks_to_bf16(w, s, s_dtype == BS_DT_E8M0, N, K, out, (cudaStream_t)stream),
+                     "e4m3_blocks_to_bf16");
+}
+
+int bs_hc_split_sinkhorn(const void* mixes, int mixes_dtype, const float* hc_scale, const float* hc_base, int64_t n,
+                         int hc_mult, int sinkhorn_iters, float eps, float* pre, float* post, float* comb,
+                         void* stream) {
+  if (n < 0 || sinkhorn_iters < 1)
+    return fail(BS_ERR_INVALID_ARG, "hc_split_sinkhorn: n=%lld iters=%d", (long long)n, sinkhorn_iters);
+  if (hc_mult != 1 && hc_mult != 2 && hc_mult != 3 && hc_mult != 4 && hc_mult != 6 && hc_mult != 8)
+    return fail(BS_ERR_UNSUPPORTED, "hc_split_sinkhorn: hc_mult %d (1, 2, 3, 4, 6 or 8)", hc_mult);
+  if (mixes_dtype != BS_DT_F32 && mixes_dtype != BS_DT_BF16 && mixes_dtype != BS_DT_F16)
+    return fail(BS_ERR_UNSUPPORTED, "hc_split_sinkhorn: mixes dtype tag %d (f32, bf16 or f16)", mixes_dtype);
+  if (n > 0 && (!mixes || !hc_scale || !hc_base || !pre || !post || !comb))
+    return fail(BS_ERR_INVALID_ARG, "hc_split_sinkhorn: null pointer");
+  if (n > 0 && (!aligned(mixes, mixes_dtype == BS_DT_F32 ? 4 : 2) || !aligned(hc_scale, 4) || !aligned(hc_base, 4) ||
+                !aligned(pre, 4) || !aligned(post, 4) || !aligned(comb, 4)))
+    return fail(BS_ERR_INVALID_ARG, "hc_split_sinkhorn: misaligned pointer");
+  return cuda_status(bs_launch_hc_sinkhorn(mixes, mixes_dtype, hc_scale, hc_base, n, hc_mult, sinkhorn_iters, eps, pre,
+                                           post, comb, (cudaStream_t)stream),
+                     "hc_split_sinkhorn");
+}
+
 int bs_fp8_gemm_allgather(const void* a, const void* a_s, int as_dtype, const void* b, const void* b_s,
                           int bs_dtype, int64_t M, int64_t N, int64_t K, void* const* c_ranks, int n_ranks,
                           int64_t ldc, int64_t col0, void* stream) {

@@ -64,6 +64,35 @@ __global__ void e4m3_to_bf16_kernel(const uint8_t* __restrict__ a, const void* _
   }
 }
 
+// e4m3 [N, K] times per-128x128 block scales [ceil(N/128), K/128] (fp32 or
+// ue8m0), rounded to bf16: one thread per 16 values of a row.
+template <bool E8M0>
+__global__ void e4m3_blocks_to_bf16_kernel(const uint8_t* __restrict__ w, const void* __restrict__ s, int64_t K,
+                                           int64_t n_vec, __nv_bfloat16* __restrict__ out) {
+  const int64_t kb_n = K / 128;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n_vec; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i / (K / 16), kv = i % (K / 16);
+    const int64_t blk = (row / 128) * kb_n + kv / 8;
+    const float sc = E8M0 ? bs_e8m0_to_f32(reinterpret_cast<const uint8_t*>(s)[blk])
+                          : __ldg(reinterpret_cast<const float*>(s) + blk);
+    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(w) + i);
+    const uint32_t v[4] = {raw.x, raw.y, raw.z, raw.w};
+    uint32_t o[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const __nv_bfloat162 h0 = __floats2bfloat162_rn(__fmul_rn(bs_e4m3_to_f32(v[j] & 0xFF), sc),
+                                                      __fmul_rn(bs_e4m3_to_f32((v[j] >> 8) & 0xFF), sc));
+      const __nv_bfloat162 h1 = __floats2bfloat162_rn(__fmul_rn(bs_e4m3_to_f32((v[j] >> 16) & 0xFF), sc),
+                                                      __fmul_rn(bs_e4m3_to_f32(v[j] >> 24), sc));
+      o[2 * j] = *reinterpret_cast<const uint32_t*>(&h0);
+      o[2 * j + 1] = *reinterpret_cast<const uint32_t*>(&h1);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(out + i * 16);
+    dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+  }
+}
+
 int grid(int64_t work) {
   int64_t b = (work + 255) / 256;
   const int64_t cap = 148 * 8;
@@ -87,5 +116,18 @@ cudaError_t bs_launch_e4m3_to_bf16(const void* a, const void* a_s, bool e8m0, in
     dq::e4m3_to_bf16_kernel<true><<<dq::grid(n_vec), 256, 0, st>>>((const uint8_t*)a, a_s, n_vec, (__nv_bfloat16*)out);
   else
     dq::e4m3_to_bf16_kernel<false><<<dq::grid(n_vec), 256, 0, st>>>((const uint8_t*)a, a_s, n_vec, (__nv_bfloat16*)out);
+  return cudaGetLastError();
+}
+
+cudaError_t bs_launch_e4m3_blocks_to_bf16(const void* w, const void* s, bool e8m0, int64_t N, int64_t K, void* out,
+                                          cudaStream_t st) {
+  const int64_t n_vec = N * (K / 16);
+  if (n_vec == 0) return cudaSuccess;
+  if (e8m0)
+    dq::e4m3_blocks_to_bf16_kernel<true><<<dq::grid(n_vec), 256, 0, st>>>((const uint8_t*)w, s, K, n_vec,
+                                                                           (__nv_bfloat16*)out);
+  else
+    dq::e4m3_blocks_to_bf16_kernel<false><<<dq::grid(n_vec), 256, 0, st>>>((const uint8_t*)w, s, K, n_vec,
+                                                                            (__nv_bfloat16*)out);
   return cudaGetLastError();
 }

@@ -3,6 +3,7 @@
 #include "common.cuh"
 #include "quant.cu"
 #include "dequant.cu"
+#include "hc.cu"
 #include "gemm.cu"
 #include "gemm_pair.cu"
 #include "moe.cu"

@@ -23,7 +23,7 @@ import torch
 
 from . import _lib
 
-__all__ = ["act_quant", "fp4_act_quant", "fp8_gemm", "fp4_gemm", "profile_report"]
+__all__ = ["act_quant", "fp4_act_quant", "fp8_gemm", "fp4_gemm", "hc_split_sinkhorn", "profile_report"]
 
 # Per-op call counter and host-side seconds, reported by profile_report() in
 # the same columns as the reference module's report (kernel_sm121.py:31-44).
@@ -206,3 +206,28 @@ def fp4_gemm(a: torch.Tensor, a_s: torch.Tensor, b: torch.Tensor, b_s: torch.Ten
                                        b_sf.data_ptr(), _lib.DT_E8M0, M, N, K, out.data_ptr(), _stream(a)))
     _tally("fp4_gemm", t0)
     return out.view(out_shape)
+
+
+def hc_split_sinkhorn(mixes: torch.Tensor, hc_scale: torch.Tensor, hc_base: torch.Tensor, hc_mult: int = 4,
+                      sinkhorn_iters: int = 20, eps: float = 1e-6):
+    """Hyper-Connection mixing weights (kernel_sm121.py:493-533) in one fused
+    kernel.  mixes [b, s, (2+hc)*hc] -> (pre [b,s,hc], post [b,s,hc],
+    comb [b,s,hc,hc]), all fp32."""
+    t0 = _time.perf_counter()
+    _require_cuda(mixes, hc_scale, hc_base)
+    b, s, _ = mixes.shape
+    hc = hc_mult
+    m = mixes.contiguous()
+    if m.dtype not in (torch.float32, torch.bfloat16, torch.float16):
+        m = m.float()
+    n = b * s
+    pre = torch.empty(b, s, hc, dtype=torch.float32, device=mixes.device)
+    post = torch.empty(b, s, hc, dtype=torch.float32, device=mixes.device)
+    comb = torch.empty(b, s, hc, hc, dtype=torch.float32, device=mixes.device)
+    sc = hc_scale.float().contiguous()
+    bs = hc_base.float().contiguous()
+    _lib.check(_lib.load().bs_hc_split_sinkhorn(m.data_ptr(), _X_DT[m.dtype], sc.data_ptr(), bs.data_ptr(), n, hc,
+                                                sinkhorn_iters, eps, pre.data_ptr(), post.data_ptr(),
+                                                comb.data_ptr(), _stream(mixes)))
+    _tally("hc_sinkhorn", t0)
+    return pre, post, comb

@@ -121,6 +121,25 @@ int bs_fp4_weights_to_bf16(const void* b, const float* b_s, int64_t N, int64_t K
 int bs_e4m3_rows_to_bf16(const void* a, const void* a_s, int as_dtype, int64_t M, int64_t K, void* out, void* stream);
 
 /*
+ * Load-time fusion of an e4m3 weight with its per-128x128 block scales into
+ * bf16 (the wo_a conversion of the reference's loader, weight_loader.py:146-163):
+ * out [N, K] = bf16(e4m3(w) * s[n/128, k/128]), s fp32 or ue8m0.
+ */
+int bs_e4m3_blocks_to_bf16(const void* w, const void* s, int s_dtype, int64_t N, int64_t K, void* out, void* stream);
+
+/*
+ * hc_split_sinkhorn (kernel_sm121.py:493-533): per token, from its
+ * (2+hc)*hc mixes (fp32, bf16 or f16; [n, (2+hc)*hc]) with hc_scale[3] and
+ * hc_base[(2+hc)*hc] (fp32): pre [n, hc] = sigmoid(m*s0 + b) + eps,
+ * post [n, hc] = 2*sigmoid(m*s1 + b), comb [n, hc, hc] = row softmax + eps
+ * followed by sinkhorn_iters column / row normalisations (each sum + eps),
+ * all fp32.  hc_mult 1, 2, 3, 4, 6 or 8.  One fused kernel.
+ */
+int bs_hc_split_sinkhorn(const void* mixes, int mixes_dtype, const float* hc_scale, const float* hc_base, int64_t n,
+                         int hc_mult, int sinkhorn_iters, float eps, float* pre, float* post, float* comb,
+                         void* stream);
+
+/*
  * Tensor-parallel GEMM with the all-gather fused into its epilogue.  This
  * rank holds the weight rows [col0, col0+N) (b, b_s as for bs_fp8_gemm /
  * bs_fp4_gemm) and computes the column slice C[:, col0:col0+N]; every output

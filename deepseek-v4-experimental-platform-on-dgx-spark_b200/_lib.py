@@ -32,6 +32,12 @@ SIGNATURES = {
     "bs_fp4_gemm": [_c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p, _i32, _i64, _i64, _i64, _c_void_p, _c_void_p],
     "bs_fp4_weights_to_bf16": [_c_void_p, _c_void_p, _i64, _i64, _c_void_p, _c_void_p],
     "bs_e4m3_rows_to_bf16": [_c_void_p, _c_void_p, _i32, _i64, _i64, _c_void_p, _c_void_p],
+    "bs_sparse_attn_workspace_size": [_i64, _i64, _i32, _i32, _i32],
+    "bs_sparse_attn": [_c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p, _i32, _i64, _i64, _i32, _i32, _i64, _i32,
+                       ctypes.c_float, _c_void_p, _c_void_p, ctypes.c_size_t, _c_void_p],
+    "bs_indexer_topk_workspace_size": [_i64, _i64],
+    "bs_indexer_topk": [_c_void_p, _c_void_p, _i32, _c_void_p, _i64, _i32, _i32, _i64, _i32, _i32, _i64, _i64,
+                        _c_void_p, _c_void_p, ctypes.c_size_t, _c_void_p],
     "bs_e4m3_blocks_to_bf16": [_c_void_p, _c_void_p, _i32, _i64, _i64, _c_void_p, _c_void_p],
     "bs_hc_split_sinkhorn": [_c_void_p, _i32, _c_void_p, _c_void_p, _i64, _i32, _i32, ctypes.c_float, _c_void_p,
                              _c_void_p, _c_void_p, _c_void_p],
@@ -76,7 +82,8 @@ SIGNATURES = {
 }
 RESTYPES = {"bs_last_error": ctypes.c_char_p, "bs_moe_workspace_size": ctypes.c_size_t,
             "bs_moe_staged_workspace_size": ctypes.c_size_t, "bs_moe_chunk_capacity": ctypes.c_int64,
-            "bs_moe_time_experts": None}
+            "bs_moe_time_experts": None, "bs_sparse_attn_workspace_size": ctypes.c_size_t,
+            "bs_indexer_topk_workspace_size": ctypes.c_size_t}
 
 
 class BsError(RuntimeError):

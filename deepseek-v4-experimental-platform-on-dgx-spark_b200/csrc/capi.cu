@@ -1,3 +1,4 @@
+#include <algorithm>
 // extern "C" entry points (include/bsgemm.h): argument validation, the
 // thread-local error message, and the device-side error word.
 #include <cstdarg>
@@ -206,6 +207,83 @@ int bs_e4m3_blocks_to_bf16(const void* w, const void* s, int s_dtype, int64_t N,
     return fail(BS_ERR_INVALID_ARG, "e4m3_blocks_to_bf16: null or misaligned pointer (w, out 16 B)");
   return cuda_status(bs_launch_e4m3_blocks_to_bf16(w, s, s_dtype == BS_DT_E8M0, N, K, out, (cudaStream_t)stream),
                      "e4m3_blocks_to_bf16");
+}
+
+// sparse_attn: keys split across CTAs only when there are too few queries
+// to fill the GPU (decode); the partial results then need a workspace.
+static void sa_split(int64_t queries, int K, int* nsplit, int* ks) {
+  int ns = 1;
+  if (queries < 2 * 148) {
+    const int64_t want = (2 * 148 + queries - 1) / queries;
+    const int64_t most = (K + 63) / 64;
+    ns = (int)std::max<int64_t>(1, std::min(want, most));
+  }
+  int per = (K + ns - 1) / ns;
+  per = (per + attn::kKT - 1) / attn::kKT * attn::kKT;
+  *nsplit = per > 0 ? (K + per - 1) / per : 1;
+  if (*nsplit < 1) *nsplit = 1;
+  *ks = per > 0 ? per : attn::kKT;
+}
+
+size_t bs_sparse_attn_workspace_size(int64_t B, int64_t S, int H, int D, int K) {
+  int ns, ks;
+  sa_split(B * S, K, &ns, &ks);
+  if (ns == 1) return 0;
+  return (size_t)B * S * ns * H * ((size_t)D + 2) * sizeof(float) + 256;
+}
+
+int bs_sparse_attn(const void* q, const void* kv, int dtype, const float* attn_sink, const void* topk_idxs,
+                   int idx_int64, int64_t B, int64_t S, int H, int D, int64_t N, int K, float softmax_scale,
+                   void* out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (B < 0 || S < 0 || H <= 0 || D <= 0 || N <= 0 || K <= 0 || B * S > 0x7fffffff)
+    return fail(BS_ERR_INVALID_ARG, "sparse_attn: B=%lld S=%lld H=%d D=%d N=%lld K=%d", (long long)B, (long long)S, H,
+                D, (long long)N, K);
+  if ((int64_t)H * D > attn::kMaxHD || N > 0x7fffffff)
+    return fail(BS_ERR_UNSUPPORTED, "sparse_attn: heads x head dim %d exceeds %d", H * D, attn::kMaxHD);
+  if (dtype != BS_DT_F32 && dtype != BS_DT_BF16 && dtype != BS_DT_F16)
+    return fail(BS_ERR_UNSUPPORTED, "sparse_attn: dtype tag %d (f32, bf16 or f16)", dtype);
+  if (B * S == 0) return BS_OK;
+  if (!q || !kv || !attn_sink || !topk_idxs || !out) return fail(BS_ERR_INVALID_ARG, "sparse_attn: null pointer");
+  attn::SAArgs a = {};
+  a.q = q; a.kv = kv; a.sink = attn_sink; a.idx = topk_idxs; a.idx64 = idx_int64 ? 1 : 0;
+  a.B = (int)B; a.S = (int)S; a.H = H; a.D = D; a.N = (int)N; a.K = K; a.scale = softmax_scale; a.out = out;
+  sa_split(B * S, K, &a.nsplit, &a.ks);
+  if (a.nsplit > 1) {
+    const size_t need = bs_sparse_attn_workspace_size(B, S, H, D, K);
+    if (!workspace || workspace_bytes < need || !aligned(workspace, 16))
+      return fail(BS_ERR_INVALID_ARG, "sparse_attn: workspace of %zu bytes, %zu needed (16-byte aligned)",
+                  workspace_bytes, need);
+    a.part_o = (float*)workspace;
+    a.part_ml = a.part_o + (size_t)B * S * a.nsplit * H * D;
+  }
+  if (bs_launch_sparse_attn_smem(H, D) > 227 * 1024)
+    return fail(BS_ERR_UNSUPPORTED, "sparse_attn: head dim %d too large for one shared-memory key tile", D);
+  return cuda_status(bs_launch_sparse_attn(a, dtype, (cudaStream_t)stream), "sparse_attn");
+}
+
+size_t bs_indexer_topk_workspace_size(int64_t S, int64_t T) { return (size_t)S * T * sizeof(float); }
+
+int bs_indexer_topk(const void* q, const void* kv, int dtype, const float* weights, int64_t S, int H, int D, int64_t T,
+                    int topk, int ratio, int64_t start_pos, int64_t offset, int64_t* out, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  if (S < 0 || H <= 0 || D <= 0 || T <= 0 || topk <= 0 || topk > T || ratio <= 0 || start_pos < 0)
+    return fail(BS_ERR_INVALID_ARG, "indexer_topk: S=%lld H=%d D=%d T=%lld topk=%d ratio=%d", (long long)S, H, D,
+                (long long)T, topk, ratio);
+  if (T > 16384 || S > 0x7fffffff)
+    return fail(BS_ERR_UNSUPPORTED, "indexer_topk: %lld keys (at most 16384 per query row)", (long long)T);
+  if ((size_t)(H * D + H + 128 * (D + 1)) * sizeof(float) > 227 * 1024)
+    return fail(BS_ERR_UNSUPPORTED, "indexer_topk: heads x head dim %d too large", H * D);
+  if (dtype != BS_DT_F32 && dtype != BS_DT_BF16 && dtype != BS_DT_F16)
+    return fail(BS_ERR_UNSUPPORTED, "indexer_topk: dtype tag %d (f32, bf16 or f16)", dtype);
+  if (S == 0) return BS_OK;
+  if (!q || !kv || !weights || !out || !workspace) return fail(BS_ERR_INVALID_ARG, "indexer_topk: null pointer");
+  if (workspace_bytes < bs_indexer_topk_workspace_size(S, T) || !aligned(workspace, 4))
+    return fail(BS_ERR_INVALID_ARG, "indexer_topk: workspace of %zu bytes, %zu needed", workspace_bytes,
+                bs_indexer_topk_workspace_size(S, T));
+  return cuda_status(bs_launch_indexer_topk(q, kv, dtype, weights, (int)S, H, D, (int)T, topk, ratio,
+                                            start_pos == 0 ? 1 : 0, offset, (float*)workspace, out,
+                                            (cudaStream_t)stream),
+                     "indexer_topk");
 }
 
 int bs_hc_split_sinkhorn(const void* mixes, int mixes_dtype, const float* hc_scale, const float* hc_base, int64_t n,

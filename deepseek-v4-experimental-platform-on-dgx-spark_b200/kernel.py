@@ -23,7 +23,8 @@ import torch
 
 from . import _lib
 
-__all__ = ["act_quant", "fp4_act_quant", "fp8_gemm", "fp4_gemm", "hc_split_sinkhorn", "profile_report"]
+__all__ = ["act_quant", "fp4_act_quant", "fp8_gemm", "fp4_gemm", "sparse_attn", "hc_split_sinkhorn", "indexer_topk",
+           "profile_report"]
 
 # Per-op call counter and host-side seconds, reported by profile_report() in
 # the same columns as the reference module's report (kernel_sm121.py:31-44).
@@ -231,3 +232,56 @@ def hc_split_sinkhorn(mixes: torch.Tensor, hc_scale: torch.Tensor, hc_base: torc
                                                 comb.data_ptr(), _stream(mixes)))
     _tally("hc_sinkhorn", t0)
     return pre, post, comb
+
+
+def sparse_attn(q: torch.Tensor, kv: torch.Tensor, attn_sink: torch.Tensor, topk_idxs: torch.Tensor,
+                softmax_scale: float) -> torch.Tensor:
+    """Sparse attention over gathered keys (kernel_sm121.py:430-486).
+    q [b, s, h, d], kv [b, n, d], attn_sink [h], topk_idxs [b, s, topk]
+    (-1 = no key) -> [b, s, h, d] in q's dtype."""
+    t0 = _time.perf_counter()
+    _require_cuda(q, kv, attn_sink, topk_idxs)
+    b, s, h, d = q.shape
+    n = kv.size(1)
+    k = topk_idxs.size(-1)
+    qc = q.contiguous()
+    if qc.dtype not in _X_DT:
+        qc = qc.float()
+    kvc = kv.contiguous().to(qc.dtype)
+    idx = topk_idxs.contiguous()
+    if idx.dtype not in (torch.int64, torch.int32):
+        idx = idx.long()
+    sink = attn_sink.float().contiguous()
+    lib = _lib.load()
+    out = torch.empty(b, s, h, d, dtype=qc.dtype, device=q.device)
+    wsb = lib.bs_sparse_attn_workspace_size(b, s, h, d, k)
+    ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=q.device)
+    _lib.check(lib.bs_sparse_attn(qc.data_ptr(), kvc.data_ptr(), _X_DT[qc.dtype], sink.data_ptr(), idx.data_ptr(),
+                                  1 if idx.dtype == torch.int64 else 0, b, s, h, d, n, k, float(softmax_scale),
+                                  out.data_ptr(), ws.data_ptr(), ws.numel(), _stream(q)))
+    _tally("sparse_attn", t0)
+    return out if out.dtype == q.dtype else out.to(q.dtype)
+
+
+def indexer_topk(q: torch.Tensor, kv: torch.Tensor, weights: torch.Tensor, topk: int, ratio: int, start_pos: int,
+                 offset: int) -> torch.Tensor:
+    """The Indexer's score -> top-k step of one rank (kernel_sm121.py:597-642):
+    q [1, S, H, D], kv [1, T, D], weights [1, S, H] -> int64 [1, S, topk]
+    (key index + offset in descending score order; in prefill, keys at or
+    beyond (s+1)//ratio are masked and reported as -1)."""
+    t0 = _time.perf_counter()
+    _require_cuda(q, kv, weights)
+    _, S, H, D = q.shape
+    T = kv.size(1)
+    qc = q.contiguous()
+    if qc.dtype not in _X_DT:
+        qc = qc.float()
+    kvc = kv.contiguous().to(qc.dtype)
+    w = weights.float().contiguous()
+    lib = _lib.load()
+    out = torch.empty(1, S, topk, dtype=torch.int64, device=q.device)
+    ws = torch.empty(max(lib.bs_indexer_topk_workspace_size(S, T), 16), dtype=torch.uint8, device=q.device)
+    _lib.check(lib.bs_indexer_topk(qc.data_ptr(), kvc.data_ptr(), _X_DT[qc.dtype], w.data_ptr(), S, H, D, T, topk,
+                                   ratio, start_pos, offset, out.data_ptr(), ws.data_ptr(), ws.numel(), _stream(q)))
+    _tally("indexer_topk", t0)
+    return out

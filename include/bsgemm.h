@@ -140,6 +140,35 @@ int bs_hc_split_sinkhorn(const void* mixes, int mixes_dtype, const float* hc_sca
                          void* stream);
 
 /*
+ * sparse_attn (kernel_sm121.py:430-486): q [B,S,H,D], kv [B,N,D] (same dtype:
+ * f32, bf16 or f16), attn_sink [H] fp32, topk_idxs [B,S,K] (int64 when
+ * idx_int64, else int32; negative = no key) -> out [B,S,H,D] in q's dtype:
+ * softmax over each query's K scores q.kv[idx]*softmax_scale (-inf for
+ * missing keys) together with the head's sink logit, output = the keys'
+ * share of the weights times the gathered keys.  fp32 arithmetic.
+ * H*D <= 8192.  Few queries (decode) split the keys across CTAs: the partial
+ * results need bs_sparse_attn_workspace_size bytes of workspace (0 when
+ * there are enough queries).
+ */
+size_t bs_sparse_attn_workspace_size(int64_t B, int64_t S, int H, int D, int K);
+int bs_sparse_attn(const void* q, const void* kv, int dtype, const float* attn_sink, const void* topk_idxs,
+                   int idx_int64, int64_t B, int64_t S, int H, int D, int64_t N, int K, float softmax_scale,
+                   void* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * The Indexer's score -> top-k step (kernel_sm121.py:597-642, one rank):
+ * q [S,H,D], kv [T,D] (same dtype: f32, bf16 or f16), weights [S,H] fp32 ->
+ * out int64 [S,topk]: score[s,t] = sum_h relu(q[s,h].kv[t]) * weights[s,h];
+ * with start_pos == 0 (prefill) keys t >= (s+1)/ratio are masked; the topk
+ * best keys in descending score (ties: lower key first), plus offset, masked
+ * picks -1.  T <= 16384.  Workspace: the [S,T] fp32 scores.
+ */
+size_t bs_indexer_topk_workspace_size(int64_t S, int64_t T);
+int bs_indexer_topk(const void* q, const void* kv, int dtype, const float* weights, int64_t S, int H, int D, int64_t T,
+                    int topk, int ratio, int64_t start_pos, int64_t offset, int64_t* out, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+/*
  * Tensor-parallel GEMM with the all-gather fused into its epilogue.  This
  * rank holds the weight rows [col0, col0+N) (b, b_s as for bs_fp8_gemm /
  * bs_fp4_gemm) and computes the column slice C[:, col0:col0+N]; every output

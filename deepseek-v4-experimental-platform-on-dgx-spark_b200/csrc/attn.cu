@@ -21,9 +21,9 @@
 
 namespace attn {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 512;
 constexpr int kKT = 16;            // keys per shared-memory tile
-constexpr int kMaxHD = 8192;       // heads x head dim of one query, in registers across the CTA
+constexpr int kMaxHD = 16384;      // heads x head dim of one query, in registers across the CTA
 constexpr int kEPT = kMaxHD / kThreads;
 
 template <typename T>

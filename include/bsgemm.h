@@ -146,7 +146,7 @@ int bs_hc_split_sinkhorn(const void* mixes, int mixes_dtype, const float* hc_sca
  * softmax over each query's K scores q.kv[idx]*softmax_scale (-inf for
  * missing keys) together with the head's sink logit, output = the keys'
  * share of the weights times the gathered keys.  fp32 arithmetic.
- * H*D <= 8192.  Few queries (decode) split the keys across CTAs: the partial
+ * H*D <= 16384.  Few queries (decode) split the keys across CTAs: the partial
  * results need bs_sparse_attn_workspace_size bytes of workspace (0 when
  * there are enough queries).
  */

@@ -49,9 +49,7 @@ def f32_to_bf16(f: np.ndarray) -> np.ndarray:
     with np.errstate(over="ignore"):
         acc += bits
     acc >>= 16
-    out = acc.astype(np.uint16)
-    out[np.isnan(f)] = 0x7FC0
-    return out
+    return np.where(np.isnan(f), np.uint16(0x7FC0), acc.astype(np.uint16)).astype(np.uint16)
 
 
 def f16_to_f32(u16: np.ndarray) -> np.ndarray:

@@ -43,6 +43,7 @@ PKG = "deepseek-v4-experimental-platform-on-dgx-spark_b200"
 NCU_TRAFFIC = {
     "fp8_gemm_4096x4096x4096": 34_120_960 + 2_532_864,
     "fp4_decode_16x4096x4096": 9_046_784 + 0,
+    "moe_experts_1024x256": 3_488_034_816 + 83_452_416,
     # dram__bytes.sum.per_second x duration
     "act_quant_16384x7168": 325_000_000,
     "fp4_act_quant_16384x7168": 410_000_000,
@@ -699,6 +700,8 @@ def bench_moe(args, torch, dist, ws, rank, dev):
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1) if gbs else None, "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 3) if gbs else None,
                          "traffic": NCU_TRAFFIC.get(f"moe_experts_{T // ws}x{E // ws}") if ws == 1 else None,
+                         "traffic_source": "recorded ncu capture of this kernel at this size (not measured in this "
+                                           "run)" if ws == 1 else None,
                          "kernel": "mf::experts_kernel (persistent W1|W3 + W2 grouped GEMMs)",
                          "kernel_ms": round(kern_ms, 4) if kern_ms else None,
                          "algorithmic_bytes": kbytes,

@@ -845,6 +845,77 @@ def bench_quant(args, torch, dist, ws, rank, dev):
     return line
 
 
+def bench_attn_side(args, torch, dist, ws, rank, dev):
+    """The attention-side consumers (one GPU; N GPUs run replicas, weak scaling):
+    hc_split_sinkhorn on [1, 65536, 24] fp32 mixes (hc=4, 20 iterations;
+    HBM GB/s of mixes in + pre/post/comb out), sparse_attn on a 4096-query
+    prefill (16 heads x 576, 512 keys per query from a 1024-row cache, bf16;
+    TFLOP/s of the two contractions), the Indexer's score -> top-k on 4096
+    queries x 1024 keys (64 heads x 128, fp32; TFLOP/s of the scores)."""
+    pkg = __import__("importlib").import_module(PKG)
+    kern = pkg.kernel
+    g = torch.Generator(device=dev)
+    g.manual_seed(31 + rank)
+    peaks, src = load_peaks()
+    if args.workload == "hc_sinkhorn":
+        n, hc = 65536, 4
+        mix = torch.randn(1, n, (2 + hc) * hc, generator=g, device=dev)
+        sc = torch.rand(3, generator=g, device=dev) + 0.5
+        base = torch.randn((2 + hc) * hc, generator=g, device=dev)
+        call = lambda: kern.hc_split_sinkhorn(mix, sc, base, hc, 20, 1e-6)       # noqa: E731
+        work, unit, metric = n * 2 * (2 + hc) * hc * 4, "GB/s", "hc_split_sinkhorn HBM GB/s"
+        bound, peak = "hbm", peaks["hbm_gbs"]
+        cfg = f"hc_split_sinkhorn mixes [1, {n}, {(2 + hc) * hc}] fp32, hc={hc}, 20 iterations"
+        h2d, d2h = n * (2 + hc) * hc * 4, n * (2 + hc) * hc * 4
+    elif args.workload == "sparse_attn":
+        b, sq, h, d, nk, k = 1, 4096, 16, 576, 1024, 512
+        q = torch.randn(b, sq, h, d, generator=g, device=dev).to(torch.bfloat16)
+        kv = torch.randn(b, nk, d, generator=g, device=dev).to(torch.bfloat16)
+        sink = torch.randn(h, generator=g, device=dev)
+        idx = torch.randint(0, nk, (b, sq, k), generator=g, device=dev)
+        call = lambda: kern.sparse_attn(q, kv, sink, idx, d ** -0.5)             # noqa: E731
+        work, unit, metric = 4.0 * b * sq * h * k * d, "TFLOP/s", "sparse_attn TFLOP/s"
+        bound, peak = "tensor", peaks["bf16_tflops"]
+        cfg = f"sparse_attn q [{b}, {sq}, {h}, {d}] bf16, kv [{b}, {nk}, {d}], {k} keys per query"
+        h2d, d2h = q.numel() * 2 + idx.numel() * 8, q.numel() * 2
+    else:
+        sq, h, d, t, k = 4096, 64, 128, 1024, 512
+        q = torch.randn(1, sq, h, d, generator=g, device=dev)
+        kv = torch.randn(1, t, d, generator=g, device=dev)
+        w = torch.randn(1, sq, h, generator=g, device=dev)
+        call = lambda: kern.indexer_topk(q, kv, w, k, 4, 0, 0)                   # noqa: E731
+        work, unit, metric = 2.0 * sq * h * d * t, "TFLOP/s", "Indexer score+top-k TFLOP/s"
+        bound, peak = "tensor", peaks["bf16_tflops"]
+        cfg = f"Indexer q [1, {sq}, {h}, {d}] fp32, kv [1, {t}, {d}], top-{k}, ratio 4, prefill"
+        h2d, d2h = q.numel() * 4 + w.numel() * 4, sq * k * 8
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    clocks = Clocks(torch.cuda.current_device())
+    clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        call()
+    t1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = max_over_ranks(torch, dist, t0.elapsed_time(t1) / args.steps)
+    scale = 1e9 if unit == "GB/s" else 1e12
+    rate = work / (ms * 1e-3) / scale
+    return {"metric": metric, "value": round(ws * rate, 3), "unit": unit, "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp32 arithmetic", "data": "synthetic (seeded)",
+            "config": {"workload": cfg, "parallelism": f"replicas x{ws}" if ws > 1 else "none"},
+            "roofline": {"bound": bound, "achieved": round(rate, 3), "peak": peak, "unit": unit,
+                         "frac": round(rate / peak, 4), "traffic": None,
+                         "peak_source": f"{'hbm_gbs' if bound == 'hbm' else 'bf16_tflops'} of {src} "
+                                        "MEASURED_PEAKS.json"},
+            "e2e": None, "io_bytes_per_step": {"h2d": h2d, "d2h": d2h}, "gpu_launches": args.steps, "clocks": clk}
+
+
 def max_over_ranks(torch, dist, v):
     if dist is None:
         return v
@@ -1108,7 +1179,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["moe", "fp8_prefill", "fp4_decode", "moe_stack", "act_quant",
-                                           "fp4_act_quant"], default="moe")
+                                           "fp4_act_quant", "hc_sinkhorn", "sparse_attn", "indexer"], default="moe")
     ap.add_argument("--tokens", type=int, default=None,
                     help="moe: 1024, moe_stack: 8192, act_quant / fp4_act_quant: 16384 rows")
     ap.add_argument("--experts", type=int, default=256)
@@ -1158,6 +1229,8 @@ def main():
         line = bench_moe_stack(args, torch, dist, ws, rank, dev)
     elif args.workload in ("act_quant", "fp4_act_quant"):
         line = bench_quant(args, torch, dist, ws, rank, dev)
+    elif args.workload in ("hc_sinkhorn", "sparse_attn", "indexer"):
+        line = bench_attn_side(args, torch, dist, ws, rank, dev)
     else:
         line = bench_fp4_decode(args, torch, dist, ws, rank, dev)
 

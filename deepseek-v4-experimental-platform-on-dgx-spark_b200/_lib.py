@@ -62,6 +62,7 @@ SIGNATURES = {
                           _c_void_p],
     "bs_moe_forward_noalloc": [_c_void_p, _c_void_p, _i64, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p,
                                _c_void_p, _c_void_p, _c_void_p, _c_void_p],
+    "bs_moe_gate": [_c_void_p, _c_void_p, _i64, _i32, _i32, _c_void_p, _c_void_p],
     "bs_moe_route": [_c_void_p, _i64, _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p],
     "bs_moe_scan": [_c_void_p, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p],
     "bs_moe_dispatch": [_c_void_p, _i64, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32,

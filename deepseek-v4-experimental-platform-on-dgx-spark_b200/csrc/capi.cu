@@ -653,6 +653,20 @@ int bs_ep_moe_forward(const void* x, const float* logits, int64_t T, int64_t max
   return cuda_status(e, "ep_moe_forward");
 }
 
+int bs_moe_gate(const void* x, const void* gate_w, int64_t T, int E, int H, float* logits, void* stream) {
+  if (T < 0 || T > 0x7fffffff || E <= 0 || E % 16 || E > 1024 || H <= 0 || H % 64)
+    return fail(BS_ERR_UNSUPPORTED, "moe_gate: T=%lld E=%d H=%d (E a multiple of 16 up to 1024, H of 64)",
+                (long long)T, E, H);
+  if (T == 0) return BS_OK;
+  if (!x || !gate_w || !logits || !aligned(x, 16) || !aligned(gate_w, 16) || !aligned(logits, 16))
+    return fail(BS_ERR_INVALID_ARG, "moe_gate: null or misaligned pointer (16 B)");
+  cudaError_t e;
+  const int r = bs_launch_moe_gate(x, gate_w, (int)T, E, H, logits, (cudaStream_t)stream, &e);
+  if (r == BS_ERR_UNSUPPORTED) return fail(r, "moe_gate: could not build TMA descriptors");
+  if (r) return cuda_status(e, "moe_gate");
+  return BS_OK;
+}
+
 int bs_moe_route(const float* logits, int64_t T, int E, int topk, int* idx, float* w, int* counts, void* stream) {
   if (T < 0 || E <= 0 || E > 1024 || topk <= 0 || topk > 8 || topk > E)
     return fail(BS_ERR_UNSUPPORTED, "moe_route: T=%lld E=%d topk=%d", (long long)T, E, topk);

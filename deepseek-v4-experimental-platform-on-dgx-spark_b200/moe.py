@@ -21,7 +21,7 @@ import torch
 
 from . import _lib
 
-__all__ = ["moe_forward", "MoEWeights", "MoEWorkspace", "pack_scales"]
+__all__ = ["moe_forward", "gate_logits", "MoEWeights", "MoEWorkspace", "pack_scales"]
 
 
 def pack_scales(w_s: torch.Tensor) -> torch.Tensor:
@@ -82,9 +82,35 @@ def _u8(t: torch.Tensor) -> torch.Tensor:
     return t.contiguous().view(torch.uint8)
 
 
-def moe_forward(x: torch.Tensor, logits: torch.Tensor, weights: MoEWeights, topk: int,
-                out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
-    """MoE layer: x bf16 [T, H], logits fp32 [T, E] -> bf16 [T, H]."""
+def gate_logits(x: torch.Tensor, gate_weight: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Gate projection on the tensor cores: x bf16 [T, H] . gate_weight bf16
+    [E, H]^T -> fp32 logits [T, E] (the routing input of moe_forward)."""
+    if not (x.is_cuda and gate_weight.is_cuda):
+        raise RuntimeError("gate_logits runs on CUDA tensors only (no CPU fallback)")
+    if x.dtype != torch.bfloat16 or gate_weight.dtype != torch.bfloat16:
+        raise TypeError("gate_logits expects bf16 activations and gate weights")
+    T, H = x.shape
+    E = gate_weight.shape[0]
+    if gate_weight.shape[1] != H:
+        raise ValueError(f"gate weight {tuple(gate_weight.shape)} does not match hidden {H}")
+    if out is None:
+        out = torch.empty(T, E, dtype=torch.float32, device=x.device)
+    xc, wc = x.contiguous(), gate_weight.contiguous()
+    _lib.check(_lib.load().bs_moe_gate(xc.data_ptr(), wc.data_ptr(), T, E, H, out.data_ptr(),
+                                       torch.cuda.current_stream(x.device).cuda_stream))
+    return out
+
+
+def moe_forward(x: torch.Tensor, logits: torch.Tensor | None, weights: MoEWeights, topk: int,
+                out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+                gate_weight: torch.Tensor | None = None) -> torch.Tensor:
+    """MoE layer: x bf16 [T, H], logits fp32 [T, E] -> bf16 [T, H].  With
+    ``gate_weight`` (bf16 [E, H]) instead of logits, the gate projection runs
+    first on the device (gate_logits), then the same layer."""
+    if logits is None:
+        if gate_weight is None:
+            raise ValueError("moe_forward needs gate logits or a gate weight")
+        logits = gate_logits(x, gate_weight)
     if not (x.is_cuda and logits.is_cuda):
         raise RuntimeError("moe_forward runs on CUDA tensors only (no CPU fallback)")
     T, H = x.shape

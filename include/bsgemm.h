@@ -254,6 +254,14 @@ int bs_moe_forward_staged(const void* x, const float* logits, int64_t T, int H, 
  * (cudaEvent_t) on its stream around its experts kernel, then forgets them. */
 void bs_moe_time_experts(void* ev_begin, void* ev_end);
 
+/* Gate projection in front of the routing: logits [T,E] fp32 = x [T,H] bf16
+ * times gate_w [E,H] bf16 transposed, on the tensor cores (tcgen05 kind::f16,
+ * fp32 accumulation).  E a multiple of 16 (<= 1024), H a multiple of 64.
+ * Feeds bs_moe_forward / bs_ep_moe_forward on the same stream: gate, route and
+ * experts with no host round trip (the caller's gate + top-k, in DeepSeek's
+ * model file, outside the reference). */
+int bs_moe_gate(const void* x, const void* gate_w, int64_t T, int E, int H, float* logits, void* stream);
+
 /* Building blocks (expert-parallel form; the caller moves rows between
  * ranks).  route: idx/w [T,topk], counts [E] (zeroed, then filled). */
 int bs_moe_route(const float* logits, int64_t T, int E, int topk, int* idx, float* w, int* counts, void* stream);

@@ -2,7 +2,8 @@
 """Benchmark of the block-scaled GEMM path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload moe|fp8_prefill|fp4_decode|moe_stack|act_quant|fp4_act_quant]
+                    [--workload moe|fp8_prefill|fp4_decode|moe_stack|act_quant|fp4_act_quant|
+                                hc_sinkhorn|sparse_attn|indexer]
 
 Default workload (one "step"): the grouped FP8 x FP4 MoE layer -- 1024 tokens,
 hidden 4096, inter 2048, 256 experts, top-8 -- through the library's

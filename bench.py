@@ -7,7 +7,7 @@
 
 Default workload (one "step"): the grouped FP8 x FP4 MoE layer -- 1024 tokens,
 hidden 4096, inter 2048, 256 experts, top-8 -- through the library's
-three-kernel layer; at N>1 GPUs expert parallel (each rank its own tokens and
+single-kernel layer; at N>1 GPUs expert parallel (each rank its own tokens and
 E/N experts, rows exchanged over NVLink peer memory inside the layer's
 kernels), total batch fixed (strong scaling).  The same line carries the
 4096^3 prefill fp8_gemm / fp4_gemm rates (one GPU).
@@ -44,7 +44,7 @@ PKG = "deepseek-v4-experimental-platform-on-dgx-spark_b200"
 NCU_TRAFFIC = {
     "fp8_gemm_4096x4096x4096": 34_120_960 + 2_532_864,
     "fp4_decode_16x4096x4096": 9_046_784 + 0,
-    "moe_experts_1024x256": 3_488_034_816 + 83_452_416,
+    "moe_layer_1024x256": None,
     # dram__bytes.sum.per_second x duration
     "act_quant_16384x7168": 325_000_000,
     "fp4_act_quant_16384x7168": 410_000_000,
@@ -571,7 +571,8 @@ def bench_moe(args, torch, dist, ws, rank, dev):
     1024), H=4096, I=2048, E=256 experts, top-8 of N(0,1) gate logits,
     weights = softmax over the top 8.
 
-    One GPU: the whole layer (bs_moe_forward: front, experts, combine).  N
+    One GPU: the whole layer (bs_moe_forward: one kernel whose phases are
+    quantise + route + dispatch, the grouped GEMMs, and the combine).  N
     GPUs: expert parallel -- rank r owns tokens [r*T/N, (r+1)*T/N) and
     experts [r*E/N, (r+1)*E/N); rows travel to the expert owners and back
     over NVLink peer memory inside the layer's own kernels (or, with
@@ -598,14 +599,14 @@ def bench_moe(args, torch, dist, ws, rank, dev):
     if ws == 1:
         def call(xd, ld, o):
             return moe.moe_forward(xd, ld, weights, k, out=o)
-        launches = 3
+        launches = 1
     else:
         ep = importlib.import_module(PKG + ".ep")
         layer = ep.EPMoE(weights, E, k, max_tokens=tl, transport=args.ep_transport)
 
         def call(xd, ld, o):
             return layer.forward(xd, ld, out=o)
-        launches = 3 if args.ep_transport == "peer" else 9
+        launches = 1 if args.ep_transport == "peer" else 9
     step = lambda: call(xl, ll, outs[0])                                        # noqa: E731
     if ws > 1 and args.ep_transport == "peer":
         # no host sync inside the layer: capture it once, replay one graph per step
@@ -638,8 +639,8 @@ def bench_moe(args, torch, dist, ws, rank, dev):
     clk = clocks.stop()
     ms = max_over_ranks(torch, dist, t0.elapsed_time(t1) / args.steps)
 
-    # the dominant kernel (persistent W1|W3 + W2 grouped GEMMs), timed live
-    # with events the library records around it on the launching stream
+    # the layer kernel (all of the layer's work), timed live with events the
+    # library records around it on the launching stream
     kern_ms = None
     if args.ep_transport == "peer" or ws == 1:
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
@@ -658,12 +659,16 @@ def bench_moe(args, torch, dist, ws, rank, dev):
     top = torch.topk(logits, k, dim=1).indices
     recv = int(((top >= rank * El) & (top < (rank + 1) * El)).sum().item())
     wbytes = w13.numel() + w13_s.numel() + w2.numel() + w2_s.numel()            # this rank's weights + scales
-    # activation bytes of the experts kernel: received rows + their scales in,
-    # hidden rows written and read back, bf16 outputs out
-    abytes = recv * (H + H // 32) + 2 * recv * (I + I // 32) + recv * H * 2
+    # activation bytes of this rank's HBM: its bf16 tokens and fp32 logits in,
+    # received e4m3 rows + scale words written (by the dispatch) and read (by
+    # the GEMMs), hidden rows written and read, its rows' bf16 expert outputs
+    # written (by the owners) and read (by the combine), bf16 output out
+    abytes = (tl * (H * 2 + E * 4) + 2 * recv * (H + H // 32) + 2 * recv * (I + I // 32) + 2 * tl * k * H * 2
+              + tl * H * 2)
     kbytes = wbytes + abytes
     peaks, src = load_peaks()
     gbs = kbytes / (kern_ms * 1e-3) / 1e9 if kern_ms else None
+    traffic = NCU_TRAFFIC.get(f"moe_layer_{T // ws}x{E // ws}") if ws == 1 else None
 
     # end to end through the public API: pinned host bf16 tokens and fp32 gate
     # logits -> device -> the layer -> pinned host output, consecutive steps
@@ -700,14 +705,16 @@ def bench_moe(args, torch, dist, ws, rank, dev):
                        "l2": f"expert weights {wbytes * ws / 2**30:.2f} GiB >> L2 (every step streams them)"},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1) if gbs else None, "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 3) if gbs else None,
-                         "traffic": NCU_TRAFFIC.get(f"moe_experts_{T // ws}x{E // ws}") if ws == 1 else None,
+                         "traffic": traffic,
                          "traffic_source": "recorded ncu capture of this kernel at this size (not measured in this "
-                                           "run)" if ws == 1 else None,
-                         "kernel": "mf::experts_kernel (persistent W1|W3 + W2 grouped GEMMs)",
+                                           "run)" if traffic else None,
+                         "kernel": "mf::layer_kernel (the whole layer: quantise + route + dispatch, persistent "
+                                   "W1|W3 + W2 grouped GEMMs, combine)",
                          "kernel_ms": round(kern_ms, 4) if kern_ms else None,
                          "algorithmic_bytes": kbytes,
-                         "note": "this rank's expert weights + scales, received rows, hidden rows written and read, "
-                                 "outputs, per launch / the kernel's event-timed duration (max over ranks)",
+                         "note": "this rank's expert weights + scales, tokens + logits in, received rows written and "
+                                 "read, hidden rows written and read, returned outputs written and read, output out, "
+                                 "per launch / the kernel's event-timed duration (max over ranks)",
                          "peak_source": f"hbm_gbs of {src} MEASURED_PEAKS.json"},
             "e2e": {"value": round(T / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": ws * tl * (H * 2 + E * 4), "d2h_bytes_per_step": ws * tl * H * 2,

@@ -388,16 +388,15 @@ MoeLayout moe_layout(int64_t T, int H, int I, int E, int topk) {
 }  // namespace
 
 namespace {
-// Sizes the three-kernel layer supports: two 128-row W2 tiles per work item
+// Sizes the single-kernel layer supports: two 128-row W2 tiles per work item
 // (H a multiple of 256) and return addresses of 24 bits.
 bool fused_ok(int64_t T, int H, int topk) { return H % 256 == 0 && T * topk < (int64_t(1) << 24); }
 
-// Workspace of the three-kernel layer.  `local_only`: the expert-parallel
+// Workspace of the single-kernel layer.  `local_only`: the expert-parallel
 // form, whose receive buffers, count matrix, return buffer and sync words
 // live in peer-mapped memory the caller passes separately.
 struct FusedLayout {
-  size_t sync, counts, cursor, zero_end, cnt_all, xq, xs, idx, w, offsets, chunks, hq, hsp, hdone, rows, rows_sp, ret,
-      y_back, total;
+  size_t sync, counts, zero_end, cnt_all, xq, xs, idx, slot, w, hq, hsp, hdone, rows, rows_sp, ret, y_back, total;
   int64_t cap, chunk_cap;
 };
 FusedLayout fused_layout(int64_t T_max, int H, int I, int E, int topk, int n_ranks, bool local_only) {
@@ -410,15 +409,13 @@ FusedLayout fused_layout(int64_t T_max, int H, int I, int E, int topk, int n_ran
   // cleared before every single-GPU call (one memset): sync words, counters
   L.sync = local_only ? 0 : take(8 * (size_t)mf::kSyncWords);
   L.counts = take(4 * 2 * (size_t)E);
-  L.cursor = take(4 * 2 * (size_t)E);
   L.zero_end = o;
   L.cnt_all = local_only ? 0 : take(8 * (size_t)E);
   L.xq = take((size_t)T_max * H);
   L.xs = take((size_t)T_max * (H / 128));
   L.idx = take(4 * (size_t)T_max * topk);
+  L.slot = take(4 * (size_t)T_max * topk);
   L.w = take(4 * (size_t)T_max * topk);
-  L.offsets = take(4 * (size_t)(El + 1));
-  L.chunks = take(4 * (size_t)(El + 1));
   L.hq = take((size_t)L.cap * I);
   L.hsp = take((size_t)L.chunk_cap * (I / 128) * 512);
   L.hdone = take(4 * (size_t)L.chunk_cap);
@@ -474,23 +471,18 @@ static int moe_forward_fused(const void* x, const float* logits, int64_t T, int 
   cudaError_t e = cudaMemsetAsync(ws, 0, L.zero_end, s);   // epoch and counters: every call is epoch 1
   if (e != cudaSuccess) return cuda_status(e, "moe: clearing the sync words");
   mf::Layer ly = {};
-  mf::FrontArgs& f = ly.f;
-  f.x = (const __nv_bfloat16*)x; f.logits = logits;
-  f.T = (int)T; f.H = H; f.E = E; f.topk = topk; f.El = E; f.n = 1; f.me = 0;
-  f.cap = L.cap; f.chunk_cap = L.chunk_cap;
-  f.xq = ws + L.xq; f.xs = ws + L.xs; f.idx = (int*)(ws + L.idx); f.w = (float*)(ws + L.w);
-  f.counts = (int*)(ws + L.counts); f.cursor = (int*)(ws + L.cursor);
-  f.offsets = (int*)(ws + L.offsets); f.chunk_prefix = (int*)(ws + L.chunks); f.h_done = (int*)(ws + L.hdone);
-  f.w13 = (const uint8_t*)w13; f.w13_sp = (const uint8_t*)w13_sp; f.I = I;
-  mf::ExpArgs& xa = ly.x;
-  xa.E = E; xa.H = H; xa.I = I; xa.n = 1; xa.me = 0; xa.cap = L.cap;
-  xa.offsets = f.offsets; xa.chunk_prefix = f.chunk_prefix; xa.a_sp = ws + L.rows_sp; xa.ret = (const int*)(ws + L.ret);
-  xa.w13_sp = (const uint8_t*)w13_sp; xa.w2_sp = (const uint8_t*)w2_sp;
-  xa.hq = ws + L.hq; xa.hs_p = ws + L.hsp; xa.h_done = f.h_done;
+  mf::LayerArgs& a = ly.a;
+  a.x = (const __nv_bfloat16*)x; a.logits = logits; a.out = (__nv_bfloat16*)out;
+  a.T = (int)T; a.H = H; a.I = I; a.E = E; a.topk = topk; a.El = E; a.n = 1; a.me = 0;
+  a.cap = L.cap; a.chunk_cap = L.chunk_cap;
+  a.xq = ws + L.xq; a.xs = ws + L.xs; a.idx = (int*)(ws + L.idx); a.slot = (int*)(ws + L.slot);
+  a.w = (float*)(ws + L.w); a.counts = (int*)(ws + L.counts); a.h_done = (int*)(ws + L.hdone);
+  a.w13 = (const uint8_t*)w13; a.w13_sp = (const uint8_t*)w13_sp; a.w2_sp = (const uint8_t*)w2_sp;
+  a.hq = ws + L.hq; a.hs_p = ws + L.hsp;
   ly.pr.cnt_all[0] = (int*)(ws + L.cnt_all); ly.pr.rows[0] = ws + L.rows; ly.pr.rows_sp[0] = ws + L.rows_sp;
   ly.pr.ret[0] = (int*)(ws + L.ret); ly.pr.y_back[0] = (__nv_bfloat16*)(ws + L.y_back);
   ly.pr.sync[0] = (unsigned long long*)(ws + L.sync);
-  ly.w13 = w13; ly.w2 = w2; ly.out = (__nv_bfloat16*)out; ly.wts = f.w;
+  ly.w2 = w2;
   int status = 0;
   e = mf::run_layer(ly, s, &status);
   if (status) return fail(status, "moe: could not build TMA descriptors");
@@ -570,7 +562,7 @@ int moe_forward_staged(const void* x, const float* logits, int64_t T, int H, int
 }  // namespace
 
 // ---------------------------------------------------------------------------
-// expert-parallel layer over peer memory (three kernels, no NCCL, no host sync)
+// expert-parallel layer over peer memory (one kernel, no NCCL, no host sync)
 // ---------------------------------------------------------------------------
 
 static int check_ep(const char* name, int64_t T_max, int H, int I, int E, int topk, int rank, int n_ranks) {
@@ -625,14 +617,14 @@ int bs_ep_moe_forward(const void* x, const float* logits, int64_t T, int64_t max
   uint8_t* ws = (uint8_t*)workspace;
   const int El = E / n_ranks;
   mf::Layer ly = {};
-  mf::FrontArgs& f = ly.f;
-  f.x = (const __nv_bfloat16*)x; f.logits = logits;
-  f.T = (int)T; f.H = H; f.E = E; f.topk = topk; f.El = El; f.n = n_ranks; f.me = rank;
-  f.cap = L.cap; f.chunk_cap = L.chunk_cap;
-  f.xq = ws + L.xq; f.xs = ws + L.xs; f.idx = (int*)(ws + L.idx); f.w = (float*)(ws + L.w);
-  f.counts = (int*)(ws + L.counts); f.cursor = (int*)(ws + L.cursor);
-  f.offsets = (int*)(ws + L.offsets); f.chunk_prefix = (int*)(ws + L.chunks); f.h_done = (int*)(ws + L.hdone);
-  f.w13 = (const uint8_t*)w13; f.w13_sp = (const uint8_t*)w13_sp; f.I = I;
+  mf::LayerArgs& a = ly.a;
+  a.x = (const __nv_bfloat16*)x; a.logits = logits; a.out = (__nv_bfloat16*)out;
+  a.T = (int)T; a.H = H; a.I = I; a.E = E; a.topk = topk; a.El = El; a.n = n_ranks; a.me = rank;
+  a.cap = L.cap; a.chunk_cap = L.chunk_cap;
+  a.xq = ws + L.xq; a.xs = ws + L.xs; a.idx = (int*)(ws + L.idx); a.slot = (int*)(ws + L.slot);
+  a.w = (float*)(ws + L.w); a.counts = (int*)(ws + L.counts); a.h_done = (int*)(ws + L.hdone);
+  a.w13 = (const uint8_t*)w13; a.w13_sp = (const uint8_t*)w13_sp; a.w2_sp = (const uint8_t*)w2_sp;
+  a.hq = ws + L.hq; a.hs_p = ws + L.hsp;
   for (int q = 0; q < n_ranks; ++q) {
     ly.pr.cnt_all[q] = (int*)peer_bufs[0 * n_ranks + q];
     ly.pr.rows[q] = (uint8_t*)peer_bufs[1 * n_ranks + q];
@@ -641,12 +633,7 @@ int bs_ep_moe_forward(const void* x, const float* logits, int64_t T, int64_t max
     ly.pr.y_back[q] = (__nv_bfloat16*)peer_bufs[4 * n_ranks + q];
     ly.pr.sync[q] = (unsigned long long*)peer_bufs[5 * n_ranks + q];
   }
-  mf::ExpArgs& xa = ly.x;
-  xa.E = El; xa.H = H; xa.I = I; xa.n = n_ranks; xa.me = rank; xa.cap = L.cap;
-  xa.offsets = f.offsets; xa.chunk_prefix = f.chunk_prefix; xa.a_sp = ly.pr.rows_sp[rank]; xa.ret = ly.pr.ret[rank];
-  xa.w13_sp = (const uint8_t*)w13_sp; xa.w2_sp = (const uint8_t*)w2_sp;
-  xa.hq = ws + L.hq; xa.hs_p = ws + L.hsp; xa.h_done = f.h_done;
-  ly.w13 = w13; ly.w2 = w2; ly.out = (__nv_bfloat16*)out; ly.wts = f.w;
+  ly.w2 = w2;
   int status = 0;
   cudaError_t e = mf::run_layer(ly, (cudaStream_t)stream, &status);
   if (status) return fail(status, "ep_moe_forward: could not build TMA descriptors");

@@ -5,8 +5,9 @@
 // kernel time on long prompts in the reference's own profile), each a full
 // pass over [tokens, hc, hc].  Here one thread owns one token: the mixes are
 // staged through shared memory by the block (coalesced), the sigmoid /
-// softmax / Sinkhorn steps run in registers, and pre / post / comb leave
-// through shared memory again.  The op is HBM-bound: (2+hc)*hc input values
+// softmax / Sinkhorn steps run in registers -- with hc = 2, 4 or 8 one thread
+// per row of comb, column sums over the token's lanes -- and pre / post /
+// comb leave through shared memory again.  The op is HBM-bound: (2+hc)*hc input values
 // and the same number of fp32 outputs per token.
 //
 // Arithmetic follows the reference step by step in fp32: sigmoid as
@@ -106,19 +107,105 @@ __global__ void __launch_bounds__(kTokens) sinkhorn_kernel(const TIn* __restrict
   for (int i = threadIdx.x; i < nt * HC * HC; i += kTokens) comb[t0 * HC * HC + i] = o_comb[i];
 }
 
+// HC threads per token (HC = 2, 4 or 8 divides the warp): thread r of a
+// token owns row r of comb and entry r of pre / post; row sums stay in the
+// thread, column sums are shuffle reductions over the token's HC lanes in
+// row order (the same order as one thread summing r = 0..HC-1).
+template <int HC, typename TIn>
+__global__ void __launch_bounds__(kTokens) sinkhorn_rows_kernel(const TIn* __restrict__ mixes,
+                                                                const float* __restrict__ scale,
+                                                                const float* __restrict__ base, int64_t n, int iters,
+                                                                float eps, float* __restrict__ pre,
+                                                                float* __restrict__ post, float* __restrict__ comb) {
+  constexpr int kMix = (2 + HC) * HC;
+  constexpr int kTok = kTokens / HC;                 // tokens per block
+  __shared__ float s_in[kTok * kMix];
+  __shared__ float s_base[kMix];
+  const int64_t t0 = (int64_t)blockIdx.x * kTok;
+  const int nt = (int)min((int64_t)kTok, n - t0);
+  for (int i = threadIdx.x; i < nt * kMix; i += kTokens) s_in[i] = bs_to_f32(mixes[t0 * kMix + i]);
+  if (threadIdx.x < kMix) s_base[threadIdx.x] = base[threadIdx.x];
+  __syncthreads();
+  const int tok = threadIdx.x / HC, r = threadIdx.x % HC;
+  const bool live = tok < nt;
+  const float* m = s_in + (live ? tok : 0) * kMix;
+  const float s0 = scale[0], s1 = scale[1], s2 = scale[2];
+  const float a = __fadd_rn(__fmul_rn(m[r], s0), s_base[r]);
+  const float p = __fadd_rn(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-a))), eps);
+  const float b = __fadd_rn(__fmul_rn(m[HC + r], s1), s_base[HC + r]);
+  const float q = __fmul_rn(2.0f, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-b))));
+  float c[HC];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int k = 0; k < HC; ++k) {
+    c[k] = __fadd_rn(__fmul_rn(m[2 * HC + r * HC + k], s2), s_base[2 * HC + r * HC + k]);
+    mx = fmaxf(mx, c[k]);
+  }
+  float sum = 0.0f;
+#pragma unroll
+  for (int k = 0; k < HC; ++k) {
+    c[k] = expf(__fsub_rn(c[k], mx));
+    sum = __fadd_rn(sum, c[k]);
+  }
+#pragma unroll
+  for (int k = 0; k < HC; ++k) c[k] = __fadd_rn(__fdiv_rn(c[k], sum), eps);
+  const int lane = threadIdx.x & 31;
+  const int g0 = lane - r;                           // first lane of this token's group
+  for (int it = 0; it < iters; ++it) {
+    if (it > 0) {
+      float rs = 0.0f;
+#pragma unroll
+      for (int k = 0; k < HC; ++k) rs = __fadd_rn(rs, c[k]);
+      rs = __fadd_rn(rs, eps);
+#pragma unroll
+      for (int k = 0; k < HC; ++k) c[k] = __fdiv_rn(c[k], rs);
+    }
+#pragma unroll
+    for (int k = 0; k < HC; ++k) {
+      float cs = 0.0f;
+#pragma unroll
+      for (int j = 0; j < HC; ++j) cs = __fadd_rn(cs, __shfl_sync(0xffffffffu, c[k], g0 + j));
+      cs = __fadd_rn(cs, eps);
+      c[k] = __fdiv_rn(c[k], cs);
+    }
+  }
+  __syncthreads();   // s_in is reused for the outputs: [pre | post | comb] per block
+  float* o_pre = s_in;
+  float* o_post = s_in + kTok * HC;
+  float* o_comb = s_in + 2 * kTok * HC;
+  if (live) {
+    o_pre[tok * HC + r] = p;
+    o_post[tok * HC + r] = q;
+#pragma unroll
+    for (int k = 0; k < HC; ++k) o_comb[tok * HC * HC + r * HC + k] = c[k];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < nt * HC; i += kTokens) {
+    pre[t0 * HC + i] = o_pre[i];
+    post[t0 * HC + i] = o_post[i];
+  }
+  for (int i = threadIdx.x; i < nt * HC * HC; i += kTokens) comb[t0 * HC * HC + i] = o_comb[i];
+}
+
+template <int HC, typename TIn>
+void launch_t(const TIn* mixes, const float* scale, const float* base, int64_t n, int iters, float eps, float* pre,
+              float* post, float* comb, cudaStream_t st) {
+  if constexpr (HC == 2 || HC == 4 || HC == 8) {
+    const int64_t blocks = (n + kTokens / HC - 1) / (kTokens / HC);
+    sinkhorn_rows_kernel<HC, TIn><<<(unsigned)blocks, kTokens, 0, st>>>(mixes, scale, base, n, iters, eps, pre, post,
+                                                                        comb);
+  } else {
+    const int64_t blocks = (n + kTokens - 1) / kTokens;
+    sinkhorn_kernel<HC, TIn><<<(unsigned)blocks, kTokens, 0, st>>>(mixes, scale, base, n, iters, eps, pre, post, comb);
+  }
+}
+
 template <int HC>
 cudaError_t launch(const void* mixes, int dtype, const float* scale, const float* base, int64_t n, int iters, float eps,
                    float* pre, float* post, float* comb, cudaStream_t st) {
-  const int64_t blocks = (n + kTokens - 1) / kTokens;
-  if (dtype == BS_DT_BF16)
-    sinkhorn_kernel<HC, __nv_bfloat16><<<(unsigned)blocks, kTokens, 0, st>>>(
-        (const __nv_bfloat16*)mixes, scale, base, n, iters, eps, pre, post, comb);
-  else if (dtype == BS_DT_F16)
-    sinkhorn_kernel<HC, __half><<<(unsigned)blocks, kTokens, 0, st>>>((const __half*)mixes, scale, base, n, iters, eps,
-                                                                       pre, post, comb);
-  else
-    sinkhorn_kernel<HC, float><<<(unsigned)blocks, kTokens, 0, st>>>((const float*)mixes, scale, base, n, iters, eps,
-                                                                      pre, post, comb);
+  if (dtype == BS_DT_BF16) launch_t<HC>((const __nv_bfloat16*)mixes, scale, base, n, iters, eps, pre, post, comb, st);
+  else if (dtype == BS_DT_F16) launch_t<HC>((const __half*)mixes, scale, base, n, iters, eps, pre, post, comb, st);
+  else launch_t<HC>((const float*)mixes, scale, base, n, iters, eps, pre, post, comb, st);
   return cudaGetLastError();
 }
 

@@ -10,16 +10,16 @@ rank sees all tokens and the partial MoE outputs are all-reduced instead.
 
 Two transports move the rows:
 
-* ``peer`` (default on GPUs): the whole layer is three kernels of this
-  library (bs_ep_moe_forward), with no NCCL call, no host round trip and no
-  separate barrier: the front kernel quantises and routes this rank's
+* ``peer`` (default on GPUs): the whole layer is one cooperative kernel of
+  this library (bs_ep_moe_forward), with no NCCL call, no host round trip
+  and no separate barrier: its front phase quantises and routes this rank's
   tokens, exchanges the per-expert counts through peer memory, and writes
   every (token, slot) row with its scales and a return address straight to
-  its final expert-major place in the owning rank's receive buffer; the
-  experts kernel (W1|W3 and W2 grouped GEMMs in one persistent launch)
-  starts once every rank's rows are in and stores each output row straight
-  back into the source rank's return buffer; the combine kernel waits for
-  every rank's returns.  The receive buffers, count matrix, return buffer
+  its final expert-major place in the owning rank's receive buffer; its
+  experts phase (W1|W3 and W2 grouped GEMMs, persistent) starts once every
+  rank's rows are in and stores each output row straight back into the
+  source rank's return buffer; its combine phase waits for every rank's
+  returns.  The receive buffers, count matrix, return buffer
   and sync words live in symmetric memory mapped by every rank.
 * ``nccl`` (and the CPU tests on gloo):
   1. counts      all-to-all of the per-(destination, local expert) row counts
@@ -178,7 +178,7 @@ class EPMoE:
         self.y_back = torch.empty(R, H, dtype=torch.bfloat16, device=dev)
 
     def _init_peer(self):
-        """The three-kernel layer (bs_ep_moe_forward): a local workspace and
+        """The single-kernel layer (bs_ep_moe_forward): a local workspace and
         six symmetric buffers per rank that peers write (count matrix, receive
         rows, their packed scales, return addresses, returned outputs, sync
         words), with one pointer list over all ranks."""

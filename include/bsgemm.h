@@ -232,11 +232,10 @@ size_t bs_moe_workspace_size(int64_t T, int H, int I, int E, int topk);
 /* Whole layer on one GPU: x bf16 [T,H], gate logits fp32 [T,E] -> out bf16
  * [T,H].  Routing: top-k logits, weights = softmax over the k selected.
  * w13_sp / w2_sp are the packed scales from bs_moe_pack_scales.
- * With H a multiple of 256 the layer runs as three kernels (front: quantise +
- * route + expert-sorted dispatch; experts: one persistent launch over the
- * W1|W3 and W2 grouped GEMMs; combine) after a small memset of the
- * workspace's counters; otherwise as the staged sequence below.  Both give
- * the same bits. */
+ * With H a multiple of 256 the layer runs as one cooperative kernel (phases:
+ * quantise + route + expert-sorted dispatch; persistent W1|W3 and W2 grouped
+ * GEMMs; combine) after a small memset of the workspace's counters;
+ * otherwise as the staged sequence below.  Both give the same bits. */
 int bs_moe_forward(const void* x, const float* logits, int64_t T, int H, int I, int E, int topk, const void* w13,
                    const void* w13_sp, const void* w2, const void* w2_sp, void* out, void* workspace,
                    size_t workspace_bytes, void* stream);
@@ -249,9 +248,9 @@ int bs_moe_forward_staged(const void* x, const float* logits, int64_t T, int H, 
                           const void* w13, const void* w13_sp, const void* w2, const void* w2_sp, void* out,
                           void* workspace, size_t workspace_bytes, void* stream);
 
-/* Profiling hook: the next three-kernel layer call (bs_moe_forward or
+/* Profiling hook: the next single-kernel layer call (bs_moe_forward or
  * bs_ep_moe_forward) made on this host thread records ev_begin / ev_end
- * (cudaEvent_t) on its stream around its experts kernel, then forgets them. */
+ * (cudaEvent_t) on its stream around its layer kernel, then forgets them. */
 void bs_moe_time_experts(void* ev_begin, void* ev_end);
 
 /* Gate projection in front of the routing: logits [T,E] fp32 = x [T,H] bf16
@@ -353,12 +352,12 @@ int bs_ep_experts_return(int E_local, int64_t capacity, int H, int I, const void
                          void* hq, void* hs_p, void* stream);
 
 /* ------------------------------------------------------------------------
- * Expert-parallel layer in three kernels over peer memory (the default
+ * Expert-parallel layer in one kernel over peer memory (the default
  * expert-parallel path; no NCCL, no host round trip).  Experts split into
  * contiguous ranges of E/n_ranks (the reference's loader ranges,
  * weight_loader.py:112-115); each rank brings its own tokens
  * (T <= max_tokens, the same max_tokens on every rank) and gets their layer
- * output back in `out`.
+ * output back in `out`.  The kernel's phases:
  *   front    quantise + route this rank's tokens, exchange the per-expert
  *            counts, write every (token, slot) row, its scales and its
  *            return address straight into the owning rank's receive buffers

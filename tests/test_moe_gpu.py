@@ -73,8 +73,8 @@ def _staged(x, logits, W, topk):
 @pytest.mark.parametrize("T,H,inter,E,topk,skew", [(64, 512, 256, 16, 4, False), (1, 256, 128, 8, 2, False),
                                                    (700, 1024, 512, 64, 8, True), (333, 4096, 2048, 256, 8, False),
                                                    (2048, 4096, 2048, 32, 8, True)])
-def test_three_kernel_layer_equals_staged(T, H, inter, E, topk, skew):
-    """The three-kernel layer (front / persistent W1|W3 + W2 / combine) gives
+def test_layer_kernel_equals_staged(T, H, inter, E, topk, skew):
+    """The single-kernel layer (front / persistent W1|W3 + W2 / combine) gives
     the staged sequence's bits, including experts with several token chunks
     (skewed routing) and a single token; two calls in a row agree."""
     mm = moe_mod()

@@ -396,7 +396,7 @@ bool fused_ok(int64_t T, int H, int topk) { return H % 256 == 0 && T * topk < (i
 // form, whose receive buffers, count matrix, return buffer and sync words
 // live in peer-mapped memory the caller passes separately.
 struct FusedLayout {
-  size_t sync, counts, zero_end, cnt_all, xq, xs, idx, slot, w, hq, hsp, hdone, rows, rows_sp, ret, y_back, total;
+  size_t sync, counts, zero_end, cnt_all, xq, xs, idx, slot, w, sched, hq, hsp, hdone, rows, rows_sp, ret, y_back, total;
   int64_t cap, chunk_cap;
 };
 FusedLayout fused_layout(int64_t T_max, int H, int I, int E, int topk, int n_ranks, bool local_only) {
@@ -416,6 +416,7 @@ FusedLayout fused_layout(int64_t T_max, int H, int I, int E, int topk, int n_ran
   L.idx = take(4 * (size_t)T_max * topk);
   L.slot = take(4 * (size_t)T_max * topk);
   L.w = take(4 * (size_t)T_max * topk);
+  L.sched = take(4);
   L.hq = take((size_t)L.cap * I);
   L.hsp = take((size_t)L.chunk_cap * (I / 128) * 512);
   L.hdone = take(4 * (size_t)L.chunk_cap);
@@ -476,7 +477,8 @@ static int moe_forward_fused(const void* x, const float* logits, int64_t T, int 
   a.T = (int)T; a.H = H; a.I = I; a.E = E; a.topk = topk; a.El = E; a.n = 1; a.me = 0;
   a.cap = L.cap; a.chunk_cap = L.chunk_cap;
   a.xq = ws + L.xq; a.xs = ws + L.xs; a.idx = (int*)(ws + L.idx); a.slot = (int*)(ws + L.slot);
-  a.w = (float*)(ws + L.w); a.counts = (int*)(ws + L.counts); a.h_done = (int*)(ws + L.hdone);
+  a.w = (float*)(ws + L.w); a.sched = (int*)(ws + L.sched); a.counts = (int*)(ws + L.counts);
+  a.h_done = (int*)(ws + L.hdone);
   a.w13 = (const uint8_t*)w13; a.w13_sp = (const uint8_t*)w13_sp; a.w2_sp = (const uint8_t*)w2_sp;
   a.hq = ws + L.hq; a.hs_p = ws + L.hsp;
   ly.pr.cnt_all[0] = (int*)(ws + L.cnt_all); ly.pr.rows[0] = ws + L.rows; ly.pr.rows_sp[0] = ws + L.rows_sp;
@@ -622,7 +624,8 @@ int bs_ep_moe_forward(const void* x, const float* logits, int64_t T, int64_t max
   a.T = (int)T; a.H = H; a.I = I; a.E = E; a.topk = topk; a.El = El; a.n = n_ranks; a.me = rank;
   a.cap = L.cap; a.chunk_cap = L.chunk_cap;
   a.xq = ws + L.xq; a.xs = ws + L.xs; a.idx = (int*)(ws + L.idx); a.slot = (int*)(ws + L.slot);
-  a.w = (float*)(ws + L.w); a.counts = (int*)(ws + L.counts); a.h_done = (int*)(ws + L.hdone);
+  a.w = (float*)(ws + L.w); a.sched = (int*)(ws + L.sched); a.counts = (int*)(ws + L.counts);
+  a.h_done = (int*)(ws + L.hdone);
   a.w13 = (const uint8_t*)w13; a.w13_sp = (const uint8_t*)w13_sp; a.w2_sp = (const uint8_t*)w2_sp;
   a.hq = ws + L.hq; a.hs_p = ws + L.hsp;
   for (int q = 0; q < n_ranks; ++q) {

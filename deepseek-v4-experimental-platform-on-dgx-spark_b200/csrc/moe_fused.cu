@@ -218,6 +218,7 @@ struct LayerArgs {
   int* idx;                   // [T, topk] expert of each (token, slot)
   int* slot;                  // [T, topk] its row among this rank's rows of that expert
   float* w;                   // [T, topk]
+  int* sched;                 // next dynamically handed-out work item (zeroed by the front phase)
   int* counts;                // [2][E] (parity of the epoch), zero before first use
   int* h_done;                // [chunk_cap] W1|W3 tile parts stored per token chunk (kEpiWarps per tile)
   const uint8_t* w13;         // [El][2I][H/2] this rank's W1|W3 (L2 prefetch of each CTA's first item)
@@ -250,6 +251,8 @@ struct C {
   static constexpr int kEpiWarps = 8;
   static constexpr int kExpWarps = 2 + kEpiWarps;           // producer, MMA issuer, epilogue
   static constexpr int kMaxE = 1024;
+  static constexpr int kItemRing = 4;                        // work items handed from the producer to the others
+  static constexpr int kDynRounds = 2;                       // the last 2-3 rounds of items come from a counter
   static constexpr int kSmemBytes = 1024 + kStages * (kStageBytes + kSfBytes) + 2 * (kMaxE + 1) * 4 + 2 * 80 * 4 + 256;
   static_assert(kStageBytes % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
   static_assert(kSmemBytes <= 232448 - 1024, "shared memory per CTA (dynamic + static)");
@@ -276,7 +279,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_full = empty + C::kStages;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* cbar = acc_empty + 2;                          // [3] combine-phase bulk loads
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(cbar + 3);
+  uint64_t* item_full = cbar + 3;                          // [kItemRing] work-item hand-off
+  uint64_t* item_empty = item_full + C::kItemRing;
+  int* s_items_raw = reinterpret_cast<int*>(item_empty + C::kItemRing);
+  volatile int* s_items = s_items_raw;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_items_raw + C::kItemRing);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -297,6 +304,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], C::kEpiWarps);
+    }
+    for (int r = 0; r < C::kItemRing; ++r) {
+      mbar_init(&item_full[r], 1);
+      mbar_init(&item_empty[r], 1 + C::kEpiWarps);           // the MMA warp and every epilogue warp
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -326,6 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- A: next call's histogram, this call's chunk counters
     for (int64_t i = gtid; i < a.E; i += nthreads) a.counts[(par ^ 1) * a.E + i] = 0;
     for (int64_t i = gtid; i < a.chunk_cap; i += nthreads) a.h_done[i] = 0;
+    if (gtid == 0) *a.sched = 0;
 
     // ---- A: even warps quantise, odd warps route (the two overlap)
     const int64_t rw = gwarp >> 1, nrw = nwarps >> 1;
@@ -538,6 +550,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nt13 = a.I / 128, nt2 = H / 256;
   const int n13 = s_chunk[El] * nt13;
   const int n_items = ok ? n13 + s_chunk[El] * nt2 : 0;
+  // Items [0, n_static) are taken statically (item = blockIdx.x + k * G),
+  // the last two to three rounds [n_static, n_items) from a counter, so CTAs
+  // whose SMs stream a little slower take fewer of them.  Either way a CTA's
+  // items rise in index, all W1|W3 items come before all W2 items, and every
+  // CTA is resident: a W2 item only waits on W1|W3 items already issued.
+  const int rounds = n_items / (int)gridDim.x;
+  const int k_static = rounds > C::kDynRounds ? rounds - C::kDynRounds : 0;
+  const int n_static = k_static * (int)gridDim.x;
 
   // item -> (W2?, expert, first row, rows, output tile, global chunk).  Inside
   // an expert, items run tile-major: consecutive items stream the same weight
@@ -574,7 +594,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!pok) *abort_flag = 1;
     int it = 0;
     const int w13_tiles = 2 * a.I / 128, w2_tiles = H / 128;
-    for (int item = blockIdx.x; item < n_items && pok; item += gridDim.x) {
+    for (int k = 0; pok; ++k) {
+      int item = (int)blockIdx.x + k * (int)gridDim.x;
+      if (k >= k_static) {
+        int v = 0;
+        if (lane == 0) v = n_static + atomicAdd(a.sched, 1);
+        item = __shfl_sync(0xffffffffu, v, 0);
+        if (item >= n_items) item = -1;
+      }
+      const int slot = k % C::kItemRing;
+      if (!__all_sync(0xffffffffu, mbar_wait(&item_empty[slot], ((k / C::kItemRing) & 1) ^ 1, abort_flag))) break;
+      if (lane == 0) {
+        s_items[slot] = item;
+        mbar_arrive(&item_full[slot]);
+      }
+      __syncwarp();
+      if (item < 0) break;
       bool w2;
       int e, row0, cnt, nt, cg;
       decode(item, w2, e, row0, cnt, nt, cg);
@@ -632,9 +667,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr uint64_t kSfStep = (uint64_t)(C::kSfBytes >> 4);
     constexpr uint64_t kYOff = (uint64_t)(C::kXBytes >> 4);
     const uint32_t sf_tmem0 = tmem_base + C::kSfCol0;
-    int it = 0, acc_it = 0;
+    int it = 0;
     bool mok = true;
-    for (int item = blockIdx.x; item < n_items && mok; item += gridDim.x, ++acc_it) {
+    for (int acc_it = 0; mok; ++acc_it) {
+      const int slot = acc_it % C::kItemRing;
+      if (!__all_sync(0xffffffffu, mbar_wait(&item_full[slot], (acc_it / C::kItemRing) & 1, abort_flag))) break;
+      const int item = s_items[slot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&item_empty[slot]);
+      if (item < 0) break;
       bool w2;
       int e, row0, cnt, nt, cg;
       decode(item, w2, e, row0, cnt, nt, cg);
@@ -683,8 +724,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quad = warp & 3;
     const int set = (warp - 2) >> 2;
     const int f = quad * 32 + lane;
-    int acc_it = 0;
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++acc_it) {
+    for (int acc_it = 0;; ++acc_it) {
+      const int slot = acc_it % C::kItemRing;
+      if (!__all_sync(0xffffffffu, mbar_wait(&item_full[slot], (acc_it / C::kItemRing) & 1, abort_flag))) break;
+      const int item = s_items[slot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&item_empty[slot]);
+      if (item < 0) break;
       bool w2;
       int e, row0, cnt, nt, cg;
       decode(item, w2, e, row0, cnt, nt, cg);

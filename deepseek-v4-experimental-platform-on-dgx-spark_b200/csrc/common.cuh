@@ -2,8 +2,10 @@
 // dtype tags, error reporting, mbarrier / TMA / tcgen05 inline-PTX wrappers.
 //
 // Every spin-wait in this library is bounded: a wait that exceeds
-// BS_SPIN_LIMIT polls records BS_ERR_DEVICE_TIMEOUT in bs_device_error and
-// returns false, and the calling kernel winds down instead of hanging.
+// BS_SPIN_LIMIT polls (and, for the suspending mbarrier waits, whose polls
+// can take microseconds each, kBsWaitLimitNs of %globaltimer) records
+// BS_ERR_DEVICE_TIMEOUT in bs_device_error and returns false, and the
+// calling kernel winds down instead of hanging.
 #pragma once
 
 #include <cuda.h>
@@ -200,23 +202,48 @@ BS_DEVINL bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+BS_DEVINL uint64_t bs_globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Time bound of the mbarrier waits: above the 2 s bound of the waits on other
+// CTAs and GPUs, so that one of those (which the mbarrier chain may sit
+// behind) expires first and reports where it gave up.
+constexpr uint64_t kBsWaitLimitNs = 5000000000ull;
+
+// Every 4096th failed poll: has the wait run past kBsWaitLimitNs?  *t0 holds
+// the time of the first check (0 before it).
+BS_DEVINL bool bs_wait_expired(uint32_t i, uint64_t* t0) {
+  if ((i & 4095u) != 4095u) return false;
+  const uint64_t t = bs_globaltimer_ns();
+  if (*t0 == 0) {
+    *t0 = t;
+    return false;
+  }
+  return t - *t0 > kBsWaitLimitNs;
+}
+
 // Bounded spin on an mbarrier whose phase completes through remote
 // transaction bytes (st.async from peer CTAs).  test_wait polls without
 // suspending the thread; a suspended try_wait was measured to wake
 // microseconds after such a phase completed.
 BS_DEVINL bool mbar_spin(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < BS_SPIN_LIMIT; ++i)
+  for (uint32_t i = 0; i < BS_SPIN_LIMIT; ++i)     // non-suspending polls: seconds at most
     if (mbar_test_wait(bar, parity)) return true;
   bs_set_error(BS_ERR_DEVICE_TIMEOUT);
   return false;
 }
 
 // Bounded wait.  Returns false (and records the error) after BS_SPIN_LIMIT
-// polls, or as soon as *abort is set by another role of the same CTA.
+// polls or kBsWaitLimitNs, or as soon as *abort is set by another role of
+// the same CTA.
 BS_DEVINL bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  uint64_t t0 = 0;
   for (uint32_t i = 0; i < BS_SPIN_LIMIT; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
+    if (bs_wait_expired(i, &t0)) break;
   }
   bs_set_error(BS_ERR_DEVICE_TIMEOUT);
   *abort = 1;

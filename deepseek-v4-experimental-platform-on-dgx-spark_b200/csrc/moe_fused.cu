@@ -474,9 +474,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       s_chunk[l] = Cc[e0 + l] - Cc[e0];
     }
     // The experts phase of this CTA starts with work item blockIdx.x (a
-    // W1|W3 item when there are enough): its weight tiles and their scales
-    // go to L2 now, while HBM is otherwise idle during the row dispatch.
-    if (threadIdx.x == 0) {
+    // W1|W3 item when there are enough).  With several ranks its weight
+    // tiles and their scales go to L2 now, while HBM is otherwise idle
+    // during the dispatch over NVLink and the wait for the other ranks' rows
+    // (on one GPU the prefetch only competes with the local dispatch).
+    if (kMulti && threadIdx.x == 0) {
       const int nt13 = a.I / 128;
       const int item = blockIdx.x;
       if (item < (Cc[e0 + El] - Cc[e0]) * nt13) {
@@ -718,7 +720,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (elect_one()) tc_commit(&acc_full[buf]);
       __syncwarp();
     }
-  } else if (warp >= 2 && warp < C::kExpWarps) {
+  } else if (warp >= 2 && warp < C::kExpWarps && n_items > 0) {
     // ------------------------------------------------------------ epilogue
     // Two sets of four warps take alternate 16-token groups of an item.
     const int quad = warp & 3;

@@ -72,14 +72,6 @@ SIGNATURES = {
     "bs_moe_experts": [_i32, _i64, _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                        _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p],
     "bs_moe_combine": [_c_void_p, _c_void_p, _c_void_p, _i64, _i32, _i32, _c_void_p, _c_void_p],
-    "bs_ep_counts_push": [_c_void_p, _i32, _i32, _i32, ctypes.POINTER(_c_void_p), _c_void_p],
-    "bs_ep_plan": [_c_void_p, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p],
-    "bs_ep_rows_push": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _i32, _i64,
-                        ctypes.POINTER(_c_void_p), ctypes.POINTER(_c_void_p), ctypes.POINTER(_c_void_p), _c_void_p],
-    "bs_ep_pack_scales": [_c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i64, _c_void_p, _c_void_p],
-    "bs_ep_experts_return": [_i32, _i64, _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
-                             _c_void_p, _c_void_p, _c_void_p, _c_void_p, ctypes.POINTER(_c_void_p), _i32, _c_void_p, _c_void_p,
-                             _c_void_p],
 }
 RESTYPES = {"bs_last_error": ctypes.c_char_p, "bs_moe_workspace_size": ctypes.c_size_t,
             "bs_moe_staged_workspace_size": ctypes.c_size_t, "bs_moe_chunk_capacity": ctypes.c_int64,

@@ -16,7 +16,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 SRC = os.path.join(HERE, "csrc", "lib.cu")
 OUT = os.path.join(HERE, "libbsgemm.so")
-DEPS = [os.path.join(HERE, "csrc", f) for f in ("lib.cu", "common.cuh", "quant.cu", "dequant.cu", "hc.cu", "attn.cu", "gemm.cu", "gemm_pair.cu", "capi.cu", "moe.cu", "peer.cu", "ep.cu", "moe_fused.cu", "gate.cu", "noalloc.cu")]
+DEPS = [os.path.join(HERE, "csrc", f) for f in ("lib.cu", "common.cuh", "quant.cu", "dequant.cu", "hc.cu", "attn.cu", "gemm.cu", "gemm_pair.cu", "capi.cu", "moe.cu", "peer.cu", "moe_fused.cu", "gate.cu", "noalloc.cu")]
 DEPS.append(os.path.join(os.path.dirname(HERE), "include", "bsgemm.h"))
 
 

@@ -30,16 +30,6 @@ int bs_launch_moe_experts(int E, int64_t rows, int H, int I, const uint8_t* ap, 
                           const void* w2, const uint8_t* w2_sp, const int* y_rowmap, uint8_t* hq, uint8_t* hs_p,
                           __nv_bfloat16* y, const int* ret, void* const* y_ranks, int n_ranks, cudaStream_t st,
                           cudaError_t* cerr);
-cudaError_t bs_launch_ep_counts_push(const int* counts, int E, int me, int n_ranks, void* const* cnt_ranks,
-                                     cudaStream_t st);
-cudaError_t bs_launch_ep_plan(const int* cnt_all, int n_ranks, int E, int me, int El, int* send_pos0, int* loc_off,
-                              int* loc_chunks, cudaStream_t st);
-cudaError_t bs_launch_ep_rows_push(const uint8_t* rows, const uint32_t* rows_sc, const int* offsets,
-                                   const int* send_pos0, int E, int El, int H, int me, int64_t max_rows,
-                                   void* const* recv_rows, void* const* recv_sc, void* const* recv_ret, int n_ranks,
-                                   cudaStream_t st);
-cudaError_t bs_launch_ep_pack_scales(const uint32_t* recv_sc, const int* loc_off, const int* loc_chunks, int El,
-                                     int H, int64_t max_rows, uint8_t* asp, cudaStream_t st);
 cudaError_t bs_launch_moe_regroup(const int* cnt, int S, int E, int64_t capacity, const uint8_t* rows_in,
                                   const uint32_t* sc_in, int H, uint8_t* rows_out, uint8_t* asp, int* rowmap,
                                   int* offsets, int* chunk_prefix, int* scratch, cudaStream_t st);
@@ -719,91 +709,6 @@ int bs_moe_experts(int E, int64_t capacity, int H, int I, const void* rows, cons
                                 (cudaStream_t)stream, &e);
   if (r == BS_ERR_UNSUPPORTED) return fail(r, "moe_experts: could not build TMA descriptors");
   if (r) return cuda_status(e, "moe_experts");
-  return BS_OK;
-}
-
-// ---------------------------------------------------------------------------
-// expert parallel over peer memory
-// ---------------------------------------------------------------------------
-
-static int check_ranks(const char* name, int n_ranks, int rank, void* const* v, int align) {
-  if (n_ranks < 1 || n_ranks > 8 || rank < 0 || rank >= n_ranks)
-    return fail(BS_ERR_INVALID_ARG, "%s: rank %d of %d (1..8 ranks)", name, rank, n_ranks);
-  if (!v) return fail(BS_ERR_INVALID_ARG, "%s: null pointer list", name);
-  for (int q = 0; q < n_ranks; ++q)
-    if (!v[q] || !aligned(v[q], align)) return fail(BS_ERR_INVALID_ARG, "%s: buffer of rank %d null or misaligned", name, q);
-  return BS_OK;
-}
-
-int bs_ep_counts_push(const int* counts, int E, int rank, int n_ranks, void* const* cnt_ranks, void* stream) {
-  if (E <= 0 || E > 1024 || E % n_ranks) return fail(BS_ERR_UNSUPPORTED, "ep_counts_push: %d experts over %d ranks", E, n_ranks);
-  int st = check_ranks("ep_counts_push", n_ranks, rank, cnt_ranks, 4);
-  if (st) return st;
-  if (!counts) return fail(BS_ERR_INVALID_ARG, "ep_counts_push: null counts");
-  return cuda_status(bs_launch_ep_counts_push(counts, E, rank, n_ranks, cnt_ranks, (cudaStream_t)stream),
-                     "ep_counts_push");
-}
-
-int bs_ep_plan(const int* cnt_all, int n_ranks, int E, int rank, int* send_pos0, int* loc_off, int* loc_chunks,
-               void* stream) {
-  if (n_ranks < 1 || n_ranks > 8 || rank < 0 || rank >= n_ranks || E <= 0 || E > 1024 || E % n_ranks ||
-      E / n_ranks + 1 > 1024)
-    return fail(BS_ERR_UNSUPPORTED, "ep_plan: %d experts, rank %d of %d", E, rank, n_ranks);
-  if (!cnt_all || !send_pos0 || !loc_off || !loc_chunks) return fail(BS_ERR_INVALID_ARG, "ep_plan: null pointer");
-  return cuda_status(bs_launch_ep_plan(cnt_all, n_ranks, E, rank, E / n_ranks, send_pos0, loc_off, loc_chunks,
-                                       (cudaStream_t)stream),
-                     "ep_plan");
-}
-
-int bs_ep_rows_push(const void* rows, const void* rows_sc, const int* offsets, const int* send_pos0, int E, int H,
-                    int rank, int n_ranks, int64_t max_rows, void* const* recv_rows, void* const* recv_sc,
-                    void* const* recv_ret, void* stream) {
-  if (E <= 0 || E > 1024 || E % n_ranks || H <= 0 || H % 128 || max_rows < 0 || max_rows >= (1 << 24))
-    return fail(BS_ERR_UNSUPPORTED, "ep_rows_push: E=%d H=%d rows=%lld", E, H, (long long)max_rows);
-  int st = check_ranks("ep_rows_push", n_ranks, rank, recv_rows, 16);
-  if (!st) st = check_ranks("ep_rows_push", n_ranks, rank, recv_sc, 4);
-  if (!st) st = check_ranks("ep_rows_push", n_ranks, rank, recv_ret, 4);
-  if (st) return st;
-  if (max_rows > 0 && (!rows || !rows_sc || !offsets || !send_pos0 || !aligned(rows, 16) || !aligned(rows_sc, 4)))
-    return fail(BS_ERR_INVALID_ARG, "ep_rows_push: null or misaligned operand");
-  return cuda_status(bs_launch_ep_rows_push((const uint8_t*)rows, (const uint32_t*)rows_sc, offsets, send_pos0, E,
-                                            E / n_ranks, H, rank, max_rows, recv_rows, recv_sc, recv_ret, n_ranks,
-                                            (cudaStream_t)stream),
-                     "ep_rows_push");
-}
-
-int bs_ep_pack_scales(const void* recv_sc, const int* loc_off, const int* loc_chunks, int E_local, int H,
-                      int64_t max_rows, void* rows_sp, void* stream) {
-  if (E_local <= 0 || E_local > 1024 || H <= 0 || H % 128 || max_rows < 0)
-    return fail(BS_ERR_UNSUPPORTED, "ep_pack_scales: E=%d H=%d", E_local, H);
-  if (max_rows > 0 && (!recv_sc || !loc_off || !loc_chunks || !rows_sp || !aligned(rows_sp, 16)))
-    return fail(BS_ERR_INVALID_ARG, "ep_pack_scales: null or misaligned pointer");
-  return cuda_status(bs_launch_ep_pack_scales((const uint32_t*)recv_sc, loc_off, loc_chunks, E_local, H, max_rows,
-                                              (uint8_t*)rows_sp, (cudaStream_t)stream),
-                     "ep_pack_scales");
-}
-
-int bs_ep_experts_return(int E_local, int64_t capacity, int H, int I, const void* rows, const void* rows_sp,
-                         const int* offsets, const int* chunk_prefix, const void* w13, const void* w13_sp,
-                         const void* w2, const void* w2_sp, const int* ret, void* const* y_ranks, int n_ranks,
-                         void* hq, void* hs_p, void* stream) {
-  int st = check_moe_dims(capacity, H, I, E_local, 1);
-  if (st) return st;
-  if (capacity == 0) return BS_OK;
-  st = check_ranks("ep_experts_return", n_ranks, 0, y_ranks, 16);
-  if (st) return st;
-  if (!rows || !rows_sp || !offsets || !chunk_prefix || !w13 || !w13_sp || !w2 || !w2_sp || !ret || !hq || !hs_p)
-    return fail(BS_ERR_INVALID_ARG, "ep_experts_return: null pointer");
-  if (!aligned(rows, 16) || !aligned(hq, 16) || !aligned(w13, 32) || !aligned(w2, 32) || !aligned(rows_sp, 16) ||
-      !aligned(hs_p, 16) || !aligned(w13_sp, 16) || !aligned(w2_sp, 16))
-    return fail(BS_ERR_INVALID_ARG, "ep_experts_return: alignment");
-  cudaError_t e;
-  int r = bs_launch_moe_experts(E_local, capacity, H, I, (const uint8_t*)rows, (const uint8_t*)rows_sp, offsets,
-                                chunk_prefix, w13, (const uint8_t*)w13_sp, w2, (const uint8_t*)w2_sp, nullptr,
-                                (uint8_t*)hq, (uint8_t*)hs_p, nullptr, ret, y_ranks, n_ranks, (cudaStream_t)stream,
-                                &e);
-  if (r == BS_ERR_UNSUPPORTED) return fail(r, "ep_experts_return: could not build TMA descriptors");
-  if (r) return cuda_status(e, "ep_experts_return");
   return BS_OK;
 }
 

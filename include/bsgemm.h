@@ -313,45 +313,6 @@ int bs_moe_forward_noalloc(const void* x, const float* logits, int64_t T, int H,
                            void* stream);
 
 /* ------------------------------------------------------------------------
- * Expert parallel over peer memory: the dispatch and the return exchange of
- * the EP MoE layer without NCCL or a host round trip (the reference shards
- * experts by contiguous ranges, weight_loader.py:112-139, and its model
- * exchanges activations with NCCL).  Buffers written by peers are mapped
- * into every rank (symmetric memory / CUDA IPC); each list holds one device
- * pointer per rank (index = rank), 1..8 ranks, E experts split evenly.
- * Order of one layer on rank r, with a bs_peer_barrier after the steps marked
- * (B):
- *   bs_moe_route / bs_moe_scan / bs_moe_dispatch (row-major scale words)
- *   bs_ep_counts_push   counts[E] -> cnt_ranks[q][r*E ..] on every rank  (B)
- *   bs_ep_plan          from cnt_all [n_ranks][E] (this rank's copy): where
- *                       this rank's rows of expert e land at the owner
- *                       (send_pos0[E]), this rank's expert offsets
- *                       loc_off[E/n+1] and token-chunk prefix loc_chunks
- *   bs_ep_rows_push     rows (H bytes), their H/128 scale words and return
- *                       addresses (r<<24 | row) into the owners' buffers at
- *                       their final expert-major place                     (B)
- *   bs_ep_pack_scales   received scale words -> packed chunk layout
- *   bs_ep_experts_return  grouped GEMMs on the received rows; W2 stores each
- *                       output row into y_ranks[ret>>24] row (ret&0xFFFFFF) (B)
- *   bs_moe_combine      on the source rank, from its return buffer.
- * Rows of one expert are ordered by source rank, then by the source's
- * expert-sorted order, as after an all-to-all and bs_moe_regroup.
- * No counterparts in the reference.
- * ------------------------------------------------------------------------ */
-int bs_ep_counts_push(const int* counts, int E, int rank, int n_ranks, void* const* cnt_ranks, void* stream);
-int bs_ep_plan(const int* cnt_all, int n_ranks, int E, int rank, int* send_pos0, int* loc_off, int* loc_chunks,
-               void* stream);
-int bs_ep_rows_push(const void* rows, const void* rows_sc, const int* offsets, const int* send_pos0, int E, int H,
-                    int rank, int n_ranks, int64_t max_rows, void* const* recv_rows, void* const* recv_sc,
-                    void* const* recv_ret, void* stream);
-int bs_ep_pack_scales(const void* recv_sc, const int* loc_off, const int* loc_chunks, int E_local, int H,
-                      int64_t max_rows, void* rows_sp, void* stream);
-int bs_ep_experts_return(int E_local, int64_t capacity, int H, int I, const void* rows, const void* rows_sp,
-                         const int* offsets, const int* chunk_prefix, const void* w13, const void* w13_sp,
-                         const void* w2, const void* w2_sp, const int* ret, void* const* y_ranks, int n_ranks,
-                         void* hq, void* hs_p, void* stream);
-
-/* ------------------------------------------------------------------------
  * Expert-parallel layer in one kernel over peer memory (the default
  * expert-parallel path; no NCCL, no host round trip).  Experts split into
  * contiguous ranges of E/n_ranks (the reference's loader ranges,

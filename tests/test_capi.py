@@ -119,14 +119,20 @@ def test_multi_gpu_entry_points_validate_arguments(lib):
     assert lib.bs_peer_barrier(two, 2, 0, 0, None) == L.BS_ERR_INVALID_ARG
     assert lib.bs_peer_barrier(two, 2, 0, 1, None) == L.BS_ERR_INVALID_ARG   # null flag arrays
     assert lib.bs_peer_barrier_counted(two, 2, 0, None, None) == L.BS_ERR_INVALID_ARG
-    # expert parallel: experts split evenly, H a multiple of 128
-    assert lib.bs_ep_counts_push(None, 255, 0, 2, two, None) == L.BS_ERR_UNSUPPORTED
-    assert lib.bs_ep_plan(None, 2, 256, 2, None, None, None, None) == L.BS_ERR_UNSUPPORTED
-    assert lib.bs_ep_plan(None, 2, 256, 0, None, None, None, None) == L.BS_ERR_INVALID_ARG
-    assert lib.bs_ep_rows_push(None, None, None, None, 256, 100, 0, 2, 16, two, two, two, None) == \
-        L.BS_ERR_UNSUPPORTED
-    assert lib.bs_ep_rows_push(None, None, None, None, 256, 128, 0, 2, 16, two, two, two, None) == \
-        L.BS_ERR_INVALID_ARG
-    assert lib.bs_ep_pack_scales(None, None, None, 0, 128, 16, None, None) == L.BS_ERR_UNSUPPORTED
-    assert lib.bs_ep_experts_return(16, 0, 4096, 2048, None, None, None, None, None, None, None, None, None, two, 2,
-                                    None, None, None) == L.BS_OK
+    # expert-parallel layer: experts split evenly over 1..8 ranks, H a multiple of 256
+    sizes = (ctypes.c_int64 * 7)()
+    assert lib.bs_ep_moe_sizes(16, 4096, 2048, 255, 8, 2, sizes) == L.BS_ERR_UNSUPPORTED
+    assert b"do not split" in lib.bs_last_error()
+    assert lib.bs_ep_moe_sizes(16, 384, 256, 16, 4, 2, sizes) == L.BS_ERR_UNSUPPORTED
+    assert lib.bs_ep_moe_sizes(16, 4096, 2048, 256, 8, 9, sizes) == L.BS_ERR_INVALID_ARG
+    assert lib.bs_ep_moe_sizes(16, 4096, 2048, 256, 8, 2, None) == L.BS_ERR_INVALID_ARG
+    assert lib.bs_ep_moe_sizes(16, 4096, 2048, 256, 8, 2, sizes) == L.BS_OK
+    assert sizes[1] == 8 * 2 * 256                    # count matrix: [ranks][E] 64-bit words
+    assert sizes[2] == 2 * 16 * 8 * 4096              # receive rows: ranks x max_tokens x topk rows of H bytes
+    assert sizes[5] == 16 * 8 * 4096 * 2              # returned bf16 rows of this rank's tokens
+    assert sizes[0] > 0 and sizes[6] > 0
+    peers = (ctypes.c_void_p * 12)()
+    assert lib.bs_ep_moe_forward(None, None, 17, 16, 4096, 2048, 256, 8, 0, 2, None, None, None, None, None, peers,
+                                 None, 0, None) == L.BS_ERR_INVALID_ARG      # more tokens than max_tokens
+    assert lib.bs_ep_moe_forward(None, None, 0, 16, 4096, 2048, 256, 8, 2, 2, None, None, None, None, None, peers,
+                                 None, 0, None) == L.BS_ERR_INVALID_ARG      # rank out of range

@@ -287,14 +287,15 @@ def bench_fp8_prefill(args, torch, dist, ws, rank, dev):
         x_dev.copy_(x_host, non_blocking=True)
         a, a_s = pkg.act_quant(x_dev, 128)
         if fused:
-            o_host.copy_(tpg(a, a_s, b_loc, s_loc), non_blocking=True)
-            return
-        c = pkg.fp8_gemm(a, a_s, b_loc, s_loc)
-        if ws > 1:
-            dist.all_gather_into_tensor(gathered, c)
-            full.view(M, ws, n_local).copy_(gathered.permute(1, 0, 2))
-            c = full
-        o_host.copy_(c, non_blocking=True)
+            c = tpg(a, a_s, b_loc, s_loc)
+        else:
+            c = pkg.fp8_gemm(a, a_s, b_loc, s_loc)
+            if ws > 1:
+                dist.all_gather_into_tensor(gathered, c)
+                full.view(M, ws, n_local).copy_(gathered.permute(1, 0, 2))
+                c = full
+        if rank == 0:      # every rank holds the gathered C: the job reads it out once
+            o_host.copy_(c, non_blocking=True)
 
     if ws == 1:
         # one GPU: consecutive steps overlap on three streams (inputs in,
@@ -354,7 +355,8 @@ def bench_fp8_prefill(args, torch, dist, ws, rank, dev):
                 "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * (N if ws > 1 else n_local) * 2,
                 "ms_per_step": round(e2e_ms, 4),
                 "path": "act_quant + fp8_gemm public API, pinned host I/O" + (
-                    "; consecutive steps overlapped on copy-in / compute / copy-out streams" if ws == 1 else "")},
+                    "; consecutive steps overlapped on copy-in / compute / copy-out streams" if ws == 1 else
+                    "; every rank copies its input in, rank 0 copies the gathered C out")},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 3), "traffic": traffic,
                      "kernel": "bsg_kernel<normal,fp8,BN=256>" + (" + peer stores" if fused else ""),

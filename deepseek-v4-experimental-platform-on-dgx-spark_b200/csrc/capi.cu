@@ -28,8 +28,7 @@ cudaError_t bs_launch_moe_combine(const __nv_bfloat16* y, const int* pos_of, con
 int bs_launch_moe_experts(int E, int64_t rows, int H, int I, const uint8_t* ap, const uint8_t* asp,
                           const int* offsets, const int* chunk_prefix, const void* w13, const uint8_t* w13_sp,
                           const void* w2, const uint8_t* w2_sp, const int* y_rowmap, uint8_t* hq, uint8_t* hs_p,
-                          __nv_bfloat16* y, const int* ret, void* const* y_ranks, int n_ranks, cudaStream_t st,
-                          cudaError_t* cerr);
+                          __nv_bfloat16* y, cudaStream_t st, cudaError_t* cerr);
 cudaError_t bs_launch_moe_regroup(const int* cnt, int S, int E, int64_t capacity, const uint8_t* rows_in,
                                   const uint32_t* sc_in, int H, uint8_t* rows_out, uint8_t* asp, int* rowmap,
                                   int* offsets, int* chunk_prefix, int* scratch, cudaStream_t st);
@@ -545,7 +544,7 @@ int moe_forward_staged(const void* x, const float* logits, int64_t T, int H, int
   if (e != cudaSuccess) return cuda_status(e, "moe front end");
   int r = bs_launch_moe_experts(E, T * topk, H, I, ws + L.ap, ws + L.asp, offsets, chunks, w13,
                                 (const uint8_t*)w13_sp, w2, (const uint8_t*)w2_sp, nullptr, ws + L.hq, ws + L.hsp,
-                                (__nv_bfloat16*)(ws + L.y), nullptr, nullptr, 0, s, &e);
+                                (__nv_bfloat16*)(ws + L.y), s, &e);
   if (r == BS_ERR_UNSUPPORTED) return fail(r, "moe: could not build TMA descriptors");
   if (r) return cuda_status(e, "moe grouped GEMM");
   e = bs_launch_moe_combine((const __nv_bfloat16*)(ws + L.y), pos, w, (int)T, topk, H, (__nv_bfloat16*)out, s);
@@ -705,8 +704,7 @@ int bs_moe_experts(int E, int64_t capacity, int H, int I, const void* rows, cons
   cudaError_t e;
   int r = bs_launch_moe_experts(E, capacity, H, I, (const uint8_t*)rows, (const uint8_t*)rows_sp, offsets,
                                 chunk_prefix, w13, (const uint8_t*)w13_sp, w2, (const uint8_t*)w2_sp, y_rowmap,
-                                (uint8_t*)hq, (uint8_t*)hs_p, (__nv_bfloat16*)y, nullptr, nullptr, 0,
-                                (cudaStream_t)stream, &e);
+                                (uint8_t*)hq, (uint8_t*)hs_p, (__nv_bfloat16*)y, (cudaStream_t)stream, &e);
   if (r == BS_ERR_UNSUPPORTED) return fail(r, "moe_experts: could not build TMA descriptors");
   if (r) return cuda_status(e, "moe_experts");
   return BS_OK;

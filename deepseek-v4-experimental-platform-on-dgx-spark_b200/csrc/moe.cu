@@ -341,10 +341,6 @@ struct GemmArgs {
   __nv_bfloat16* y;          // W2: [rows, H] bf16
   int H;
   const int* y_rowmap;       // W2: optional output row map (EP: expert-major -> arrival order)
-  // W2, expert parallel over peer memory: output row r goes to row
-  // (ret[r] & 0xFFFFFF) of source rank (ret[r] >> 24)'s return buffer
-  const int* ret;
-  __nv_bfloat16* y_ranks[8];
 };
 
 // Grouped GEMM modes: W2 with one 128-row weight tile per item; W1/W3 with
@@ -599,13 +595,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
           for (int j = 0; j < 16; ++j) {
             const int tok = c0 + j;
             if (tok < cnt) {
-              __nv_bfloat16* yrow;
-              if (p.ret) {
-                const int rr = p.ret[row0 + tok];
-                yrow = p.y_ranks[rr >> 24] + (int64_t)(rr & 0xFFFFFF) * p.H;
-              } else {
-                yrow = p.y + (int64_t)(p.y_rowmap ? p.y_rowmap[row0 + tok] : row0 + tok) * p.H;
-              }
+              __nv_bfloat16* yrow = p.y + (int64_t)(p.y_rowmap ? p.y_rowmap[row0 + tok] : row0 + tok) * p.H;
               yrow[nt * p.nt_stride + f] = __float2bfloat16_rn(__uint_as_float(g[j]));
               if constexpr (MODE == kModeW2Pair)
                 yrow[nt * p.nt_stride + p.up_off + f] = __float2bfloat16_rn(__uint_as_float(g2[j]));
@@ -756,8 +746,7 @@ cudaError_t bs_launch_moe_combine(const __nv_bfloat16* y, const int* pos_of, con
 int bs_launch_moe_experts(int E, int64_t rows, int H, int I, const uint8_t* ap, const uint8_t* asp,
                           const int* offsets, const int* chunk_prefix, const void* w13, const uint8_t* w13_sp,
                           const void* w2, const uint8_t* w2_sp, const int* y_rowmap, uint8_t* hq, uint8_t* hs_p,
-                          __nv_bfloat16* y, const int* ret, void* const* y_ranks, int n_ranks, cudaStream_t st,
-                          cudaError_t* cerr) {
+                          __nv_bfloat16* y, cudaStream_t st, cudaError_t* cerr) {
   *cerr = cudaSuccess;
   if (rows == 0) return 0;
   CUtensorMap mw1, ma1, mw2, ma2;
@@ -779,8 +768,6 @@ int bs_launch_moe_experts(int E, int64_t rows, int H, int I, const uint8_t* ap, 
   a2.nt_stride = w2_pair ? 256 : 128;
   a2.offsets = offsets; a2.chunk_prefix = chunk_prefix; a2.w_sp = w2_sp; a2.a_sp = hs_p;
   a2.hq = nullptr; a2.hs_p = nullptr; a2.I = I; a2.y = y; a2.H = H; a2.y_rowmap = y_rowmap;
-  a2.ret = ret;
-  for (int q = 0; q < n_ranks && q < 8; ++q) a2.y_ranks[q] = reinterpret_cast<__nv_bfloat16*>(y_ranks[q]);
   *cerr = w2_pair ? moe::launch_grouped<moe::kModeW2Pair>(mw2, ma2, a2, st)
                   : moe::launch_grouped<moe::kModeW2>(mw2, ma2, a2, st);
   return *cerr == cudaSuccess ? 0 : BS_ERR_CUDA;

@@ -21,8 +21,10 @@
 //   experts  (persistent) waits until every rank's CTAs have dispatched,
 //            then runs W1|W3 work items (gate + up tiles, fused SwiGLU + e4m3
 //            quantisation of the hidden rows) and W2 work items (two 128-row
-//            output tiles) from one static list; a W2 item waits until all
-//            W1|W3 items of its token chunk are done (per-chunk counters),
+//            output tiles) from one list (W1|W3 items first), taken
+//            statically except for the last two to three rounds, which a
+//            counter hands out; a W2 item waits until all W1|W3 items of
+//            its token chunk are done (per-chunk counters),
 //            and its epilogue stores each output row into the source rank's
 //            return buffer; each CTA then adds 1 to every rank's
 //            returns-arrived counter

@@ -653,7 +653,7 @@ def bench_moe(args, torch, dist, ws, rank, dev):
         if dist is not None:
             dist.barrier()
         for e0, e1 in evs:
-            lib.bs_moe_time_experts(e0.cuda_event, e1.cuda_event)
+            lib.bs_moe_time_layer(e0.cuda_event, e1.cuda_event)
             call(xl, ll, outs[0])
         torch.cuda.synchronize()
         kern_ms = max_over_ranks(torch, dist, statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs))

@@ -55,7 +55,7 @@ SIGNATURES = {
     "bs_moe_staged_workspace_size": [_i64, _i32, _i32, _i32, _i32],
     "bs_moe_forward_staged": [_c_void_p, _c_void_p, _i64, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p,
                               _c_void_p, _c_void_p, _c_void_p, ctypes.c_size_t, _c_void_p],
-    "bs_moe_time_experts": [_c_void_p, _c_void_p],
+    "bs_moe_time_layer": [_c_void_p, _c_void_p],
     "bs_ep_moe_sizes": [_i64, _i32, _i32, _i32, _i32, _i32, ctypes.POINTER(_i64)],
     "bs_ep_moe_forward": [_c_void_p, _c_void_p, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p,
                           _c_void_p, _c_void_p, _c_void_p, ctypes.POINTER(_c_void_p), _c_void_p, ctypes.c_size_t,
@@ -75,7 +75,7 @@ SIGNATURES = {
 }
 RESTYPES = {"bs_last_error": ctypes.c_char_p, "bs_moe_workspace_size": ctypes.c_size_t,
             "bs_moe_staged_workspace_size": ctypes.c_size_t, "bs_moe_chunk_capacity": ctypes.c_int64,
-            "bs_moe_time_experts": None, "bs_sparse_attn_workspace_size": ctypes.c_size_t,
+            "bs_moe_time_layer": None, "bs_sparse_attn_workspace_size": ctypes.c_size_t,
             "bs_indexer_topk_workspace_size": ctypes.c_size_t}
 
 

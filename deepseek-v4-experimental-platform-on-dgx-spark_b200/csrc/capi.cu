@@ -435,7 +435,7 @@ size_t bs_moe_staged_workspace_size(int64_t T, int H, int I, int E, int topk) {
   return moe_layout(T, H, I, E, topk).total;
 }
 
-void bs_moe_time_experts(void* ev_begin, void* ev_end) {
+void bs_moe_time_layer(void* ev_begin, void* ev_end) {
   mf::t_ev_begin = (cudaEvent_t)ev_begin;
   mf::t_ev_end = (cudaEvent_t)ev_end;
 }

@@ -251,7 +251,7 @@ int bs_moe_forward_staged(const void* x, const float* logits, int64_t T, int H, 
 /* Profiling hook: the next single-kernel layer call (bs_moe_forward or
  * bs_ep_moe_forward) made on this host thread records ev_begin / ev_end
  * (cudaEvent_t) on its stream around its layer kernel, then forgets them. */
-void bs_moe_time_experts(void* ev_begin, void* ev_end);
+void bs_moe_time_layer(void* ev_begin, void* ev_end);
 
 /* Gate projection in front of the routing: logits [T,E] fp32 = x [T,H] bf16
  * times gate_w [E,H] bf16 transposed, on the tensor cores (tcgen05 kind::f16,
